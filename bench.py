@@ -1,0 +1,379 @@
+"""Benchmark: GQA decode tokens/s over the int4-compressed KV cache (B200).
+
+Workload (Llama-3-8B decode layer): batch 64, 32 query /
+8 KV heads, head_dim 128, context 8192 (8191 cached tokens + the new one),
+bf16 activations, PolarQuant int4 KV cache, RoPE theta 500000.  One step is
+one GroupQueryAttention operator call through the C ABI
+(sa_group_query_attention): RoPE + quantize-on-append of the new token's K/V,
+then attention of the 32 query heads over all 8192 cached tokens.  Inputs are
+synthetic (seeded normal); the cache (604 MB) is larger than L2 (126 MB), so
+no flush is needed between steps.
+
+  value   tokens/s of the device-resident step (B / step time), max over ranks
+  e2e     same metric through the same C-ABI call with q/k/v copied from
+          pinned host memory and attn_out copied back inside the timed region
+  roofline  the attention kernel(s) alone: algorithmic bytes / launch time
+  cpu_baseline  the CPU oracle (C restatement of the reference's Rust CPU
+          path: encode + read_k/read_v + SDPA) on a bounded sample, rank 0
+
+``--impl reference`` times that CPU restatement (all host threads) as the
+reference arm.  ``--gpus N`` under torchrun: each rank decodes its own batch of
+64 sequences (batch sharding, no collective; weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, D, T, BITS, THETA = 64, 32, 8, 128, 8192, 4, 500000.0
+CB = D * BITS // 8
+METRIC = "GQA decode tokens/s over int4-compressed KV (Llama-3-8B layer, B=64, T=8192)"
+UNIT = "tokens/s"
+
+
+def algorithmic_bytes(b=B, hkv=HKV, t=T, hq=HQ, d=D, cb=CB, act=2):
+    """Per step: K+V codes and {scale, zp} of every cached token, q in, out, appended vectors."""
+    cache = 2 * b * hkv * t * (cb + 8)
+    return cache + b * hq * d * act * 2 + 2 * b * hkv * (cb + 8)
+
+
+def attend_bytes(b=B, hkv=HKV, t=T, hq=HQ, d=D, cb=CB, act=2):
+    return 2 * b * hkv * t * (cb + 8) + b * hq * d * act * 2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        self.gpu_id = gpu_id
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_uuid(torch, dev):
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index)
+
+
+def build_workload(torch, sa, dev, seed):
+    """Cache filled with T-1 tokens (seeded), plus the step's q/k/v."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    std = 1.28  # N(0,1) activations through N(0, 0.02) projections of width 4096
+    cache = sa.GpuKvCache(1, HKV, D, T, batch=B, num_heads=HQ, bits=BITS, device=dev)
+    cos_np, sin_np = rope_np(T, D, THETA)
+    cos = torch.from_numpy(cos_np).to(dev)
+    sin = torch.from_numpy(sin_np).to(dev)
+    chunk = 512
+    pos = 0
+    while pos < T - 1:
+        n = min(chunk, T - 1 - pos)
+        k = (torch.randn(B, n, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+        v = (torch.randn(B, n, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+        cache.append(0, k, v, cos_cache=cos, sin_cache=sin, do_rotary=True)
+        cache.advance_position(n)
+        pos += n
+    q = (torch.randn(B, 1, HQ * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    k = (torch.randn(B, 1, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    v = (torch.randn(B, 1, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    return cache, cos, sin, q, k, v
+
+
+def rope_np(rows, d, theta):
+    half = d // 2
+    inv = 1.0 / (theta ** (np.arange(half, dtype=np.float64) * 2.0 / d))
+    ang = np.arange(rows, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def cpu_oracle_step_time(cache_view_np, q_np, k_new, v_new, signs, units, nthreads):
+    """One CPU step of the reference path on `units` (b, kv_head) pairs:
+    encode the new token (write_kv) + read_k/read_v of all T tokens + SDPA."""
+    import oracle
+
+    kc, km, vc, vm = cache_view_np
+    scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(D)))
+    t0 = time.perf_counter()
+    # append: PolarQuantizer::encode of the new K and V of every sampled unit
+    for u in range(units):
+        b, h = divmod(u, HKV)
+        oracle.polar_encode(k_new[b, h], BITS, signs[h])
+        oracle.polar_encode(v_new[b, h], BITS, signs[h])
+    nb = (units + HKV - 1) // HKV
+    oracle.compressed_gqa(q_np[:nb], kc[:nb], km[:nb], vc[:nb], vm[:nb], signs, BITS, scale, nthreads=nthreads,
+                          unit_begin=0, unit_end=units)
+    return time.perf_counter() - t0
+
+
+def cpu_sample(torch, cache, q, k, v, dev, target_s=10.0, nthreads=1):
+    """Bounded CPU sample of the same workload; returns (tokens/s, sample description)."""
+    view = cache.view(0)
+    nb = 2  # batch rows copied to host (16 units)
+    kc = view.k_codes[:nb, :, :T].cpu().numpy()
+    km = view.k_meta[:nb, :, :T].cpu().numpy()
+    vc = view.v_codes_tokens()[:nb, :, :T].cpu().numpy()
+    vm = view.v_meta[:nb, :, :T].cpu().numpy()
+    signs = view.signs.cpu().numpy().astype(np.int8)
+    qn = q.float().cpu().numpy().reshape(B, 1, HQ, D).transpose(0, 2, 1, 3)[:nb].copy()
+    kn = k.float().cpu().numpy().reshape(B, HKV, D)
+    vn = v.float().cpu().numpy().reshape(B, HKV, D)
+    data = (kc, km, vc, vm)
+    per_unit = cpu_oracle_step_time(data, qn, kn, vn, signs, 1, 1)
+    units = int(max(1, min(nb * HKV, target_s * nthreads / max(per_unit, 1e-6))))
+    if nthreads > 1:
+        units = max(units, min(nb * HKV, nthreads))
+    dt = cpu_oracle_step_time(data, qn, kn, vn, signs, units, nthreads)
+    total_units = B * HKV
+    step_time = dt * total_units / units
+    desc = (f"{units} of {total_units} (batch row, kv head) units of the full step (T={T}), {nthreads} thread(s), "
+            f"scaled by {total_units}/{units}; C restatement of the reference Rust CPU path (-O2, no FMA)")
+    return B / step_time, desc
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement, all host threads, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+
+    oracle.build()
+    nthreads = os.cpu_count() or 1
+    rng = np.random.default_rng(1234)
+    nb = max(1, (nthreads + HKV - 1) // HKV)
+    units = nb * HKV
+    signs = oracle.cache_signs(oracle.DEFAULT_SEED, 1, HKV, D)[0]
+    # seeded cache contents: codes uniform, meta like int4 PolarQuant of std-1.28 vectors
+    kc = rng.integers(0, 256, size=(nb, HKV, T, CB), dtype=np.uint8)
+    vc = rng.integers(0, 256, size=(nb, HKV, T, CB), dtype=np.uint8)
+    km = np.stack([rng.uniform(0.3, 0.5, (nb, HKV, T)), rng.uniform(-4, -2.5, (nb, HKV, T))], -1).astype(np.float32)
+    vm = km.copy()
+    q = (rng.standard_normal((nb, HQ, 1, D)) * 1.28).astype(np.float32)
+    kn = (rng.standard_normal((nb, HKV, D)) * 1.28).astype(np.float32)
+    vn = (rng.standard_normal((nb, HKV, D)) * 1.28).astype(np.float32)
+    data = (kc, km, vc, vm)
+    for _ in range(max(0, args.warmup)):
+        cpu_oracle_step_time(data, q, kn, vn, signs, min(units, nthreads), nthreads)
+    times = [cpu_oracle_step_time(data, q, kn, vn, signs, units, nthreads) for _ in range(args.steps)]
+    step = float(np.mean(times)) * (B * HKV) / units
+    value = B / step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama3-8b-layer-decode", "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                   "context": T, "kv_bits": BITS},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": f"{units} of {B * HKV} (batch row, kv head) units per step, scaled; the C "
+                                   "restatement of the reference Rust CPU path (reference not compilable: no rustc)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        cache.set_position(T - 1)
+        sa.group_query_attention(q, k, v, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
+                                 sin_cache=sin, do_rotary=True, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    sampler.start()
+    launches0 = lib.sa_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    launches = lib.sa_kernel_launches() - launches0
+    t_ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+
+    # Attention kernel(s) alone, for the roofline (no append).
+    for _ in range(3):
+        cache.set_position(T - 1)
+        sa.gqa_attend(q, cache, 0, num_heads=HQ, cos_cache=cos, sin_cache=sin, do_rotary=True, out=out)
+    torch.cuda.synchronize(dev)
+    la0 = lib.sa_kernel_launches()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        sa.gqa_attend(q, cache, 0, num_heads=HQ, cos_cache=cos, sin_cache=sin, do_rotary=True, out=out)
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    attend_launches = (lib.sa_kernel_launches() - la0) // args.steps
+    attend_ms = a0.elapsed_time(a1) / args.steps
+
+    # End to end: pinned host q/k/v in, attn_out back to pinned host, every step.
+    hq_ = q.cpu().pin_memory()
+    hk_ = k.cpu().pin_memory()
+    hv_ = v.cpu().pin_memory()
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        cache.set_position(T - 1)
+        sa.group_query_attention(dq, dk, dv, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
+                                 sin_cache=sin, do_rotary=True, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    x1.record(stream)
+    barrier()
+    e2e_ms = x0.elapsed_time(x1) / args.steps
+
+    # max over ranks
+    times = torch.tensor([t_ms, e2e_ms, attend_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, attend_ms = times.tolist()
+
+    peak, peak_kind = load_peaks()
+    abytes = attend_bytes()
+    achieved = abytes / (attend_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": B * world / (t_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
+        "config": {"workload": "llama3-8b-layer-decode (BASELINE config 3)", "batch_per_gpu": B,
+                   "global_batch": B * world, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
+                   "kv_bits": BITS, "rope_theta": THETA, "parallelism": f"batch-sharded x{world} (no collective)",
+                   "l2": "cache 604 MB > 126 MB L2 per step; no flush"},
+        "gpu_launches": int(launches),
+        "e2e": {"value": B * world / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
+                "d2h_bytes_per_step": int(out.numel() * 2)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "gqa attend (split + merge)", "launches_per_call": attend_launches,
+                     "algorithmic_bytes": abytes, "ms_per_call": attend_ms,
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        "step_bytes": algorithmic_bytes(),
+        "step_gbs": algorithmic_bytes() / (t_ms * 1e-3) / 1e9,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle  # checker / CPU baseline only
+
+        oracle.build()
+        val, desc = cpu_sample(torch, cache, q, k, v, dev, target_s=8.0, nthreads=1)
+        line["cpu_baseline"] = {"value": val, "unit": UNIT, "cores": 1, "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    cache.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

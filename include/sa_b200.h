@@ -1,0 +1,213 @@
+/*
+ * sa_b200.h -- C ABI of the B200-native (sm_100a) LLM decode hot path of the
+ * SmallAIOS onnx-rt runtime.
+ *
+ * The path: com.microsoft.GroupQueryAttention over a PolarQuant-compressed
+ * KV cache (quantize-on-append with fused RoPE on K, attention dequantizing
+ * inside the kernel) and the block-quantized int4 MatMulNBits GEMV/GEMM.
+ *
+ * Conventions (replacing the reference's Rust FFI, onnx-rt/src/cuda/ffi.rs):
+ *   - every entry point returns an int status (sa_status); 0 is success.
+ *     On failure sa_last_error_string() describes it (thread-local).
+ *   - all tensor arguments are caller-owned DEVICE pointers, row-major,
+ *     in the layouts onnx-rt uses ((B, S, heads*D) for Q/K/V/out).
+ *   - every compute call takes an explicit CUDA stream (cudaStream_t passed
+ *     as a plain pointer; NULL is the legacy default stream) and is fully
+ *     asynchronous: no host synchronisation, no allocation.
+ *   - dtype codes are ONNX TensorProto data types (onnx-rt/src/tensor.rs).
+ *   - calls on distinct cache handles are thread-safe; calls on one handle
+ *     must be serialised by the caller (the reference holds it behind a
+ *     Mutex, onnx-rt/src/session.rs:377).
+ */
+#ifndef SA_B200_H
+#define SA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SA_B200_VERSION 1
+
+typedef void *sa_stream_t; /* cudaStream_t */
+
+/* Status codes.  The reference maps CUDA failures to CudaError
+ * (onnx-rt/src/cuda/mod.rs:51-100) and operator failures to OpError
+ * (onnx-rt/src/operators.rs); the codes keep that split. */
+typedef enum sa_status {
+    SA_OK = 0,
+    SA_ERR_INVALID_ATTRIBUTE = 1, /* OpError::InvalidAttribute */
+    SA_ERR_SHAPE_MISMATCH = 2,    /* OpError::ShapeMismatch */
+    SA_ERR_UNSUPPORTED = 3,       /* OpError::UnsupportedOp / unsupported dtype or layout */
+    SA_ERR_CAPACITY = 4,          /* kv_cache_append:position_overflow (kv_cache.rs:246-251) */
+    SA_ERR_OUT_OF_MEMORY = 5,     /* CudaError::AllocFailed */
+    SA_ERR_CUDA = 6,              /* CudaError::RuntimeError / KernelLaunchFailed */
+    SA_ERR_DEVICE_CHECK = 7,      /* a device-side bounds check recorded a violation */
+    SA_ERR_TIMEOUT = 8,           /* a bounded device-side wait gave up */
+    SA_ERR_INVALID_ARGUMENT = 9   /* NULL handle/pointer, negative size */
+} sa_status;
+
+/* ONNX TensorProto.DataType codes (onnx-rt/src/tensor.rs DataType). */
+typedef enum sa_dtype {
+    SA_DTYPE_FLOAT = 1,
+    SA_DTYPE_FLOAT16 = 10,
+    SA_DTYPE_BFLOAT16 = 16
+} sa_dtype;
+
+/* Thread-local description of the last failure on this thread. */
+const char *sa_last_error_string(void);
+/* Static name of a status code. */
+const char *sa_status_string(int status);
+/* SA_B200_VERSION of the loaded library. */
+int sa_version(void);
+/* Diagnostic: number of kernels this library has launched in this process
+ * (all devices, all threads).  Lets a harness count its launches. */
+uint64_t sa_kernel_launches(void);
+
+/* ======================================================================
+ * Compressed KV cache.
+ *
+ * Replaces GpuKvCache (onnx-rt/src/cuda/kv_cache.rs:111-388: allocate,
+ * append, advance_position, view_pending, reset) and carries the
+ * compression state of CompressedKVCache (onnx-rt/src/kv_compression.rs:
+ * 742-925): one PolarQuantizer per (layer, kv_head) seeded with
+ * seed * 0x9E3779B97F4A7C15 + (layer * num_kv_heads + head) (:776-779),
+ * shared by K and V and by every sequence of the batch.
+ *
+ * Layout in HBM, per layer (b = batch row, h = local KV head, t = token,
+ * CB = head_dim * bits / 8 code bytes per vector, T = capacity rounded up to
+ * a multiple of 64):
+ *   k_codes  uint8 [B][H][T][CB]        pack_bits order per token (bit-exact
+ *                                       with PolarQuantizer::encode)
+ *   v_codes  uint8 [B][H][T/4][CB][4]   the same bytes, byte-interleaved by
+ *                                       groups of 4 tokens: byte j of token t
+ *                                       sits at ((t/4)*CB + j)*4 + t%4
+ *   k_meta   float [B][H][T][2]         {scale, zero_point} per K vector
+ *   v_meta   float [B][H][T][2]         {scale, zero_point} per V vector
+ * ====================================================================== */
+typedef struct sa_kv_cache sa_kv_cache;
+
+typedef struct sa_kv_cache_config {
+    int32_t num_layers;    /* KVCacheConfig::num_layers */
+    int32_t batch;         /* sequences decoded together (the reference is batch 1) */
+    int32_t num_heads;     /* query heads of the model (sizes the split-K workspace) */
+    int32_t num_kv_heads;  /* KVCacheConfig::num_kv_heads, model total */
+    int32_t kv_head_begin; /* first KV head held here (KV-head sharding); 0 if unsharded */
+    int32_t kv_head_count; /* KV heads held here; num_kv_heads if unsharded */
+    int32_t head_dim;      /* KVCacheConfig::head_dim: power of two, 16..256 */
+    int32_t max_seq_len;   /* GpuKvCache::max_seq_len */
+    int32_t bits;          /* KVCacheConfig::kv_quant_bits: 3, 4 or 8 */
+    uint64_t seed;         /* KVCacheConfig::seed (default 0xDEADBEEFCAFE1234) */
+} sa_kv_cache_config;
+
+/* Raw device pointers of one layer (GpuKvCache::view_at, kv_cache.rs:336-378). */
+typedef struct sa_kv_layer_view {
+    uint8_t *k_codes;
+    uint8_t *v_codes;
+    float *k_meta;
+    float *v_meta;
+    const float *signs;        /* [H][D] the +-1 sign vector of each local head, as float */
+    int32_t batch;
+    int32_t kv_heads;          /* local heads H */
+    int32_t head_dim;
+    int32_t bits;
+    int32_t code_bytes;        /* CB */
+    int32_t capacity;          /* T (padded capacity, tokens) */
+    float wht_scale;           /* 1 / sqrt_approx(head_dim), kv_compression.rs:100 */
+} sa_kv_layer_view;
+
+/* GpuKvCache::allocate (kv_cache.rs:129-193) + CompressedKVCache::new
+ * (kv_compression.rs:766-807).  Allocates every layer and the split-K
+ * workspace on the current device, zero-filled.  This is the only call that
+ * allocates device memory. */
+int sa_kv_cache_create(const sa_kv_cache_config *config, sa_kv_cache **out);
+/* Frees the cache (DeviceBuffer drop, onnx-rt/src/cuda/memory.rs). NULL is ok. */
+int sa_kv_cache_destroy(sa_kv_cache *cache);
+/* GpuKvCache::reset (kv_cache.rs:386): position back to 0, memory kept. */
+int sa_kv_cache_reset(sa_kv_cache *cache);
+/* GpuKvCache::current_position (kv_cache.rs:201). */
+int sa_kv_cache_position(const sa_kv_cache *cache, int64_t *position);
+/* Rewind or move the committed position (0 <= position <= max_seq_len). */
+int sa_kv_cache_set_position(sa_kv_cache *cache, int64_t position);
+/* GpuKvCache::advance_position (kv_cache.rs:281), by n tokens. */
+int sa_kv_cache_advance(sa_kv_cache *cache, int64_t n);
+/* The layer's device pointers and layout. */
+int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_view *view);
+/* Copy of the cache configuration. */
+int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config);
+
+/* Quantize-on-append: GpuKvCache::append (kv_cache.rs:233-277) fused with
+ * CompressedKVCache::write_kv (kv_compression.rs:814-854, kv_qjl_residual and
+ * kv_lowrank_k off) and with the K half of gqa_apply_rotary
+ * (ops/microsoft.rs:1004-1050).
+ *
+ * key/value: (batch, seq_len, kv_head_count * head_dim) in `dtype`.  Token s
+ * is written at position (cache position + s); RoPE on K uses that position
+ * as the cos/sin row.  The codes, scale and zero_point of every vector are
+ * bit-exact with PolarQuantizer::encode applied to the f32 value of the
+ * (rotated) input.  Does not advance the position. */
+int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void *value,
+                 int32_t dtype, int32_t batch, int32_t seq_len,
+                 const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                 int32_t do_rotary, int32_t rotary_interleaved, sa_stream_t stream);
+
+/* Attention of seq_len query tokens over the compressed cache: query token s
+ * sits at position p + s (p = cache position) and attends causally to cache
+ * tokens [0, p + s] -- scaled_dot_product_attention with causal mask and
+ * past_sk = p (ops/microsoft.rs:380-438), reading K/V through
+ * PolarQuantizer::decode semantics (computed in the rotated domain).
+ *
+ * query/attn_out: (batch, seq_len, q_heads_local * head_dim), q_heads_local =
+ * (num_heads / num_kv_heads) * kv_head_count.  RoPE is applied to the query
+ * in the kernel prologue when do_rotary is set.  has_scale selects the
+ * `scale` attribute, else 1/sqrt(head_dim) (sqrt_f32, ops/microsoft.rs:54).
+ * Positions beyond the appended tokens are never read. */
+int sa_gqa_attend(sa_kv_cache *cache, int32_t layer, const void *query, void *attn_out,
+                  int32_t dtype, int32_t batch, int32_t seq_len, int64_t num_heads,
+                  int32_t has_scale, float scale,
+                  const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                  int32_t do_rotary, int32_t rotary_interleaved, sa_stream_t stream);
+
+/* The operator: com.microsoft.GroupQueryAttention with the cache as past
+ * K/V -- op_group_query_attention (ops/microsoft.rs:1082-1196) as the GPU
+ * executor dispatches it with a cache (dispatch_gqa / gqa_with_cache,
+ * onnx-rt/src/cuda/gpu_executor.rs:917-968): validates the attributes like
+ * gqa_validate (:933-985), appends key/value (sa_kv_append) and runs
+ * sa_gqa_attend.  num_heads / kv_num_heads are the node attributes (model
+ * totals).  local_window_size must be -1 (the CPU op rejects windows,
+ * ops/microsoft.rs:1089-1094).  Only attn_out is produced: present K/V live in
+ * the cache (gpu_executor.rs:965-967).  Does not advance the position. */
+int sa_group_query_attention(sa_kv_cache *cache, int32_t layer,
+                             const void *query, const void *key, const void *value,
+                             void *attn_out, int32_t dtype, int32_t batch, int32_t seq_len,
+                             int64_t num_heads, int64_t kv_num_heads,
+                             int32_t has_scale, float scale, int64_t local_window_size,
+                             int32_t do_rotary, int32_t rotary_interleaved,
+                             const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                             sa_stream_t stream);
+
+/* ======================================================================
+ * MatMulNBits (ONNX Runtime com.microsoft.MatMulNBits contract; absent from
+ * the reference, which would register it next to MatMul in
+ * dispatch_gpu_node, onnx-rt/src/cuda/gpu_executor.rs:490-514).
+ *
+ *   a            (m, k) in dtype
+ *   b            uint8 (n, ceil(k/block_size), block_size*bits/8), low nibble first
+ *   scales       (n, ceil(k/block_size)) in dtype
+ *   zero_points  NULL (=> 2^(bits-1)) or uint8 (n, ceil(ceil(k/block_size)*bits/8)), packed
+ *   bias         NULL or (n) in dtype
+ *   y            (m, n) in dtype
+ * y[i][j] = sum_k a[i][k] * (code[j][k] - zp[j][k/bs]) * scale[j][k/bs] (+ bias[j]),
+ * accumulated in f32.  bits must be 4; block_size a power of two >= 16.
+ * ====================================================================== */
+int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales,
+                    const uint8_t *zero_points, const void *bias, void *y,
+                    int32_t dtype, int64_t m, int64_t n, int64_t k,
+                    int32_t bits, int32_t block_size, sa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SA_B200_H */

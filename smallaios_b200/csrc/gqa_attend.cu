@@ -1,0 +1,344 @@
+// GroupQueryAttention over the PolarQuant-compressed cache: generic split-K
+// kernel (any bits in {3,4,8}, head_dim 16..256, any group size <= 8, any
+// number of query tokens).  The fast decode kernel for the common shapes
+// lives in gqa_decode_mma.cu; this one covers everything else.
+//
+// Math (rotated domain).  The reference decodes every cached vector,
+// k_hat = S.H.(c*scale + zp)/sqrt(n) (PolarQuantizer::decode,
+// kv_compression.rs:270-286), and runs SDPA on k_hat (ops/microsoft.rs:
+// 241-319).  S.H/sqrt(n) is orthogonal and symmetric, so
+//   q . k_hat          = q' . (c*scale + zp) = scale*(q'.c) + zp*sum(q'),
+//   sum_t p_t v_hat_t  = S.H.(sum_t p_t (c_t*scale_t + zp_t))/sqrt(n),
+// with q' = H.S.q/sqrt(n), the same rotation encode applies.  The kernel
+// rotates q once, streams codes without ever decoding a vector, and applies
+// the inverse rotation once per output row.
+#include "sa_common.cuh"
+#include "sa_internal.h"
+
+namespace sa {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Layout {
+    int d, bits, cb, cap, heads, group;
+};
+
+// Code of element e from a token's packed row (pack_bits order, stride `step`
+// bytes between consecutive bytes of the row: 1 for K, 4 for interleaved V).
+__device__ __forceinline__ uint32_t code_at(const uint8_t *row, int step, int e, int bits, int cb) {
+    const int bo = e * bits;
+    const int j = bo >> 3, sh = bo & 7;
+    uint32_t w = row[(int64_t)j * step];
+    if (sh + bits > 8 && j + 1 < cb) w |= (uint32_t)row[(int64_t)(j + 1) * step] << 8;
+    return (w >> sh) & ((1u << bits) - 1u);
+}
+
+template <typename T, int EPL>
+__device__ __forceinline__ void rope_and_rotate(const T *src, float (&x)[EPL], int lane, int d, int64_t pos,
+                                                const AttendArgs &a, const float *sg) {
+    const bool active = lane * EPL < d;
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = active ? ld_f32(src + lane * EPL + r) : 0.0f;
+    if (a.do_rotary && active) {
+        const int half = d / 2;
+        const float *cr = a.cos_cache + pos * half;
+        const float *sr = a.sin_cache + pos * half;
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            const int e = lane * EPL + r;
+            int pair, partner;
+            bool first;
+            if (a.interleaved) {
+                pair = e >> 1;
+                first = (e & 1) == 0;
+                partner = first ? e + 1 : e - 1;
+            } else {
+                first = e < half;
+                pair = first ? e : e - half;
+                partner = first ? e + half : e - half;
+            }
+            const float c = cr[pair], sn = sr[pair];
+            const float xo = ld_f32(src + partner);
+            x[r] = first ? __fsub_rn(__fmul_rn(c, x[r]), __fmul_rn(sn, xo))
+                         : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x[r]));
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] *= active ? sg[lane * EPL + r] : 1.0f;
+    warp_wht_butterfly<EPL>(x, lane, d);
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] *= a.wht_scale;
+}
+
+// Inverse rotation of one output vector held as EPL values per lane and
+// store to out (dtype T).
+template <typename T, int EPL>
+__device__ __forceinline__ void unrotate_store(float (&x)[EPL], int lane, int d, const float *sg, float wht_scale,
+                                               T *dst) {
+    warp_wht_butterfly<EPL>(x, lane, d);
+    if (lane * EPL < d) {
+#pragma unroll
+        for (int r = 0; r < EPL; r++) st_from_f32(dst + lane * EPL + r, x[r] * wht_scale * sg[lane * EPL + r]);
+    }
+}
+
+// grid = (splits, heads, batch*seq_len), block = 32*kWarps.
+template <typename T, int EPL, int MAXG>
+__global__ void __launch_bounds__(32 * kWarps) attend_split_kernel(AttendArgs a, int n_splits, int tokens_per_split) {
+    extern __shared__ float smem[];
+    const int d = a.head_dim, G = a.group;
+    float *s_q = smem;                                   // [G][d] rotated queries
+    float *s_qsum = s_q + MAXG * d;                      // [G]
+    float *s_acc = s_qsum + MAXG;                        // [kWarps][G][d]
+    float *s_mlz = s_acc + kWarps * MAXG * d;            // [kWarps][G][3]
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
+    const int b = row / a.seq_len, s = row % a.seq_len;
+    const int64_t qpos = a.pos0 + s;
+    const int64_t total = qpos + 1;  // causal: keys [0, qpos]
+    const float *sg = a.signs + (int64_t)h * d;
+    const int qheads = a.heads * G;
+
+    // Prologue: RoPE + rotation of the G query heads of this KV head.
+    for (int g = warp; g < G; g += kWarps) {
+        const T *src = static_cast<const T *>(a.query) + ((int64_t)row * qheads + h * G + g) * d;
+        float x[EPL];
+        rope_and_rotate<T, EPL>(src, x, lane, d, qpos, a, sg);
+        float part = 0.0f;
+        if (lane * EPL < d) {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) {
+                s_q[g * d + lane * EPL + r] = x[r];
+                part += x[r];
+            }
+        }
+        part = warp_sum(part);
+        if (lane == 0) s_qsum[g] = part;
+    }
+    __syncthreads();
+
+    float q[MAXG][EPL], acc[MAXG][EPL], m[MAXG], l[MAXG], z[MAXG];
+    const bool active = lane * EPL < d;
+#pragma unroll
+    for (int g = 0; g < MAXG; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+        z[g] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            q[g][r] = (g < G && active) ? s_q[g * d + lane * EPL + r] : 0.0f;
+            acc[g][r] = 0.0f;
+        }
+    }
+
+    const int64_t hrow = (int64_t)b * a.heads + h;
+    const uint8_t *kc = a.k_codes + hrow * a.capacity * a.code_bytes;
+    const uint8_t *vc = a.v_codes + hrow * a.capacity * a.code_bytes;
+    const float *km = a.k_meta + hrow * a.capacity * 2;
+    const float *vm = a.v_meta + hrow * a.capacity * 2;
+    const int64_t t_begin = (int64_t)split * tokens_per_split;
+    int64_t t_end = t_begin + tokens_per_split;
+    if (t_end > total) t_end = total;
+
+    for (int64_t t = t_begin + warp; t < t_end; t += kWarps) {
+        const uint8_t *krow = kc + t * a.code_bytes;
+        const uint8_t *vrow = vc + ((t / kVGroup) * a.code_bytes) * kVGroup + (t % kVGroup);
+        float ck[EPL], cv[EPL];
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            const int e = lane * EPL + r;
+            ck[r] = active ? (float)code_at(krow, 1, e, a.bits, a.code_bytes) : 0.0f;
+            cv[r] = active ? (float)code_at(vrow, kVGroup, e, a.bits, a.code_bytes) : 0.0f;
+        }
+        const float kscale = km[t * 2], kzp = km[t * 2 + 1];
+        const float vscale = vm[t * 2], vzp = vm[t * 2 + 1];
+#pragma unroll
+        for (int g = 0; g < MAXG; g++) {
+            if (g >= G) break;
+            float dot = 0.0f;
+#pragma unroll
+            for (int r = 0; r < EPL; r++) dot += ck[r] * q[g][r];
+            dot = warp_sum(dot);
+            const float sc = (kscale * dot + kzp * s_qsum[g]) * a.scale * kLog2e;
+            const float mn = fmaxf(m[g], sc);
+            const float alpha = exp2f(m[g] - mn);
+            const float p = exp2f(sc - mn);
+            m[g] = mn;
+            l[g] = l[g] * alpha + p;
+            z[g] = z[g] * alpha + p * vzp;
+            const float pv = p * vscale;
+#pragma unroll
+            for (int r = 0; r < EPL; r++) acc[g][r] = acc[g][r] * alpha + pv * cv[r];
+        }
+    }
+
+    // Merge the warps of this CTA.
+    for (int g = 0; g < G; g++) {
+        if (lane == 0) {
+            s_mlz[(warp * MAXG + g) * 3 + 0] = m[g];
+            s_mlz[(warp * MAXG + g) * 3 + 1] = l[g];
+            s_mlz[(warp * MAXG + g) * 3 + 2] = z[g];
+        }
+        if (active) {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) s_acc[(warp * MAXG + g) * d + lane * EPL + r] = acc[g][r];
+        }
+    }
+    __syncthreads();
+
+    for (int g = warp; g < G; g += kWarps) {
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; w++) M = fmaxf(M, s_mlz[(w * MAXG + g) * 3]);
+        float L = 0.0f, Z = 0.0f, wts[kWarps];
+        for (int w = 0; w < kWarps; w++) {
+            const float mw = s_mlz[(w * MAXG + g) * 3];
+            wts[w] = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+            L += wts[w] * s_mlz[(w * MAXG + g) * 3 + 1];
+            Z += wts[w] * s_mlz[(w * MAXG + g) * 3 + 2];
+        }
+        float x[EPL];
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            float A = 0.0f;
+            if (active)
+                for (int w = 0; w < kWarps; w++) A += wts[w] * s_acc[(w * MAXG + g) * d + lane * EPL + r];
+            x[r] = A;
+        }
+        if (n_splits == 1) {
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+            for (int r = 0; r < EPL; r++) x[r] = L > 0.0f ? (x[r] + Z) * inv : 0.0f;
+            T *dst = static_cast<T *>(a.out) + ((int64_t)row * qheads + h * G + g) * d;
+            unrotate_store<T, EPL>(x, lane, d, sg, a.wht_scale, dst);
+        } else {
+            float *ws = a.workspace + ((((int64_t)row * a.heads + h) * n_splits + split) * G + g) * (d + 4);
+            if (active) {
+#pragma unroll
+                for (int r = 0; r < EPL; r++) ws[lane * EPL + r] = x[r];
+            }
+            if (lane == 0) {
+                ws[d] = M;
+                ws[d + 1] = L;
+                ws[d + 2] = Z;
+            }
+        }
+    }
+}
+
+// Merge split-K partials, normalise, inverse-rotate, store.
+// grid = (heads*group, batch*seq_len), block = 32.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(32) attend_combine_kernel(AttendArgs a, int n_splits) {
+    const int lane = threadIdx.x;
+    const int d = a.head_dim, G = a.group;
+    const int hg = blockIdx.x, row = blockIdx.y;
+    const int h = hg / G, g = hg % G;
+    const float *base = a.workspace + (((int64_t)row * a.heads + h) * n_splits * G + g) * (d + 4);
+    const int64_t sstride = (int64_t)G * (d + 4);
+    float M = -INFINITY;
+    for (int sp = 0; sp < n_splits; sp++) M = fmaxf(M, base[sp * sstride + d]);
+    float L = 0.0f, Z = 0.0f, x[EPL];
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = 0.0f;
+    const bool active = lane * EPL < d;
+    for (int sp = 0; sp < n_splits; sp++) {
+        const float *p = base + sp * sstride;
+        const float ms = p[d];
+        const float w = (ms == -INFINITY) ? 0.0f : exp2f(ms - M);
+        L += w * p[d + 1];
+        Z += w * p[d + 2];
+        if (active) {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) x[r] += w * p[lane * EPL + r];
+        }
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = L > 0.0f ? (x[r] + Z) * inv : 0.0f;
+    const int qheads = a.heads * G;
+    T *dst = static_cast<T *>(a.out) + ((int64_t)row * qheads + h * G + g) * d;
+    unrotate_store<T, EPL>(x, lane, d, a.signs + (int64_t)h * d, a.wht_scale, dst);
+}
+
+template <int MAXG>
+size_t split_smem_bytes(int d) {
+    return sizeof(float) * ((size_t)MAXG * d + MAXG + (size_t)kWarps * MAXG * d + (size_t)kWarps * MAXG * 3);
+}
+
+template <typename T, int EPL, int MAXG>
+int launch_generic(const AttendArgs &a, int n_splits, int tps, cudaStream_t stream) {
+    const size_t smem = split_smem_bytes<MAXG>(a.head_dim);
+    auto kern = attend_split_kernel<T, EPL, MAXG>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return check_cuda(e, "gqa_attend smem attribute");
+    }
+    const int rows = a.batch * a.seq_len;
+    dim3 grid(n_splits, a.heads, rows);
+    kern<<<grid, 32 * kWarps, smem, stream>>>(a, n_splits, tps);
+    count_launch();
+    int rc = check_cuda(cudaGetLastError(), "gqa_attend split launch");
+    if (rc != SA_OK || n_splits == 1) return rc;
+    attend_combine_kernel<T, EPL><<<dim3(a.heads * a.group, rows), 32, 0, stream>>>(a, n_splits);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "gqa_attend combine launch");
+}
+
+template <typename T, int EPL>
+int launch_by_group(const AttendArgs &a, int n_splits, int tps, cudaStream_t stream) {
+    if (a.group <= 1) return launch_generic<T, EPL, 1>(a, n_splits, tps, stream);
+    if (a.group <= 2) return launch_generic<T, EPL, 2>(a, n_splits, tps, stream);
+    if (a.group <= 4) return launch_generic<T, EPL, 4>(a, n_splits, tps, stream);
+    if (a.group <= 8) return launch_generic<T, EPL, 8>(a, n_splits, tps, stream);
+    return set_error(SA_ERR_UNSUPPORTED, "gqa_attend: group size %d > 8 not supported", a.group);
+}
+
+template <typename T>
+int launch_by_dim(const AttendArgs &a, int n_splits, int tps, cudaStream_t stream) {
+    switch (a.head_dim) {
+        case 16:
+        case 32: return launch_by_group<T, 1>(a, n_splits, tps, stream);
+        case 64: return launch_by_group<T, 2>(a, n_splits, tps, stream);
+        case 128: return launch_by_group<T, 4>(a, n_splits, tps, stream);
+        case 256: return launch_by_group<T, 8>(a, n_splits, tps, stream);
+        default: return set_error(SA_ERR_UNSUPPORTED, "gqa_attend: head_dim %d not supported", a.head_dim);
+    }
+}
+
+}  // namespace
+
+// Split-K partition: enough CTAs for a few waves, at least 256 tokens each,
+// within the workspace.
+void choose_splits(const AttendArgs &a, int64_t total, int *n_splits, int *tps) {
+    const int64_t units = (int64_t)a.batch * a.seq_len * a.heads;
+    int64_t want = (4LL * a.sm_count + units - 1) / units;
+    int64_t by_len = (total + 255) / 256;
+    int64_t n = want < by_len ? want : by_len;
+    if (n > kMaxSplits) n = kMaxSplits;
+    const int64_t per_split = (int64_t)a.group * (a.head_dim + 4);
+    const int64_t by_ws = per_split > 0 ? (int64_t)(a.workspace_floats / (size_t)(units * per_split)) : 0;
+    if (n > by_ws) n = by_ws;
+    if (n < 1) n = 1;
+    int64_t t = (total + n - 1) / n;
+    n = (total + t - 1) / t;
+    *n_splits = (int)n;
+    *tps = (int)t;
+}
+
+int launch_gqa_attend_generic(const AttendArgs &a, cudaStream_t stream) {
+    const int64_t total = a.pos0 + a.seq_len;
+    int n_splits, tps;
+    choose_splits(a, total, &n_splits, &tps);
+    switch (a.dtype) {
+        case SA_DTYPE_FLOAT: return launch_by_dim<float>(a, n_splits, tps, stream);
+        case SA_DTYPE_FLOAT16: return launch_by_dim<__half>(a, n_splits, tps, stream);
+        case SA_DTYPE_BFLOAT16: return launch_by_dim<__nv_bfloat16>(a, n_splits, tps, stream);
+        default: return set_error(SA_ERR_UNSUPPORTED, "gqa_attend: dtype %d not supported", a.dtype);
+    }
+}
+
+}  // namespace sa

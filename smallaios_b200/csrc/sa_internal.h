@@ -1,0 +1,82 @@
+// Internal (non-ABI) structures shared by the sa_b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/sa_b200.h"
+
+namespace sa {
+
+constexpr int kCapacityAlign = 64;   // token capacity is padded to this
+constexpr int kVGroup = 4;           // V codes are byte-interleaved by 4 tokens
+constexpr int kMaxSplits = 64;       // split-K partitions per (row, kv head)
+
+struct kv_cache_impl {
+    sa_kv_cache_config cfg;
+    int device;
+    int sm_count;
+    int capacity;      // padded token capacity
+    int code_bytes;    // head_dim * bits / 8
+    int group;         // num_heads / num_kv_heads
+    float wht_scale;   // 1 / sqrt_approx(head_dim)
+    int64_t position;  // committed tokens
+    // one device allocation carved into the arrays below
+    void *base;
+    size_t base_bytes;
+    uint8_t *k_codes;  // [L][B][H][T][CB]
+    uint8_t *v_codes;  // [L][B][H][T/4][CB][4]
+    float *k_meta;     // [L][B][H][T][2]
+    float *v_meta;     // [L][B][H][T][2]
+    float *signs;      // [L][H][D]  +-1.0f
+    float *workspace;  // split-K partials
+    size_t workspace_floats;
+    size_t layer_codes_bytes;  // B*H*T*CB
+    size_t layer_meta_floats;  // B*H*T*2
+};
+
+// Parameters of one append launch (K and V of `batch * seq_len` tokens).
+struct AppendArgs {
+    const void *key;
+    const void *value;
+    int dtype;
+    int batch, seq_len, heads, head_dim, bits, code_bytes, capacity;
+    int64_t pos0;
+    uint8_t *k_codes, *v_codes;
+    float *k_meta, *v_meta;
+    const float *signs;
+    float wht_scale;
+    const float *cos_cache, *sin_cache;
+    int cache_rows, do_rotary, interleaved;
+};
+
+// Parameters of one attention launch.
+struct AttendArgs {
+    const void *query;
+    void *out;
+    int dtype;
+    int batch, seq_len, heads, group, head_dim, bits, code_bytes, capacity;
+    int64_t pos0;  // tokens cached before query token 0
+    const uint8_t *k_codes, *v_codes;
+    const float *k_meta, *v_meta;
+    const float *signs;
+    float wht_scale;
+    float scale;  // attention scale
+    const float *cos_cache, *sin_cache;
+    int cache_rows, do_rotary, interleaved;
+    float *workspace;
+    size_t workspace_floats;
+    int sm_count;
+};
+
+int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
+int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
+int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
+                        const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
+                        int block_size, cudaStream_t stream);
+
+void count_launch(int n = 1);
+float host_sqrt_approx(float x);
+float host_sqrt_f32(float x);
+
+}  // namespace sa

@@ -1,0 +1,173 @@
+"""Compressed, GPU-resident KV cache.
+
+Host-side mirror of onnx-rt's ``GpuKvCache`` (onnx-rt/src/cuda/kv_cache.rs:
+111-388) carrying the compression state of ``CompressedKVCache``
+(onnx-rt/src/kv_compression.rs:742-925).  Storage, quantization and every
+kernel live in libsa_b200.so; this class owns the handle and exposes the
+layer views as torch tensors (zero-copy) for inspection.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+DEFAULT_SEED = 0xDEADBEEFCAFE1234  # KVCacheConfig::default (kv_compression.rs:724)
+
+
+class _DevArray:
+    """__cuda_array_interface__ wrapper so torch can view library memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _view(ptr: int, shape, typestr: str, device) -> torch.Tensor:
+    with torch.cuda.device(device):
+        return torch.as_tensor(_DevArray(ptr, shape, typestr), device=device)
+
+
+@dataclass
+class LayerView:
+    """GpuKvCache::view_at (kv_cache.rs:336-378), as torch tensors."""
+
+    k_codes: torch.Tensor  # uint8 (B, H, T, CB)
+    v_codes: torch.Tensor  # uint8 (B, H, T/4, CB, 4)  (4-token byte interleave)
+    k_meta: torch.Tensor   # f32 (B, H, T, 2) {scale, zero_point}
+    v_meta: torch.Tensor   # f32 (B, H, T, 2)
+    signs: torch.Tensor    # f32 (H, D) +-1
+    wht_scale: float
+    bits: int
+    code_bytes: int
+    capacity: int
+
+    def v_codes_tokens(self) -> torch.Tensor:
+        """V codes in per-token pack_bits order (B, H, T, CB)."""
+        b, h, tg, cb, g = self.v_codes.shape
+        return self.v_codes.permute(0, 1, 2, 4, 3).reshape(b, h, tg * g, cb)
+
+
+class GpuKvCache:
+    """Per-layer compressed K/V cache for a batch of sequences on one GPU.
+
+    Mirrors ``GpuKvCache::allocate/append/advance_position/current_position/
+    reset`` (kv_cache.rs).  ``kv_head_begin/kv_head_count`` select a shard of
+    the KV heads (KV-head sharding across GPUs); the PolarQuant seed of each
+    head still uses its global index, so a sharded cache holds exactly the
+    codes the unsharded one would.
+    """
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_seq_len: int, *,
+                 batch: int = 1, num_heads: int | None = None, bits: int = 4, seed: int = DEFAULT_SEED,
+                 kv_head_begin: int = 0, kv_head_count: int | None = None, device=None):
+        self.device = torch.device(device if device is not None else "cuda", )
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        cfg = _lib.KvCacheConfig()
+        cfg.num_layers = num_layers
+        cfg.batch = batch
+        cfg.num_heads = num_heads if num_heads is not None else num_kv_heads
+        cfg.num_kv_heads = num_kv_heads
+        cfg.kv_head_begin = kv_head_begin
+        cfg.kv_head_count = kv_head_count if kv_head_count is not None else num_kv_heads - kv_head_begin
+        cfg.head_dim = head_dim
+        cfg.max_seq_len = max_seq_len
+        cfg.bits = bits
+        cfg.seed = seed & (2**64 - 1)
+        self._handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib.sa_kv_cache_create(ctypes.byref(cfg), ctypes.byref(self._handle)))
+        self.config = cfg
+
+    # -- GpuKvCache API ------------------------------------------------------
+    @classmethod
+    def allocate(cls, num_layers, num_kv_heads, head_dim, max_seq_len, **kw) -> "GpuKvCache":
+        return cls(num_layers, num_kv_heads, head_dim, max_seq_len, **kw)
+
+    @property
+    def handle(self) -> int:
+        if not self._handle:
+            raise RuntimeError("GpuKvCache used after close()")
+        return self._handle.value
+
+    def num_layers(self) -> int:
+        return self.config.num_layers
+
+    def max_seq_len(self) -> int:
+        return self.config.max_seq_len
+
+    def current_position(self) -> int:
+        pos = ctypes.c_int64()
+        check(lib.sa_kv_cache_position(self.handle, ctypes.byref(pos)))
+        return pos.value
+
+    def set_position(self, position: int) -> None:
+        check(lib.sa_kv_cache_set_position(self.handle, position))
+
+    def advance_position(self, n: int = 1) -> None:
+        check(lib.sa_kv_cache_advance(self.handle, n))
+
+    def reset(self) -> None:
+        check(lib.sa_kv_cache_reset(self.handle))
+
+    def append(self, layer: int, new_k: torch.Tensor, new_v: torch.Tensor, *, cos_cache=None, sin_cache=None,
+               do_rotary: bool = False, rotary_interleaved: bool = False, stream=None) -> None:
+        """Quantize-on-append of (B, S, H*D) K/V at the current position."""
+        from .ops import _dtype_code, _stream_handle, _raise_op
+
+        _check_tensor(new_k, self.device)
+        _check_tensor(new_v, self.device)
+        if new_k.shape != new_v.shape or new_k.dim() != 3:
+            raise _shape("kv_cache_append: key and value must be (B, S, H*D) with equal shapes")
+        rows = 0 if cos_cache is None else cos_cache.shape[0]
+        rc = lib.sa_kv_append(self.handle, layer, new_k.data_ptr(), new_v.data_ptr(), _dtype_code(new_k),
+                              new_k.shape[0], new_k.shape[1], _ptr_or_none(cos_cache), _ptr_or_none(sin_cache),
+                              rows, int(do_rotary), int(rotary_interleaved), _stream_handle(stream, self.device))
+        _raise_op(rc, "kv_cache_append")
+
+    def view(self, layer: int) -> LayerView:
+        v = _lib.KvLayerView()
+        check(lib.sa_kv_cache_layer_view(self.handle, layer, ctypes.byref(v)))
+        B, H, T, CB, D = v.batch, v.kv_heads, v.capacity, v.code_bytes, v.head_dim
+        dev = self.device
+        return LayerView(
+            k_codes=_view(v.k_codes, (B, H, T, CB), "|u1", dev),
+            v_codes=_view(v.v_codes, (B, H, T // 4, CB, 4), "|u1", dev),
+            k_meta=_view(v.k_meta, (B, H, T, 2), "<f4", dev),
+            v_meta=_view(v.v_meta, (B, H, T, 2), "<f4", dev),
+            signs=_view(v.signs, (H, D), "<f4", dev),
+            wht_scale=v.wht_scale, bits=v.bits, code_bytes=CB, capacity=T)
+
+    def close(self) -> None:
+        if self._handle:
+            with torch.cuda.device(self.device):
+                lib.sa_kv_cache_destroy(self._handle.value)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _ptr_or_none(t):
+    return None if t is None else t.data_ptr()
+
+
+def _shape(msg):
+    from .ops import ShapeMismatch
+
+    return ShapeMismatch(msg)
+
+
+def _check_tensor(t: torch.Tensor, device) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")

@@ -1,0 +1,263 @@
+"""Operator-level API: the onnx-rt operators of the decode hot path on B200.
+
+Mirrors the reference's operator interface for this path:
+  * ``group_query_attention`` -- com.microsoft.GroupQueryAttention as the GPU
+    executor dispatches it with a KV cache (dispatch_gqa / gqa_with_cache,
+    onnx-rt/src/cuda/gpu_executor.rs:917-968; attribute parsing and
+    validation as op_group_query_attention, ops/microsoft.rs:1082-1196 and
+    the CPU arm executor.rs:2341-2362).
+  * ``matmul_nbits`` -- com.microsoft.MatMulNBits (ORT contract; the reference
+    has no such op and would register it next to MatMul in
+    dispatch_gpu_node, gpu_executor.rs:490-514).
+  * ``dispatch_gpu_node`` / ``KvCacheDispatchCtx`` / ``finalize_kv_cache`` --
+    the executor-side glue (gpu_executor.rs:277-280, 422, 490-514).
+
+Errors map the library's status codes onto the reference's OpError variants.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from ._lib import lib
+from .kv_cache import GpuKvCache
+
+
+# ---- OpError mirror (onnx-rt/src/operators.rs) ------------------------------
+class OpError(RuntimeError):
+    pass
+
+
+class InvalidAttribute(OpError):
+    pass
+
+
+class ShapeMismatch(OpError):
+    pass
+
+
+class UnsupportedOp(OpError):
+    pass
+
+
+class InternalError(OpError):
+    """CUDA failures, as the GPU executor wraps CudaError (gpu_executor.rs:963)."""
+
+
+class CapacityError(InternalError):
+    """kv_cache_append:position_overflow (kv_cache.rs:246-251)."""
+
+
+_STATUS_TO_ERROR = {
+    _lib.SA_ERR_INVALID_ATTRIBUTE: InvalidAttribute,
+    _lib.SA_ERR_SHAPE_MISMATCH: ShapeMismatch,
+    _lib.SA_ERR_UNSUPPORTED: UnsupportedOp,
+    _lib.SA_ERR_CAPACITY: CapacityError,
+    _lib.SA_ERR_INVALID_ARGUMENT: InvalidAttribute,
+}
+
+
+def _raise_op(status: int, op: str) -> None:
+    if status == _lib.SA_OK:
+        return
+    msg = lib.sa_last_error_string().decode(errors="replace")
+    cls = _STATUS_TO_ERROR.get(status, InternalError)
+    raise cls(f"{op}: {msg} [{lib.sa_status_string(status).decode()}]")
+
+
+_DTYPES = {torch.float32: _lib.SA_DTYPE_FLOAT, torch.float16: _lib.SA_DTYPE_FLOAT16,
+           torch.bfloat16: _lib.SA_DTYPE_BFLOAT16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise UnsupportedOp(f"dtype {t.dtype} not supported") from None
+
+
+def _stream_handle(stream, device) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _cuda(t, what):
+    if t is None:
+        return None
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{what} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+    return t
+
+
+def _rope_tables(cos_cache, sin_cache):
+    for name, t in (("cos_cache", cos_cache), ("sin_cache", sin_cache)):
+        if t is not None:
+            _cuda(t, name)
+            if t.dtype != torch.float32:
+                raise UnsupportedOp(f"{name} must be float32")
+            if t.dim() != 2:
+                raise ShapeMismatch("apply_rope_in_place: cos/sin caches must be rank-2")
+    if cos_cache is not None and sin_cache is not None and cos_cache.shape[1] != sin_cache.shape[1]:
+        raise ShapeMismatch("apply_rope_in_place: cos and sin caches must share the inner dim")
+    return (0 if cos_cache is None else cos_cache.shape[0])
+
+
+def group_query_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, cache: GpuKvCache,
+                          layer: int, *, num_heads: int, kv_num_heads: int, scale: float | None = None,
+                          local_window_size: int = -1, do_rotary: bool = True, rotary_interleaved: bool = False,
+                          cos_cache: torch.Tensor | None = None, sin_cache: torch.Tensor | None = None,
+                          out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """GroupQueryAttention with ``cache`` as past K/V; returns attn_out (B, S, Hq_local*D).
+
+    ``key``/``value`` (B, S, Hkv_local*D) are quantized into the cache at the
+    current position (RoPE'd when ``do_rotary``); the query attends causally to
+    every cached token up to its own position.  The position is not advanced
+    (call ``finalize_kv_cache`` / ``cache.advance_position`` once per forward
+    pass, as the reference executor does).
+    """
+    if query is None:
+        raise ShapeMismatch("GroupQueryAttention: missing query")
+    if key is None:
+        raise ShapeMismatch("GroupQueryAttention: missing key")
+    if value is None:
+        raise ShapeMismatch("GroupQueryAttention: missing value")
+    for name, t in (("query", query), ("key", key), ("value", value)):
+        _cuda(t, name)
+        if t.dim() != 3:
+            raise ShapeMismatch("GroupQueryAttention: Q/K/V must be rank-3")
+    if key.shape != value.shape:
+        raise ShapeMismatch("GroupQueryAttention: key and value must have the same shape")
+    if not (query.dtype == key.dtype == value.dtype):
+        raise UnsupportedOp("GroupQueryAttention: Q/K/V dtypes differ")
+    cfg = cache.config
+    if num_heads > 0 and kv_num_heads > 0 and num_heads % kv_num_heads == 0:
+        d = cfg.head_dim
+        g = num_heads // kv_num_heads
+        if query.shape[2] != g * cfg.kv_head_count * d or key.shape[2] != cfg.kv_head_count * d:
+            raise ShapeMismatch("GroupQueryAttention: hidden sizes do not match the cache's heads/head_dim")
+        if query.shape[:2] != key.shape[:2]:
+            raise ShapeMismatch("GroupQueryAttention: Q and K batch/sequence differ")
+    rows = _rope_tables(cos_cache, sin_cache)
+    if out is None:
+        out = torch.empty_like(query)
+    rc = lib.sa_group_query_attention(
+        cache.handle, layer, query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+        _dtype_code(query), query.shape[0], query.shape[1], int(num_heads), int(kv_num_heads),
+        int(scale is not None), float(scale or 0.0), int(local_window_size), int(bool(do_rotary)),
+        int(bool(rotary_interleaved)), None if cos_cache is None else cos_cache.data_ptr(),
+        None if sin_cache is None else sin_cache.data_ptr(), rows, _stream_handle(stream, query.device))
+    _raise_op(rc, "GroupQueryAttention")
+    return out
+
+
+def gqa_attend(query: torch.Tensor, cache: GpuKvCache, layer: int, *, num_heads: int, scale: float | None = None,
+               do_rotary: bool = True, rotary_interleaved: bool = False, cos_cache=None, sin_cache=None,
+               out=None, stream=None) -> torch.Tensor:
+    """Attention only (no append): queries at positions [p, p+S) over cache tokens [0, p+S)."""
+    _cuda(query, "query")
+    rows = _rope_tables(cos_cache, sin_cache)
+    if out is None:
+        out = torch.empty_like(query)
+    rc = lib.sa_gqa_attend(cache.handle, layer, query.data_ptr(), out.data_ptr(), _dtype_code(query),
+                           query.shape[0], query.shape[1], int(num_heads), int(scale is not None),
+                           float(scale or 0.0), None if cos_cache is None else cos_cache.data_ptr(),
+                           None if sin_cache is None else sin_cache.data_ptr(), rows, int(bool(do_rotary)),
+                           int(bool(rotary_interleaved)), _stream_handle(stream, query.device))
+    _raise_op(rc, "gqa_attend")
+    return out
+
+
+def matmul_nbits(a: torch.Tensor, b: torch.Tensor, scales: torch.Tensor, zero_points: torch.Tensor | None = None,
+                 bias: torch.Tensor | None = None, *, K: int, N: int, bits: int = 4, block_size: int = 32,
+                 out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """com.microsoft.MatMulNBits: Y[..., N] = A[..., K] . dequant(B)^T (+ bias)."""
+    _cuda(a, "A")
+    _cuda(b, "B")
+    _cuda(scales, "scales")
+    _cuda(zero_points, "zero_points")
+    _cuda(bias, "bias")
+    if bits != 4:
+        raise UnsupportedOp(f"MatMulNBits: bits={bits} not supported (4 only)")
+    if a.shape[-1] != K:
+        raise ShapeMismatch(f"MatMulNBits: A inner dim {a.shape[-1]} != K={K}")
+    if b.dtype != torch.uint8:
+        raise UnsupportedOp("MatMulNBits: B must be uint8")
+    if scales.dtype != a.dtype:
+        raise UnsupportedOp("MatMulNBits: scales must have A's dtype")
+    if zero_points is not None and zero_points.dtype != torch.uint8:
+        raise UnsupportedOp("MatMulNBits: only packed uint8 zero_points are supported")
+    nblk = (K + block_size - 1) // block_size
+    if b.numel() != N * nblk * (block_size * bits // 8):
+        raise ShapeMismatch("MatMulNBits: B size does not match (N, k_blocks, blob_size)")
+    if scales.numel() != N * nblk:
+        raise ShapeMismatch("MatMulNBits: scales size does not match N * k_blocks")
+    m = a.numel() // K
+    if out is None:
+        out = torch.empty(*a.shape[:-1], N, dtype=a.dtype, device=a.device)
+    rc = lib.sa_matmul_nbits(a.data_ptr(), b.data_ptr(), scales.data_ptr(),
+                             None if zero_points is None else zero_points.data_ptr(),
+                             None if bias is None else bias.data_ptr(), out.data_ptr(), _dtype_code(a), m, N, K,
+                             bits, block_size, _stream_handle(stream, a.device))
+    _raise_op(rc, "MatMulNBits")
+    return out
+
+
+# ---- executor glue ------------------------------------------------------------
+SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits")
+
+
+def supports_op(op_type: str) -> bool:
+    """CudaRuntime::supports_op (onnx-rt/src/cuda/mod.rs:874-889) for this path."""
+    return op_type in SUPPORTED_OPS
+
+
+@dataclass
+class KvCacheDispatchCtx:
+    """KvCacheDispatchCtx (gpu_executor.rs:277-280)."""
+
+    cache: GpuKvCache
+    next_layer_idx: int = 0
+    rope: dict = field(default_factory=dict)  # optional cos_cache / sin_cache tensors
+
+
+def dispatch_gpu_node(op_type: str, inputs: list, attrs: dict, kv_cache_ctx: KvCacheDispatchCtx | None = None):
+    """dispatch_gpu_node (gpu_executor.rs:490-514) for the ops of this path.
+
+    GroupQueryAttention inputs follow the ORT order (query, key, value,
+    past_key, past_value, seqlens_k, total_sequence_length, cos_cache,
+    sin_cache); past K/V come from the cache, so inputs 3-6 are ignored as in
+    the reference GPU executor.  Returns the list of outputs ([attn_out]).
+    """
+    if op_type == "GroupQueryAttention":
+        if kv_cache_ctx is None:
+            raise InternalError("GroupQueryAttention on this path needs a KV cache context")
+        inp = list(inputs) + [None] * (9 - len(inputs))
+        layer = kv_cache_ctx.next_layer_idx
+        kv_cache_ctx.next_layer_idx += 1
+        scale = attrs.get("scale")
+        out = group_query_attention(
+            inp[0], inp[1], inp[2], kv_cache_ctx.cache, layer,
+            num_heads=int(attrs.get("num_heads", 0)), kv_num_heads=int(attrs.get("kv_num_heads", 0)),
+            scale=None if scale is None else float(scale),
+            local_window_size=int(attrs.get("local_window_size", -1)),
+            do_rotary=bool(int(attrs.get("do_rotary", 1))),
+            rotary_interleaved=bool(int(attrs.get("rotary_interleaved", 0))),
+            cos_cache=inp[7] if inp[7] is not None else kv_cache_ctx.rope.get("cos_cache"),
+            sin_cache=inp[8] if inp[8] is not None else kv_cache_ctx.rope.get("sin_cache"))
+        return [out]
+    if op_type == "MatMulNBits":
+        inp = list(inputs) + [None] * (6 - len(inputs))
+        return [matmul_nbits(inp[0], inp[1], inp[2], inp[3], inp[5], K=int(attrs["K"]), N=int(attrs["N"]),
+                             bits=int(attrs.get("bits", 4)), block_size=int(attrs.get("block_size", 32)))]
+    raise InternalError(f"GPU executor: no GPU implementation for {op_type}")
+
+
+def finalize_kv_cache(ctx: KvCacheDispatchCtx | None, tokens: int = 1) -> None:
+    """finalize_kv_cache (gpu_executor.rs:422): one advance per forward pass."""
+    if ctx is not None and ctx.next_layer_idx > 0:
+        ctx.cache.advance_position(tokens)

@@ -1,0 +1,64 @@
+"""Shared test helpers: seeded synthetic inputs and oracle compositions.
+
+The oracle (oracle/) is only used here as the checker.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle
+
+
+def rng(seed: int) -> np.random.Generator:
+    return np.random.default_rng(seed)
+
+
+def rope_tables(rows: int, head_dim: int, theta: float = 10000.0):
+    return oracle.rope_tables(rows, head_dim // 2, theta)
+
+
+def oracle_append(k_bshd: np.ndarray, v_bshd: np.ndarray, signs_hd: np.ndarray, bits: int, pos0: int,
+                  cos=None, sin=None, do_rotary=False, interleaved=False):
+    """Reference codes for appending K/V (B, S, H, D) at positions pos0..pos0+S-1.
+
+    RoPE via apply_rope_in_place then PolarQuantizer::encode per vector.
+    Returns k_codes, k_meta, v_codes, v_meta shaped (B, H, S, ...).
+    """
+    b, s, h, d = k_bshd.shape
+    k = np.ascontiguousarray(np.transpose(k_bshd, (0, 2, 1, 3)), np.float32)  # (B, H, S, D)
+    v = np.ascontiguousarray(np.transpose(v_bshd, (0, 2, 1, 3)), np.float32)
+    if do_rotary:
+        k = oracle.apply_rope(k, cos, sin, np.arange(pos0, pos0 + s), interleaved=interleaved)
+    cb = oracle.code_bytes(d, bits)
+    kc = np.zeros((b, h, s, cb), np.uint8)
+    vc = np.zeros_like(kc)
+    km = np.zeros((b, h, s, 2), np.float32)
+    vm = np.zeros_like(km)
+    for hi in range(h):
+        c, m = oracle.polar_encode_many(k[:, hi], bits, signs_hd[hi])
+        kc[:, hi], km[:, hi] = c, m
+        c, m = oracle.polar_encode_many(v[:, hi], bits, signs_hd[hi])
+        vc[:, hi], vm[:, hi] = c, m
+    return kc, km, vc, vm
+
+
+def oracle_attend(q_bshd: np.ndarray, kc, km, vc, vm, signs_hd, bits, pos0, scale=None, cos=None, sin=None,
+                  do_rotary=False, interleaved=False):
+    """Composite oracle: RoPE q at positions pos0.., read_k/read_v, causal SDPA.
+
+    q_bshd: (B, S, Hq, D); codes/meta (B, Hkv, T, ...) with T = pos0 + S.
+    Returns (B, S, Hq*D).
+    """
+    b, s, hq, d = q_bshd.shape
+    q = np.ascontiguousarray(np.transpose(q_bshd, (0, 2, 1, 3)), np.float32)
+    if do_rotary:
+        q = oracle.apply_rope(q, cos, sin, np.arange(pos0, pos0 + s), interleaved=interleaved)
+    if scale is None:
+        scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(d)))
+    return oracle.compressed_gqa(q, kc, km, vc, vm, signs_hd, bits, scale)
+
+
+def interleave_v(vc_tokens: np.ndarray) -> np.ndarray:
+    """(B, H, T, CB) per-token codes -> (B, H, T/4, CB, 4) library layout."""
+    b, h, t, cb = vc_tokens.shape
+    return np.ascontiguousarray(vc_tokens.reshape(b, h, t // 4, 4, cb).transpose(0, 1, 2, 4, 3))

@@ -1,0 +1,87 @@
+"""MatMulNBits on the GPU vs the oracle (dequantize in f32 + gemm_f32).
+
+Parity is unpinned (the reference has no MatMulNBits): the oracle restates the
+ORT contract on the reference's own f32 GEMM.  Bar: max-abs 1e-3 with f32
+activations; fp16/bf16 outputs add half an ulp of the output dtype.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import rng
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(m, n, k, block=32, zp=False, bias=False, seed=0, adtype=torch.float32):
+    r = rng(seed)
+    nblk = k // block
+    codes = r.integers(0, 256, size=(n, nblk, block // 2), dtype=np.uint8)
+    scales = r.uniform(0.005, 0.02, size=(n, nblk)).astype(np.float16).astype(np.float32)
+    a = r.standard_normal((m, k)).astype(np.float32)
+    a = torch.from_numpy(a).to(adtype).float().numpy()
+    if adtype != torch.float32:
+        scales = torch.from_numpy(scales).to(adtype).float().numpy()
+    zps = r.integers(0, 256, size=(n, (nblk + 1) // 2), dtype=np.uint8) if zp else None
+    bvec = r.standard_normal(n).astype(np.float32) if bias else None
+    if bvec is not None:
+        bvec = torch.from_numpy(bvec).to(adtype).float().numpy()
+    want = oracle.matmul_nbits(a, codes, scales, zps, n=n, k=k, block_size=block)
+    if bvec is not None:
+        want = want + bvec[None, :]
+    return a, codes, scales, zps, bvec, want
+
+
+def _run(dev, m, n, k, adtype=torch.float32, **kw):
+    import smallaios_b200 as sa
+
+    a, codes, scales, zps, bvec, want = _case(m, n, k, adtype=adtype, **kw)
+    t = lambda x, dt: None if x is None else torch.from_numpy(x).to(dt).to(dev)
+    y = sa.matmul_nbits(t(a, adtype), t(codes, torch.uint8), t(scales, adtype), t(zps, torch.uint8),
+                        t(bvec, adtype), K=k, N=n, block_size=kw.get("block", 32))
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    if adtype == torch.float32:
+        bound = 1e-3
+    else:
+        ulp = 2.0 ** -8 if adtype == torch.bfloat16 else 2.0 ** -11
+        bound = 1e-3 + np.abs(want) * ulp
+    err = np.abs(got - want)
+    assert np.all(err <= bound), f"max err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 13])
+def test_gemv_f32(cuda_device, m):
+    _run(cuda_device, m, 384, 1024, seed=m)
+
+
+def test_c2_shape_m1_fp16(cuda_device):
+    """BASELINE config 2 decode shape: K=4096, N=14336, block 32, zp 8, fp16."""
+    _run(cuda_device, 1, 14336, 4096, adtype=torch.float16, seed=21)
+
+
+def test_c2_shape_m64_fp16(cuda_device):
+    _run(cuda_device, 64, 14336, 4096, adtype=torch.float16, seed=22)
+
+
+@pytest.mark.parametrize("block", [16, 32, 64, 128])
+def test_block_sizes_zero_points_bias(cuda_device, block):
+    _run(cuda_device, 2, 200, 512, block=block, zp=True, bias=True, seed=block)
+
+
+def test_bf16(cuda_device):
+    _run(cuda_device, 4, 256, 2048, adtype=torch.bfloat16, seed=5)
+
+
+def test_errors(cuda_device):
+    import smallaios_b200 as sa
+
+    dev = cuda_device
+    a = torch.zeros(1, 64, device=dev)
+    b = torch.zeros(8, 2, 16, dtype=torch.uint8, device=dev)
+    s = torch.zeros(8, 2, device=dev)
+    with pytest.raises(sa.UnsupportedOp):
+        sa.matmul_nbits(a, b, s, K=64, N=8, bits=3)
+    with pytest.raises(sa.ShapeMismatch):
+        sa.matmul_nbits(a, b, s, K=32, N=8)
