@@ -188,6 +188,42 @@ int sa_group_query_attention(sa_kv_cache *cache, int32_t layer,
                              const float *cos_cache, const float *sin_cache, int32_t cache_rows,
                              sa_stream_t stream);
 
+/* Allocation-free variant of sa_gqa_attend.  It has no counterpart in the
+ * reference.
+ *
+ * It serves callers that may not allocate device memory while they run.
+ * Examples are a real-time partition that reserves every buffer at start-up
+ * so that an inference step has a bounded, failure-free footprint, or a host
+ * whose memory belongs to its own pool.  sa_gqa_attend needs a cache handle,
+ * and that handle owns a library-allocated split-K workspace.  This call
+ * instead reads the caller's cache buffers, described by `layer` in the
+ * layout documented above (for example filled by sa_kv_cache_layer_view, or
+ * pointing into memory the caller manages).  It keeps its split-K partials
+ * in a fixed array of SA_STATIC_SCRATCH_BYTES that the library's CUDA module
+ * reserves on every GPU that loads it, until the process exits.  It calls no
+ * cudaMalloc, cudaFree or allocating routine.
+ *
+ *   - past_len tokens are cached before query token 0.  Query token s attends
+ *     to [0, past_len + s].  group = query heads per KV head (1..8).  The other
+ *     arguments mean what they mean for sa_gqa_attend.
+ *   - The first call on each device resolves the array's device address
+ *     (cudaGetSymbolAddress) with that device current.  Make that first call
+ *     before any stream capture.
+ *   - Limit: the partials take batch * seq_len * kv_heads * group *
+ *     (head_dim + 4) floats per split.  The call uses as many splits as fit.
+ *     When the problem wants splits and two do not fit, it returns
+ *     SA_ERR_CAPACITY with the sizes in sa_last_error_string().
+ *   - Every call on a device shares the one array, and the array keeps the
+ *     last call's contents.  Each call writes every partial before it reads
+ *     it, so nothing needs clearing.  Calls that overlap on the GPU (other
+ *     streams or threads) race on it: serialise them. */
+#define SA_STATIC_SCRATCH_BYTES (8u << 20)
+int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t past_len, const void *query,
+                           void *attn_out, int32_t dtype, int32_t batch, int32_t seq_len,
+                           int32_t group, int32_t has_scale, float scale,
+                           const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                           int32_t do_rotary, int32_t rotary_interleaved, sa_stream_t stream);
+
 /* ======================================================================
  * MatMulNBits (ONNX Runtime com.microsoft.MatMulNBits contract; absent from
  * the reference, which would register it next to MatMul in

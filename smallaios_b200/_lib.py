@@ -33,8 +33,9 @@ EXPORTED = [
     "sa_last_error_string", "sa_status_string", "sa_version", "sa_kernel_launches",
     "sa_kv_cache_create", "sa_kv_cache_destroy", "sa_kv_cache_reset", "sa_kv_cache_position",
     "sa_kv_cache_set_position", "sa_kv_cache_advance", "sa_kv_cache_layer_view", "sa_kv_cache_get_config",
-    "sa_kv_append", "sa_gqa_attend", "sa_group_query_attention", "sa_matmul_nbits",
+    "sa_kv_append", "sa_gqa_attend", "sa_group_query_attention", "sa_matmul_nbits", "sa_gqa_attend_no_alloc",
 ]
+SA_STATIC_SCRATCH_BYTES = 8 << 20
 
 
 class KvCacheConfig(ctypes.Structure):
@@ -107,6 +108,9 @@ def _declare(l: ctypes.CDLL) -> None:
     l.sa_group_query_attention.restype = ctypes.c_int
     l.sa_group_query_attention.argtypes = [_P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I32, _F, _I64,
                                            _I32, _I32, _P, _P, _I32, _P]
+    l.sa_gqa_attend_no_alloc.restype = ctypes.c_int
+    l.sa_gqa_attend_no_alloc.argtypes = [ctypes.POINTER(KvLayerView), _I64, _P, _P, _I32, _I32, _I32, _I32, _I32, _F,
+                                         _P, _P, _I32, _I32, _I32, _P]
     l.sa_matmul_nbits.restype = ctypes.c_int
     l.sa_matmul_nbits.argtypes = [_P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I64, _I32, _I32, _P]
 

@@ -342,3 +342,165 @@ int launch_gqa_attend_generic(const AttendArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace sa
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention entry point.
+//
+// Some callers may not allocate device memory once they are running: a
+// real-time partition that reserves every buffer at start-up so that an
+// inference step has a bounded, failure-free memory footprint, or a host
+// whose memory is owned by its own pool and must not see a cudaMalloc /
+// cudaFree from a library.  sa_gqa_attend needs a cache handle, and that
+// handle owns a split-K workspace the library allocated.  This entry point
+// instead takes the caller's cache buffers directly (an sa_kv_layer_view the
+// caller fills in) and keeps its split-K partials in the fixed array below,
+// which the CUDA module reserves on every GPU that loads the library and keeps
+// until the process exits.  It never calls cudaMalloc, cudaFree or any
+// allocating routine.
+// ---------------------------------------------------------------------------
+namespace sa {
+namespace {
+
+constexpr size_t kStaticScratchFloats = SA_STATIC_SCRATCH_BYTES / sizeof(float);
+constexpr int kMaxDevices = 64;
+
+// Split-K partials of the allocation-free path.  Host code must not pass this
+// name to a kernel: on the host it is only a stand-in for the symbol, so its
+// device address is looked up with cudaGetSymbolAddress once per device.
+static __device__ __align__(256) float g_static_scratch[kStaticScratchFloats];
+
+struct StaticScratchSlot {
+    float *ptr;
+    int sm_count;
+};
+static StaticScratchSlot g_scratch_slots[kMaxDevices];
+static int g_scratch_ready[kMaxDevices];  // 0 = not set up, 1 = ready
+
+// One-time set-up on the current device (the first call on each device does
+// it): resolve the array's device address and the SM count.  Concurrent
+// first calls on one device may both resolve it; they store the same values.
+int static_scratch_for_current_device(StaticScratchSlot *slot) {
+    int dev = -1;
+    int rc = check_cuda(cudaGetDevice(&dev), "gqa_attend_no_alloc: cudaGetDevice");
+    if (rc != SA_OK) return rc;
+    if (dev < 0 || dev >= kMaxDevices)
+        return set_error(SA_ERR_UNSUPPORTED, "gqa_attend_no_alloc: device %d beyond %d", dev, kMaxDevices);
+    if (__atomic_load_n(&g_scratch_ready[dev], __ATOMIC_ACQUIRE)) {
+        *slot = g_scratch_slots[dev];
+        return SA_OK;
+    }
+    StaticScratchSlot s;
+    s.ptr = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(reinterpret_cast<void **>(&s.ptr), g_static_scratch),
+                    "gqa_attend_no_alloc: cudaGetSymbolAddress(static scratch)");
+    if (rc != SA_OK) return rc;
+    if (s.ptr == nullptr) return set_error(SA_ERR_CUDA, "gqa_attend_no_alloc: static scratch has no device address");
+    s.sm_count = 0;
+    rc = check_cuda(cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev),
+                    "gqa_attend_no_alloc: SM count");
+    if (rc != SA_OK) return rc;
+    if (s.sm_count <= 0) s.sm_count = 148;
+    g_scratch_slots[dev] = s;
+    __atomic_store_n(&g_scratch_ready[dev], 1, __ATOMIC_RELEASE);
+    *slot = s;
+    return SA_OK;
+}
+
+}  // namespace
+}  // namespace sa
+
+extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t past_len, const void *query,
+                                      void *attn_out, int32_t dtype, int32_t batch, int32_t seq_len,
+                                      int32_t group, int32_t has_scale, float scale, const float *cos_cache,
+                                      const float *sin_cache, int32_t cache_rows, int32_t do_rotary,
+                                      int32_t rotary_interleaved, sa_stream_t stream) {
+    using namespace sa;
+    if (!layer) return set_error(SA_ERR_INVALID_ARGUMENT, "gqa_attend_no_alloc: NULL layer view");
+    const sa_kv_layer_view &v = *layer;
+    if (!v.k_codes || !v.v_codes || !v.k_meta || !v.v_meta || !v.signs)
+        return set_error(SA_ERR_INVALID_ARGUMENT, "gqa_attend_no_alloc: NULL pointer in the layer view");
+    const int d = v.head_dim;
+    if (d < 16 || d > 256 || (d & (d - 1)) != 0)
+        return set_error(SA_ERR_UNSUPPORTED, "gqa_attend_no_alloc: head_dim %d not a power of two in 16..256", d);
+    if (v.bits != 3 && v.bits != 4 && v.bits != 8)
+        return set_error(SA_ERR_INVALID_ATTRIBUTE, "bits must be 3, 4, or 8");
+    if (v.code_bytes != d * v.bits / 8)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: code_bytes %d != head_dim*bits/8", v.code_bytes);
+    if (v.kv_heads <= 0 || v.batch <= 0 || v.capacity <= 0 || v.capacity % kVGroup != 0)
+        return set_error(SA_ERR_SHAPE_MISMATCH,
+                         "gqa_attend_no_alloc: kv_heads/batch must be > 0 and capacity a positive multiple of 4");
+    if (group < 1 || group > 8)
+        return set_error(SA_ERR_UNSUPPORTED, "gqa_attend_no_alloc: group size %d outside 1..8", group);
+    if (dtype != SA_DTYPE_FLOAT && dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16)
+        return set_error(SA_ERR_UNSUPPORTED, "gqa_attend_no_alloc: dtype %d not supported", dtype);
+    if (batch != v.batch)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: batch %d != view batch %d", batch, v.batch);
+    if (seq_len < 0 || past_len < 0)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: negative seq_len/past_len");
+    if (seq_len == 0) return SA_OK;
+    if (!query || !attn_out) return set_error(SA_ERR_INVALID_ARGUMENT, "gqa_attend_no_alloc: NULL query/attn_out");
+    if (past_len + seq_len > v.capacity)
+        return set_error(SA_ERR_CAPACITY, "gqa_attend_no_alloc: %lld tokens exceed the view capacity %d",
+                         (long long)(past_len + seq_len), v.capacity);
+    if (do_rotary) {
+        if (!cos_cache || !sin_cache)
+            return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: do_rotary=1 but cos/sin cache missing");
+        if (past_len + seq_len - 1 >= cache_rows)
+            return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: position %lld out of cache range %d",
+                             (long long)(past_len + seq_len - 1), cache_rows);
+    }
+
+    StaticScratchSlot slot;
+    int rc = static_scratch_for_current_device(&slot);
+    if (rc != SA_OK) return rc;
+
+    AttendArgs a;
+    a.query = query;
+    a.out = attn_out;
+    a.dtype = dtype;
+    a.batch = batch;
+    a.seq_len = seq_len;
+    a.heads = v.kv_heads;
+    a.group = group;
+    a.head_dim = d;
+    a.bits = v.bits;
+    a.code_bytes = v.code_bytes;
+    a.capacity = v.capacity;
+    a.pos0 = past_len;
+    a.k_codes = v.k_codes;
+    a.v_codes = v.v_codes;
+    a.k_meta = v.k_meta;
+    a.v_meta = v.v_meta;
+    a.signs = v.signs;
+    a.wht_scale = v.wht_scale;
+    a.scale = has_scale ? scale : 1.0f / host_sqrt_f32((float)d);
+    a.cos_cache = cos_cache;
+    a.sin_cache = sin_cache;
+    a.cache_rows = cache_rows;
+    a.do_rotary = do_rotary ? 1 : 0;
+    a.interleaved = rotary_interleaved ? 1 : 0;
+    a.workspace = slot.ptr;
+    a.workspace_floats = kStaticScratchFloats;
+    a.sm_count = slot.sm_count;
+
+    // The split count the library would pick with unlimited scratch; a problem
+    // that wants a split but cannot fit even two splits' partials is rejected.
+    const int64_t total = past_len + seq_len;
+    AttendArgs unlimited = a;
+    unlimited.workspace_floats = (size_t)1 << 60;
+    int want_splits = 1, tps = 0;
+    choose_splits(unlimited, total, &want_splits, &tps);
+    const size_t per_split = (size_t)batch * seq_len * v.kv_heads * group * (d + 4);
+    if (want_splits > 1 && 2 * per_split > kStaticScratchFloats)
+        return set_error(SA_ERR_CAPACITY,
+                         "gqa_attend_no_alloc: split-K partials need %zu bytes (2 splits of %zu), above the "
+                         "static scratch maximum of %zu bytes",
+                         2 * per_split * sizeof(float), per_split * sizeof(float), (size_t)SA_STATIC_SCRATCH_BYTES);
+    int n_splits = 1;
+    choose_splits(a, total, &n_splits, &tps);
+    switch (dtype) {
+        case SA_DTYPE_FLOAT: return launch_by_dim<float>(a, n_splits, tps, static_cast<cudaStream_t>(stream));
+        case SA_DTYPE_FLOAT16: return launch_by_dim<__half>(a, n_splits, tps, static_cast<cudaStream_t>(stream));
+        default: return launch_by_dim<__nv_bfloat16>(a, n_splits, tps, static_cast<cudaStream_t>(stream));
+    }
+}
