@@ -329,6 +329,28 @@ void choose_splits(const AttendArgs &a, int64_t total, int *n_splits, int *tps) 
     *tps = (int)t;
 }
 
+// Split merge + normalisation + inverse rotation for a workspace filled by
+// any split kernel (same partial format).
+int launch_gqa_combine(const AttendArgs &a, int n_splits, cudaStream_t stream) {
+    const dim3 grid(a.heads * a.group, a.batch * a.seq_len);
+    switch (a.dtype) {
+        case SA_DTYPE_FLOAT:
+            if (a.head_dim == 64) attend_combine_kernel<float, 2><<<grid, 32, 0, stream>>>(a, n_splits);
+            else attend_combine_kernel<float, 4><<<grid, 32, 0, stream>>>(a, n_splits);
+            break;
+        case SA_DTYPE_FLOAT16:
+            if (a.head_dim == 64) attend_combine_kernel<__half, 2><<<grid, 32, 0, stream>>>(a, n_splits);
+            else attend_combine_kernel<__half, 4><<<grid, 32, 0, stream>>>(a, n_splits);
+            break;
+        default:
+            if (a.head_dim == 64) attend_combine_kernel<__nv_bfloat16, 2><<<grid, 32, 0, stream>>>(a, n_splits);
+            else attend_combine_kernel<__nv_bfloat16, 4><<<grid, 32, 0, stream>>>(a, n_splits);
+            break;
+    }
+    count_launch();
+    return check_cuda(cudaGetLastError(), "gqa_attend combine launch");
+}
+
 int launch_gqa_attend_generic(const AttendArgs &a, cudaStream_t stream) {
     const int64_t total = a.pos0 + a.seq_len;
     int n_splits, tps;
