@@ -81,9 +81,12 @@ uint64_t sa_kernel_launches(void);
  * a multiple of 64):
  *   k_codes  uint8 [B][H][T][CB]        pack_bits order per token (bit-exact
  *                                       with PolarQuantizer::encode)
- *   v_codes  uint8 [B][H][T/4][CB][4]   the same bytes, byte-interleaved by
- *                                       groups of 4 tokens: byte j of token t
- *                                       sits at ((t/4)*CB + j)*4 + t%4
+ *   v_codes  uint8 [B][H][T*CB]         the same bytes, arranged for the
+ *                                       tensor-core fragments: in 16-token
+ *                                       blocks of 16*CB bytes, byte j of token
+ *                                       t sits at (t/16)*16*CB + (k/16)*64 +
+ *                                       ((t/4)%4)*16 + k%16, k = 4*j + t%4
+ *                                       (CB must be a multiple of 4)
  *   k_meta   float [B][H][T][2]         {scale, zero_point} per K vector
  *   v_meta   float [B][H][T][2]         {scale, zero_point} per V vector
  * ====================================================================== */
@@ -137,6 +140,12 @@ int sa_kv_cache_advance(sa_kv_cache *cache, int64_t n);
 int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_view *view);
 /* Copy of the cache configuration. */
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config);
+/* Device-side status of the kernels that used this cache: 0, or bit 0 set when
+ * a bounded wait inside a kernel gave up (the kernel then stopped and its
+ * output is not valid).  Synchronises with the device; `clear` resets it.
+ * The reference has no device-side waits; this reports the safety net that
+ * replaces a hang. */
+int sa_kv_cache_device_status(sa_kv_cache *cache, int32_t *status, int32_t clear);
 
 /* Quantize-on-append: GpuKvCache::append (kv_cache.rs:233-277) fused with
  * CompressedKVCache::write_kv (kv_compression.rs:814-854, kv_qjl_residual and

@@ -26,13 +26,21 @@ struct Layout {
     int d, bits, cb, cap, heads, group;
 };
 
-// Code of element e from a token's packed row (pack_bits order, stride `step`
-// bytes between consecutive bytes of the row: 1 for K, 4 for interleaved V).
-__device__ __forceinline__ uint32_t code_at(const uint8_t *row, int step, int e, int bits, int cb) {
+// Code of element e of a K token row (pack_bits order, contiguous bytes).
+__device__ __forceinline__ uint32_t code_at(const uint8_t *row, int e, int bits, int cb) {
     const int bo = e * bits;
     const int j = bo >> 3, sh = bo & 7;
-    uint32_t w = row[(int64_t)j * step];
-    if (sh + bits > 8 && j + 1 < cb) w |= (uint32_t)row[(int64_t)(j + 1) * step] << 8;
+    uint32_t w = row[j];
+    if (sh + bits > 8 && j + 1 < cb) w |= (uint32_t)row[j + 1] << 8;
+    return (w >> sh) & ((1u << bits) - 1u);
+}
+
+// Code of element e of V token t (bytes placed by v_byte_offset).
+__device__ __forceinline__ uint32_t v_code_at(const uint8_t *vrow, int64_t t, int e, int bits, int cb) {
+    const int bo = e * bits;
+    const int j = bo >> 3, sh = bo & 7;
+    uint32_t w = vrow[v_byte_offset(t, j, cb)];
+    if (sh + bits > 8 && j + 1 < cb) w |= (uint32_t)vrow[v_byte_offset(t, j + 1, cb)] << 8;
     return (w >> sh) & ((1u << bits) - 1u);
 }
 
@@ -146,13 +154,12 @@ __global__ void __launch_bounds__(32 * kWarps) attend_split_kernel(AttendArgs a,
 
     for (int64_t t = t_begin + warp; t < t_end; t += kWarps) {
         const uint8_t *krow = kc + t * a.code_bytes;
-        const uint8_t *vrow = vc + ((t / kVGroup) * a.code_bytes) * kVGroup + (t % kVGroup);
         float ck[EPL], cv[EPL];
 #pragma unroll
         for (int r = 0; r < EPL; r++) {
             const int e = lane * EPL + r;
-            ck[r] = active ? (float)code_at(krow, 1, e, a.bits, a.code_bytes) : 0.0f;
-            cv[r] = active ? (float)code_at(vrow, kVGroup, e, a.bits, a.code_bytes) : 0.0f;
+            ck[r] = active ? (float)code_at(krow, e, a.bits, a.code_bytes) : 0.0f;
+            cv[r] = active ? (float)v_code_at(vc, t, e, a.bits, a.code_bytes) : 0.0f;
         }
         const float kscale = km[t * 2], kzp = km[t * 2 + 1];
         const float vscale = vm[t * 2], vzp = vm[t * 2 + 1];
@@ -448,9 +455,10 @@ extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t pas
         return set_error(SA_ERR_INVALID_ATTRIBUTE, "bits must be 3, 4, or 8");
     if (v.code_bytes != d * v.bits / 8)
         return set_error(SA_ERR_SHAPE_MISMATCH, "gqa_attend_no_alloc: code_bytes %d != head_dim*bits/8", v.code_bytes);
-    if (v.kv_heads <= 0 || v.batch <= 0 || v.capacity <= 0 || v.capacity % kVGroup != 0)
+    if (v.kv_heads <= 0 || v.batch <= 0 || v.capacity <= 0 || v.capacity % kVBlock != 0 || v.code_bytes % 4 != 0)
         return set_error(SA_ERR_SHAPE_MISMATCH,
-                         "gqa_attend_no_alloc: kv_heads/batch must be > 0 and capacity a positive multiple of 4");
+                         "gqa_attend_no_alloc: kv_heads/batch must be > 0, capacity a positive multiple of 16 and "
+                         "code_bytes a multiple of 4");
     if (group < 1 || group > 8)
         return set_error(SA_ERR_UNSUPPORTED, "gqa_attend_no_alloc: group size %d outside 1..8", group);
     if (dtype != SA_DTYPE_FLOAT && dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16)

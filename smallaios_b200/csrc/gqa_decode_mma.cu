@@ -1,43 +1,92 @@
-// Tensor-core decode attention over the PolarQuant cache (one query token,
-// 4/8-bit codes, head_dim 64/128, up to 4 query heads per KV head).
+// Tensor-core decode attention over the PolarQuant cache: one query token per
+// sequence, 4/8-bit codes, head_dim 64/128, up to 4 query heads per KV head.
 //
-// One CTA per (split of the context, KV head, batch row); each warp owns a
-// contiguous token range of the split and runs two phases over it:
+// Two launches per step:
 //
-//  1. scores.  q' = H.S.q/sqrt(n) is written as three signed 8-bit digits
-//     (24-bit fixed point per head, q' ~= sigma * (d0*2^16 + d1*2^8 + d2)),
-//     so q'.c for 16 tokens x 4 heads is one exact int32 contraction:
-//     mma.m16n8k32 u8 (K codes, unpacked in registers) x s8 (digits).  The
-//     score of token t, head h is scale_t*(q'.c) + zp_t*sum(q'), in log2
-//     units, kept in shared memory.
-//  2. values.  With the warp's max R over max(s, s + log2 vscale), each token
-//     gets u = 2^(s + log2 vscale - R) in (0, 1] as a 24-bit fixed-point
-//     number (three unsigned 8-bit digits) and the PV product
-//     sum_t u_t * c_t is again an exact int32 mma.m16n8k32 u8 x u8, with the
-//     V codes of 4 consecutive tokens coming from one 32-bit word of the
-//     4-token interleaved layout.  No online rescaling is needed inside a
-//     warp because R is known before phase 2 starts.
+//  decode_prep_kernel, one CTA per (KV head, batch row):
+//    - quantize-on-append of the new token's K and V (same bit-exact encoder
+//      as sa_kv_append), when the operator appends;
+//    - RoPE + rotation of the G query heads, q' = H.S.q/sqrt(n), written as
+//      three signed 8-bit digits of a 24-bit fixed-point number per head:
+//      q' ~= sigma * (d0*2^16 + d1*2^8 + d2), |d| <= 127, stored already
+//      arranged as each lane's mma B-fragment words.
 //
-// The warps of a CTA merge their (R, L, Z, acc) in shared memory; splits are
-// merged by attend_combine_kernel (or the CTA writes the output directly when
-// there is one split), which also applies the inverse rotation.
-#include "sa_common.cuh"
-#include "sa_internal.h"
+//  decode_persistent_kernel, two CTAs per SM, each looping over work items
+//  (batch row, KV head, split of the context).  Warp 8 is the producer: one
+//  thread streams every item's K then V chunks (256 tokens each) into a ring
+//  of shared-memory slots with 1-D bulk copies (cp.async.bulk + mbarrier, no
+//  multicast), running ahead across items as far as free slots allow.
+//  Warps 0-7 consume:
+//    phase 1 (K): K codes are unpacked to u8 in registers and contracted with
+//      the q' digits by mma.m16n8k32 u8 x s8 -> exact int32 dots q'.c; the
+//      score s = scale_t*sigma*(q'.c) + zp_t*sum(q') (log2 units) goes to
+//      shared memory.
+//    phase 2 (V): with the item's reference R = max over max(s, s + log2
+//      vscale), every token gets u = 2^(s + log2 vscale - R) in (0, 1] as a
+//      24-bit fixed-point number (three unsigned digits) and sum_t u_t * c_t
+//      is an exact int32 mma.m16n8k32 u8 x u8 whose B fragments are single
+//      32-bit words of the 4-token interleaved V layout.  L = sum u/vscale and
+//      Z = sum u*vzp/vscale are float sums.  No rescaling: R is known before
+//      phase 2 starts.
+//    The last CTA to finish a (row, head) merges its splits (counter per
+//    (row, head)), normalises, applies the inverse rotation and stores.
+//  Every mbarrier wait is bounded; a wait that gives up sets the cache's
+//  device status, the CTA stops writing and drains its own copies.
+#include "sa_append.cuh"
 
 namespace sa {
 
-// defined in gqa_attend.cu
-void choose_splits(const AttendArgs &a, int64_t total, int *n_splits, int *tps);
 int launch_gqa_combine(const AttendArgs &a, int n_splits, cudaStream_t stream);
 
 namespace {
 
-constexpr int kNW = 8;           // warps per CTA
-constexpr int kTPW = 256;        // max tokens per warp (phase-1 score buffer)
-constexpr int kPRow = 48;        // bytes per row of the P-digit tile (bank-conflict free)
+constexpr int kNW = 8;            // warps per decode CTA
+constexpr int kTileW = 12;        // u32 words per row of a warp's P-digit tile
 constexpr float kLog2eF = 1.4426950408889634f;
-constexpr float kQMax = 8355711.0f;      // 127*65536 + 127*256 + 127
-constexpr float kUMax = 16777215.0f;     // 2^24 - 1
+constexpr float kQMax = 8355711.0f;   // 127*65536 + 127*256 + 127
+constexpr float kUMax = 16777215.0f;  // 2^24 - 1
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+// ---- PTX helpers ------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kWaitLimit; ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, size a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -57,484 +106,635 @@ __device__ __forceinline__ void mma_u8u8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 ldg_nc(const void *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
-// The SEGW 32-bit words of one quad's share of a K row (8, 16 or 32 bytes).
-template <int SEGW>
-__device__ __forceinline__ void load_seg(const uint8_t *p, uint32_t (&w)[SEGW]) {
-    if (SEGW == 2) {
-        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
-    } else {
-#pragma unroll
-        for (int v = 0; v < SEGW / 4; v++) {
-            const uint4 x = ldg_nc(p + 16 * v);
-            w[4 * v] = x.x;
-            w[4 * v + 1] = x.y;
-            w[4 * v + 2] = x.z;
-            w[4 * v + 3] = x.w;
-        }
-    }
-}
-
-__device__ __forceinline__ float2 ldg_f2(const float *p) {
-    return __ldg(reinterpret_cast<const float2 *>(p));
-}
-
-// Physical dimension of logical k (0..31) in K-chunk c for quad q: the byte
-// layout of one token's codes, as consumed by the A fragment.
+// ---- fragment layouts ---------------------------------------------------------
+// Dimension carried by logical k (0..31) of K-chunk c for quad q in the QK
+// A fragment built from one token's packed codes.
 template <int BITS, int D>
 __device__ __forceinline__ int k_dim(int c, int q, int k) {
-    constexpr int KB = D * BITS / 8;  // code bytes per token
-    constexpr int SEG = KB / 4;       // bytes owned by one quad
-    const int hi = k >> 4, e = k & 3;  // k = 4q+e (hi=0) or 16+4q+e (hi=1)
+    constexpr int KB = D * BITS / 8;
+    constexpr int SEG = KB / 4;
+    const int hi = k >> 4, e = k & 3;
     if (BITS == 4) return 2 * (q * SEG + 4 * c + e) + hi;
     return q * SEG + 8 * c + 4 * hi + e;
 }
 
-// Word index (within a 4-token group) that gives n-tile `nt`, column `col`
-// of the PV B fragment, and the dimension it carries.
+// Dimension carried by column `col` of PV n-tile `nt` (B fragment from the
+// 4-token interleaved V words; word index 32*(i/4) + 4*col + i%4).
 template <int BITS, int D>
 __device__ __forceinline__ int v_dim(int nt, int col) {
     if (BITS == 4) {
         const int i = nt >> 1, hi = nt & 1;
-        const int w = 32 * (i >> 2) + 4 * col + (i & 3);
-        return 2 * w + hi;
+        return 2 * (32 * (i >> 2) + 4 * col + (i & 3)) + hi;
     }
     return 32 * (nt >> 2) + 4 * col + (nt & 3);
 }
 
+// Inverse of v_dim: n-tile and column of dimension `dim`.
+template <int BITS, int D>
+__device__ __forceinline__ void v_inv(int dim, int &nt, int &col) {
+    if (BITS == 4) {
+        const int w = dim >> 1, hi = dim & 1;
+        col = (w >> 2) & 7;
+        nt = 2 * (4 * (w >> 5) + (w & 3)) + hi;
+    } else {
+        col = (dim >> 2) & 7;
+        nt = 4 * (dim >> 5) + (dim & 3);
+    }
+}
+
+template <int BITS, int D>
+struct Geo {
+    static constexpr int NCH = D / 32;  // QK k-chunks of 32 dimensions
+    static constexpr int QW = NCH * 4;  // q-digit words per lane
+};
+
+// ---- prep: append the new token + q digits --------------------------------
 template <typename T, int BITS, int D>
-__global__ void __launch_bounds__(kNW * 32, 2)
-    decode_mma_kernel(AttendArgs a, int n_splits, int tokens_per_split, int tokens_per_warp) {
-    constexpr int KB = D * BITS / 8;
-    constexpr int SEGW = KB / 16;         // 32-bit words per quad per K row
-    constexpr int NCH = D / 32;           // K chunks of 32 dims
-    constexpr int NTV = D / 8;            // PV n-tiles
-    constexpr int VW = (BITS == 4) ? NTV / 2 : NTV;  // V words per thread per 4-token group
-    constexpr int VV = VW / 4;            // uint4 loads per thread per 4-token group
+__global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendArgs ap, int do_append,
+                                                          uint32_t *qfrag, float *qscal) {
+    using GG = Geo<BITS, D>;
     constexpr int EPL = D / 32;
-
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    float *s_q = reinterpret_cast<float *>(smem_raw);            // [4][D]
-    float *s_qsum = s_q + 4 * D;                                  // [4]
-    float *s_sigma = s_qsum + 4;                                  // [4]
-    float *s_R = s_sigma + 4;                                     // [kNW][4]
-    float *s_sc = s_R + kNW * 4;                                  // [kNW][kTPW][4]
-    float *s_lv = s_sc + kNW * kTPW * 4;                          // [kNW][kTPW]
-    unsigned char *s_p = reinterpret_cast<unsigned char *>(s_lv + kNW * kTPW);  // [kNW][16][kPRow]
-    // merge area (reuses s_sc after phase 2): [kNW][4][D] acc + [kNW][4][3] R,L,Z
-    float *m_acc = s_sc;
-    float *m_rlz = s_sc + kNW * 4 * D;
-
+    __shared__ float s_q[4][D];
+    __shared__ float s_sig[4], s_qs[4];
+    __shared__ uint8_t s_codes[2][256];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r = lane >> 2, q = lane & 3;
-    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int h = blockIdx.x, b = blockIdx.y;
     const int G = a.group;
-    const int64_t qpos = a.pos0;  // single query token
-    const int64_t total = qpos + 1;
+    const int q0w = do_append ? 2 : 0;
     const float *sg = a.signs + (int64_t)h * D;
-    const int qheads = a.heads * G;
-
-    // ---- prologue: RoPE + rotation + digit scale of the G query heads ----
-    if (warp < G) {
-        const int g = warp;
+    if (do_append && warp < 2) {
+        encode_append_vector<T, EPL>(ap, b, 0, h, warp, lane, s_codes[warp]);
+    } else if (warp >= q0w && warp - q0w < G) {
+        const int g = warp - q0w;
+        const int qheads = a.heads * G;
         const T *src = static_cast<const T *>(a.query) + ((int64_t)b * qheads + h * G + g) * D;
         float x[EPL];
 #pragma unroll
-        for (int rr = 0; rr < EPL; rr++) x[rr] = ld_f32(src + lane * EPL + rr);
-        if (a.do_rotary) {
-            const int half = D / 2;
-            const float *cr = a.cos_cache + qpos * half;
-            const float *sr = a.sin_cache + qpos * half;
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) {
-                const int e = lane * EPL + rr;
-                int pair, partner;
-                bool first;
-                if (a.interleaved) {
-                    pair = e >> 1;
-                    first = (e & 1) == 0;
-                    partner = first ? e + 1 : e - 1;
-                } else {
-                    first = e < half;
-                    pair = first ? e : e - half;
-                    partner = first ? e + half : e - half;
-                }
-                const float c = cr[pair], sn = sr[pair];
-                const float xo = ld_f32(src + partner);
-                x[rr] = first ? __fsub_rn(__fmul_rn(c, x[rr]), __fmul_rn(sn, xo))
-                              : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x[rr]));
-            }
+        for (int r = 0; r < EPL; r++) {
+            const int e = lane * EPL + r;
+            x[r] = ld_f32(src + e);
+            if (a.do_rotary) x[r] = rope_element(src, x[r], e, D, a.pos0, a.cos_cache, a.sin_cache, a.interleaved);
+            x[r] *= sg[e];
         }
-#pragma unroll
-        for (int rr = 0; rr < EPL; rr++) x[rr] *= sg[lane * EPL + rr];
         warp_wht_butterfly<EPL>(x, lane, D);
         float sum = 0.0f, mabs = 0.0f;
 #pragma unroll
-        for (int rr = 0; rr < EPL; rr++) {
-            x[rr] *= a.wht_scale;
-            s_q[g * D + lane * EPL + rr] = x[rr];
-            sum += x[rr];
-            mabs = fmaxf(mabs, fabsf(x[rr]));
+        for (int r = 0; r < EPL; r++) {
+            x[r] *= a.wht_scale;
+            s_q[g][lane * EPL + r] = x[r];
+            sum += x[r];
+            mabs = fmaxf(mabs, fabsf(x[r]));
         }
         sum = warp_sum(sum);
         mabs = warp_max(mabs);
         if (lane == 0) {
-            s_qsum[g] = sum;
-            s_sigma[g] = mabs > 0.0f ? mabs / kQMax : 1.0f;
+            s_qs[g] = sum;
+            s_sig[g] = mabs > 0.0f ? mabs / kQMax : 1.0f;
         }
     }
     __syncthreads();
-
-    // Q-digit B fragments: n-tile 0 column 2j -> (head j, digit 0), 2j+1 -> (head j, digit 1);
-    // n-tile 1 column 2j -> (head j, digit 2), 2j+1 -> zero.  Column = r here.
-    uint32_t bq[NCH][2][2];
-    {
-        const int hh = r >> 1;
-        const bool has_head = hh < G;
-        const float inv_sigma = has_head ? 1.0f / s_sigma[hh] : 0.0f;
+    if (warp != 0) return;
+    // lane (r, q): B fragment words for k-chunk c, n-tile t, half.  n-tile 0
+    // column 2j -> (head j, digit 0), 2j+1 -> (head j, digit 1); n-tile 1
+    // column 2j -> (head j, digit 2), 2j+1 -> zero.  Column = r.
+    const int r = lane >> 2, q = lane & 3;
+    const int hh = r >> 1;
+    const bool has_head = hh < G;
+    const float inv_sigma = has_head ? 1.0f / s_sig[hh] : 0.0f;
+    const int64_t bh = (int64_t)b * a.heads + h;
+    uint32_t *dst = qfrag + (bh * 32 + lane) * GG::QW;
 #pragma unroll
-        for (int c = 0; c < NCH; c++) {
+    for (int c = 0; c < GG::NCH; c++) {
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                uint32_t w0 = 0, w1 = 0;  // n-tile 0, n-tile 1
+        for (int half = 0; half < 2; half++) {
+            uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int k = 16 * half + 4 * q + e;
-                    int qi = 0;
-                    if (has_head) {
-                        // |q'/sigma| <= kQMax up to rounding; clamp so the top digit stays in int8
-                        qi = __float2int_rn(s_q[hh * D + k_dim<BITS, D>(c, q, k)] * inv_sigma);
-                        qi = min(max(qi, -(int)kQMax), (int)kQMax);
-                    }
-                    // balanced base-256 digits: qi = d0*65536 + d1*256 + d2, each in [-127, 127]
-                    const int d2 = (int)(int8_t)(qi & 0xff);
-                    const int rest = (qi - d2) >> 8;
-                    const int d1 = (int)(int8_t)(rest & 0xff);
-                    const int d0 = (rest - d1) >> 8;
-                    const int t0dig = (r & 1) ? d1 : d0;
-                    const int t1dig = (r & 1) ? 0 : d2;
-                    w0 |= ((uint32_t)(t0dig & 0xff)) << (8 * e);
-                    w1 |= ((uint32_t)(t1dig & 0xff)) << (8 * e);
+            for (int e = 0; e < 4; e++) {
+                const int k = 16 * half + 4 * q + e;
+                int qi = 0;
+                if (has_head) {
+                    qi = __float2int_rn(s_q[hh][k_dim<BITS, D>(c, q, k)] * inv_sigma);
+                    qi = min(max(qi, -(int)kQMax), (int)kQMax);  // keep the top digit within int8
                 }
-                bq[c][0][half] = w0;
-                bq[c][1][half] = w1;
+                const int d2 = (int)(int8_t)(qi & 0xff);
+                const int rest = (qi - d2) >> 8;
+                const int d1 = (int)(int8_t)(rest & 0xff);
+                const int d0 = (rest - d1) >> 8;
+                w0 |= ((uint32_t)(((r & 1) ? d1 : d0) & 0xff)) << (8 * e);
+                w1 |= ((uint32_t)(((r & 1) ? 0 : d2) & 0xff)) << (8 * e);
             }
-        }
-    }
-    const bool my_head = q < G;
-    const float my_sigma = my_head ? s_sigma[q] : 0.0f;
-    const float my_qsum = my_head ? s_qsum[q] : 0.0f;
-    const float sl2 = a.scale * kLog2eF;
-
-    const int64_t hrow = (int64_t)b * a.heads + h;
-    const uint8_t *kc = a.k_codes + hrow * (int64_t)a.capacity * KB;
-    const uint8_t *vc = a.v_codes + hrow * (int64_t)a.capacity * KB;
-    const float *km = a.k_meta + hrow * (int64_t)a.capacity * 2;
-    const float *vm = a.v_meta + hrow * (int64_t)a.capacity * 2;
-
-    int64_t s_begin = (int64_t)split * tokens_per_split;
-    int64_t s_end = s_begin + tokens_per_split;
-    if (s_end > total) s_end = total;
-    const int64_t tw0 = s_begin + (int64_t)warp * tokens_per_warp;
-    int64_t tw1 = tw0 + tokens_per_warp;
-    if (tw1 > s_end) tw1 = s_end;
-
-    float *sc = s_sc + warp * kTPW * 4;
-    float *lvb = s_lv + warp * kTPW;
-
-    // ---- phase 1: scores ----
-    float rmax = -INFINITY;
-    for (int64_t t0 = tw0; t0 < tw1; t0 += 64) {
-        uint32_t kr[4][2][SEGW];
-        float2 kmt[4][2];
-        float vsc[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-#pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                const int64_t t = t0 + 16 * i + r + 8 * hf;
-                if (t < tw1) {
-                    load_seg<SEGW>(kc + t * KB + q * (KB / 4), kr[i][hf]);
-                    kmt[i][hf] = ldg_f2(km + 2 * t);
-                    vsc[i][hf] = __ldg(vm + 2 * t);
-                } else {
-#pragma unroll
-                    for (int w = 0; w < SEGW; w++) kr[i][hf][w] = 0u;
-                    kmt[i][hf] = make_float2(0.0f, 0.0f);
-                    vsc[i][hf] = 1.0f;
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            if (t0 + 16 * i >= tw1) break;
-            int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-            const uint32_t *w0 = kr[i][0];
-            const uint32_t *w1 = kr[i][1];
-#pragma unroll
-            for (int c = 0; c < NCH; c++) {
-                uint32_t a0, a1, a2, a3;
-                if (BITS == 4) {
-                    a0 = w0[c] & 0x0F0F0F0Fu;
-                    a1 = w1[c] & 0x0F0F0F0Fu;
-                    a2 = (w0[c] >> 4) & 0x0F0F0F0Fu;
-                    a3 = (w1[c] >> 4) & 0x0F0F0F0Fu;
-                } else {
-                    a0 = w0[2 * c];
-                    a1 = w1[2 * c];
-                    a2 = w0[2 * c + 1];
-                    a3 = w1[2 * c + 1];
-                }
-                mma_u8s8(acc[0], a0, a1, a2, a3, bq[c][0][0], bq[c][0][1]);
-                mma_u8s8(acc[1], a0, a1, a2, a3, bq[c][1][0], bq[c][1][1]);
-            }
-#pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                const int64_t t = t0 + 16 * i + r + 8 * hf;
-                const float dot =
-                    fmaf((float)acc[0][2 * hf], 65536.0f, fmaf((float)acc[0][2 * hf + 1], 256.0f, (float)acc[1][2 * hf])) *
-                    my_sigma;
-                float s = (kmt[i][hf].x * dot + kmt[i][hf].y * my_qsum) * sl2;
-                const float lv = __log2f(vsc[i][hf]);
-                const bool valid = t < tw1;
-                if (!valid || !my_head) s = -INFINITY;
-                const int tl = (int)(t - tw0);
-                if (valid) {
-                    if (my_head) sc[tl * 4 + q] = s;
-                    if (q == 0) lvb[tl] = lv;
-                    rmax = fmaxf(rmax, fmaxf(s, s + lv));
-                }
-            }
-        }
-    }
-    // warp max over the 8 token rows sharing a head (lanes with equal q)
-    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 4));
-    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 8));
-    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 16));
-    if (lane < 4) s_R[warp * 4 + lane] = rmax;
-    __syncwarp();
-
-    // ---- phase 2: values ----
-    float Rh[4];
-#pragma unroll
-    for (int hh = 0; hh < 4; hh++) Rh[hh] = s_R[warp * 4 + hh];
-    unsigned char *pb = s_p + warp * 16 * kPRow;
-    // rows 12..15 of the P tile stay zero
-    reinterpret_cast<uint32_t *>(pb + (12 + (lane >> 3)) * kPRow)[lane & 7] = 0u;
-    int pacc[NTV][4];
-#pragma unroll
-    for (int nt = 0; nt < NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
-    float Lp[4] = {0.f, 0.f, 0.f, 0.f}, Zp[4] = {0.f, 0.f, 0.f, 0.f};
-    const int64_t ngroups = a.capacity / kVGroup;
-
-    for (int64_t t0 = tw0; t0 < tw1; t0 += 32) {
-        // V codes of token groups (t0/4 + q) and (t0/4 + 4 + q)
-        uint4 vw[2][VV];
-#pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-            const int64_t grp = t0 / kVGroup + 4 * hf + q;
-            const bool ok = grp * kVGroup < tw1 && grp < ngroups;
-            const uint8_t *gbase = vc + grp * (int64_t)(KB * kVGroup);
-#pragma unroll
-            for (int v = 0; v < VV; v++)
-                vw[hf][v] = ok ? ldg_nc(gbase + 128 * v + 16 * r) : make_uint4(0, 0, 0, 0);
-        }
-        // P digits: lane = token
-        {
-            const int64_t t = t0 + lane;
-            const bool valid = t < tw1;
-            const int tl = (int)(t - tw0);
-            float4 s4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-            float lv = 0.0f, vz = 0.0f;
-            if (valid) {
-                s4 = *reinterpret_cast<const float4 *>(sc + tl * 4);
-                lv = lvb[tl];
-                vz = __ldg(vm + 2 * t + 1);
-            }
-            const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int hh = 0; hh < 4; hh++) {
-                uint32_t U = 0;
-                if (hh < G && valid) {
-                    const float p = exp2f(sv[hh] - Rh[hh]);
-                    const float u = exp2f(sv[hh] + lv - Rh[hh]);
-                    Lp[hh] += p;
-                    Zp[hh] = fmaf(p, vz, Zp[hh]);
-                    U = __float2uint_rn(fminf(u, 1.0f) * kUMax);
-                }
-                pb[(0 + hh) * kPRow + lane] = (unsigned char)(U >> 16);
-                pb[(4 + hh) * kPRow + lane] = (unsigned char)((U >> 8) & 0xffu);
-                pb[(8 + hh) * kPRow + lane] = (unsigned char)(U & 0xffu);
-            }
-        }
-        __syncwarp();
-        const uint32_t pa0 = *reinterpret_cast<const uint32_t *>(pb + r * kPRow + 4 * q);
-        const uint32_t pa1 = *reinterpret_cast<const uint32_t *>(pb + (r + 8) * kPRow + 4 * q);
-        const uint32_t pa2 = *reinterpret_cast<const uint32_t *>(pb + r * kPRow + 16 + 4 * q);
-        const uint32_t pa3 = *reinterpret_cast<const uint32_t *>(pb + (r + 8) * kPRow + 16 + 4 * q);
-        __syncwarp();
-#pragma unroll
-        for (int v = 0; v < VV; v++) {
-            const uint32_t x0[4] = {vw[0][v].x, vw[0][v].y, vw[0][v].z, vw[0][v].w};
-            const uint32_t x1[4] = {vw[1][v].x, vw[1][v].y, vw[1][v].z, vw[1][v].w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int i = 4 * v + j;  // word index within the thread's VW words
-                if (BITS == 4) {
-                    mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, x0[j] & 0x0F0F0F0Fu, x1[j] & 0x0F0F0F0Fu);
-                    mma_u8u8(pacc[2 * i + 1], pa0, pa1, pa2, pa3, (x0[j] >> 4) & 0x0F0F0F0Fu,
-                             (x1[j] >> 4) & 0x0F0F0F0Fu);
-                } else {
-                    mma_u8u8(pacc[i], pa0, pa1, pa2, pa3, x0[j], x1[j]);
-                }
-            }
-        }
-    }
-
-    // ---- warp partial -> shared memory ----
-#pragma unroll
-    for (int hh = 0; hh < 4; hh++) {
-        Lp[hh] = warp_sum(Lp[hh]);
-        Zp[hh] = warp_sum(Zp[hh]);
-    }
-    __syncthreads();  // every warp is done with s_sc before it becomes the merge area
-    float *macc = m_acc + warp * 4 * D;
-    // rows: r<4 -> (digit 0, head r) and (digit 2, head r); r>=4 -> (digit 1, head r-4)
-#pragma unroll
-    for (int nt = 0; nt < NTV; nt++) {
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const int mid = __shfl_down_sync(0xffffffffu, pacc[nt][cc], 16);
-            if (r < 4 && r < G) {
-                const float v = fmaf((float)pacc[nt][cc], 65536.0f, fmaf((float)mid, 256.0f, (float)pacc[nt][2 + cc]));
-                macc[r * D + v_dim<BITS, D>(nt, 2 * q + cc)] = v * (1.0f / kUMax);
-            }
+            dst[c * 4 + 0 * 2 + half] = w0;  // n-tile 0
+            dst[c * 4 + 1 * 2 + half] = w1;  // n-tile 1
         }
     }
     if (lane < 4) {
-        m_rlz[(warp * 4 + lane) * 3 + 0] = Rh[lane];
-        m_rlz[(warp * 4 + lane) * 3 + 1] = Lp[lane];
-        m_rlz[(warp * 4 + lane) * 3 + 2] = Zp[lane];
+        const float sl2 = a.scale * kLog2eF;
+        qscal[bh * 8 + lane] = lane < G ? s_sig[lane] * sl2 : 0.0f;
+        qscal[bh * 8 + 4 + lane] = lane < G ? s_qs[lane] * sl2 : 0.0f;
     }
-    __syncthreads();
+}
 
-    // ---- merge warps; warp g finishes head g ----
-    if (warp < G) {
-        const int g = warp;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kNW; w++) M = fmaxf(M, m_rlz[(w * 4 + g) * 3]);
-        float wt[kNW], L = 0.0f, Z = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kNW; w++) {
-            const float Rw = m_rlz[(w * 4 + g) * 3];
-            wt[w] = (Rw == -INFINITY) ? 0.0f : exp2f(Rw - M);
-            L = fmaf(wt[w], m_rlz[(w * 4 + g) * 3 + 1], L);
-            Z = fmaf(wt[w], m_rlz[(w * 4 + g) * 3 + 2], Z);
-        }
-        float x[EPL];
-#pragma unroll
-        for (int rr = 0; rr < EPL; rr++) {
-            float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kNW; w++) s = fmaf(wt[w], m_acc[(w * 4 + g) * D + lane * EPL + rr], s);
-            x[rr] = s;
-        }
-        if (n_splits == 1) {
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
-            warp_wht_butterfly<EPL>(x, lane, D);
-            T *dst = static_cast<T *>(a.out) + ((int64_t)b * qheads + h * G + g) * D;
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + lane * EPL + rr, x[rr] * a.wht_scale * sg[lane * EPL + rr]);
-        } else {
-            float *ws = a.workspace + ((((int64_t)b * a.heads + h) * n_splits + split) * G + g) * (D + 4);
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) ws[lane * EPL + rr] = x[rr];
-            if (lane == 0) {
-                ws[D] = M;
-                ws[D + 1] = L;
-                ws[D + 2] = Z;
+// ---- decode: independent warp streams -------------------------------------------
+// Each warp owns a contiguous range of up to kTPW tokens of an item and streams
+// it through its own two shared-memory slots (K chunks, then V chunks), so no
+// warp ever waits for another inside an item.
+constexpr int kTPW = 128;           // tokens per warp per item
+constexpr int kScStride = kTPW + 8;  // floats per head row of a warp's score buffer (bank offset)
+
+template <int BITS, int D>
+struct WGeo {
+    static constexpr int KB = D * BITS / 8;             // code bytes per token
+    static constexpr int CT = (KB > 64) ? 32 : 64;       // tokens per chunk
+    static constexpr int SLOT = CT * (KB + 16);          // K chunk: codes + K meta + V meta (a V chunk is smaller)
+    static constexpr int SEGW = KB / 16;                 // K words per quad per row
+    static constexpr int NCH = D / 32;                   // QK k-chunks
+    static constexpr int NTV = D / 8;                    // PV n-tiles
+    static constexpr int VV = ((BITS == 4) ? NTV / 2 : NTV) / 4;  // 16-byte V loads per 16-token block
+    static constexpr int QW = NCH * 4;                   // q-digit words per lane
+    static constexpr int SCW = 4 * kScStride;            // floats of a warp's score buffer / merge area
+    static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 1024;
+    static_assert(4 * D <= SCW, "merge area must fit the score buffer");
+};
+
+struct ItemGeo {
+    int64_t u;  // b * heads + h
+    int b, h, split;
+    int64_t s_begin;
+    int n_tok;
+};
+
+__device__ __forceinline__ ItemGeo item_geo(const AttendArgs &a, int item, int n_splits, int tps) {
+    ItemGeo g;
+    g.u = item / n_splits;
+    g.split = item % n_splits;
+    g.b = (int)(g.u / a.heads);
+    g.h = (int)(g.u % a.heads);
+    g.s_begin = (int64_t)g.split * tps;
+    const int64_t total = a.pos0 + 1;
+    const int64_t e = g.s_begin + tps < total ? g.s_begin + tps : total;
+    g.n_tok = (int)(e - g.s_begin);
+    return g;
+}
+
+// Tokens of warp `warp` in an item (0 if the item ends before its range).
+__device__ __forceinline__ int warp_tokens(int n_tok, int warp, int tpw) {
+    const int n = n_tok - warp * tpw;
+    return n <= 0 ? 0 : (n < tpw ? n : tpw);
+}
+
+// The chunk schedule of one warp over the CTA's items: for every item with a
+// non-empty range, its K chunks then its V chunks.  Lane 0 keeps the cursor
+// of the next chunk to issue, two chunks ahead of consumption.
+template <int BITS, int D>
+struct WarpStream {
+    using GG = WGeo<BITS, D>;
+    int item, c, nk, n;
+    int64_t u, t0;
+
+    __device__ __forceinline__ void seek(const AttendArgs &a, int n_items, int n_splits, int tps, int tpw, int warp) {
+        for (; item < n_items; item += gridDim.x) {
+            const ItemGeo g = item_geo(a, item, n_splits, tps);
+            n = warp_tokens(g.n_tok, warp, tpw);
+            if (n > 0) {
+                u = g.u;
+                t0 = g.s_begin + (int64_t)warp * tpw;
+                nk = (n + GG::CT - 1) / GG::CT;
+                c = 0;
+                return;
             }
         }
     }
-}
 
-size_t decode_smem_bytes(int d) {
-    return sizeof(float) * ((size_t)4 * d + 4 + 4 + kNW * 4 + (size_t)kNW * kTPW * 4 + (size_t)kNW * kTPW) +
-           (size_t)kNW * 16 * kPRow;
+    __device__ __forceinline__ void issue(const AttendArgs &a, unsigned char *dst, uint64_t *bar) const {
+        constexpr int KB = GG::KB, CT = GG::CT;
+        const int64_t cap = a.capacity;
+        const int cc = c < nk ? c : c - nk;
+        const int cnt = n - cc * CT < CT ? n - cc * CT : CT;
+        const int mcnt = (cnt + 1) & ~1;  // meta rows rounded to even: 16-byte copies
+        const int64_t g0 = t0 + cc * CT;  // multiple of CT (>= 32)
+        const uint32_t mb = (uint32_t)(mcnt * 8);
+        if (c < nk) {  // K chunk: codes, K meta, V meta
+            const uint32_t cb = (uint32_t)(cnt * KB);
+            mbar_expect_tx(bar, cb + 2 * mb);
+            bulk_g2s(dst, a.k_codes + (u * cap + g0) * KB, cb, bar);
+            bulk_g2s(dst + CT * KB, a.k_meta + (u * cap + g0) * 2, mb, bar);
+            bulk_g2s(dst + CT * KB + CT * 8, a.v_meta + (u * cap + g0) * 2, mb, bar);
+        } else {  // V chunk: whole 16-token blocks of codes, V meta
+            const uint32_t vb = (uint32_t)(((cnt + kVBlock - 1) / kVBlock) * KB * kVBlock);
+            mbar_expect_tx(bar, vb + mb);
+            bulk_g2s(dst, a.v_codes + (u * cap + g0) * KB, vb, bar);
+            bulk_g2s(dst + CT * KB, a.v_meta + (u * cap + g0) * 2, mb, bar);
+        }
+    }
+
+    __device__ __forceinline__ void advance(const AttendArgs &a, int n_items, int n_splits, int tps, int tpw,
+                                            int warp) {
+        if (++c == 2 * nk) {
+            item += gridDim.x;
+            seek(a, n_items, n_splits, tps, tpw, warp);
+        }
+    }
+};
+
+template <typename T, int BITS, int D>
+__global__ void __launch_bounds__(kNW * 32, 2)
+    decode_stream_kernel(AttendArgs a, int n_splits, int tps, int tpw, int n_items, const uint32_t *__restrict__ qfrag,
+                         const float *__restrict__ qscal) {
+    using GG = WGeo<BITS, D>;
+    constexpr int KB = GG::KB, CT = GG::CT;
+    constexpr int EPL = D / 32;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned char *slots = smem + warp * 2 * GG::SLOT;                              // this warp's 2 slots
+    float *scw_all = reinterpret_cast<float *>(smem + kNW * 2 * GG::SLOT);          // [kNW][4][kScStride]
+    float *scw = scw_all + warp * GG::SCW;                                          // s' scores, then merge area
+    uint32_t *tile = reinterpret_cast<uint32_t *>(scw_all + kNW * GG::SCW) + warp * 12 * kTileW;
+    float *rlz = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(scw_all + kNW * GG::SCW) + kNW * 12 * kTileW);
+    int *s_flag = reinterpret_cast<int *>(rlz + kNW * 4 * 3);                       // [1] failure
+    uint64_t *bars = reinterpret_cast<uint64_t *>(rlz + 128);                      // [kNW][2]
+    uint64_t *mybar = bars + 2 * warp;
+
+    const int G = a.group;
+    const int r = lane >> 2, q = lane & 3;
+    const int ph = lane >> 3, tq = lane & 7;  // P-digit role: head ph, token quad tq of a 32-token step
+    const bool my_head = q < G;
+
+    if (tid == 0) {
+        for (int i = 0; i < 2 * kNW; i++) mbar_init(bars + i, 1);
+        s_flag[0] = 0;
+        s_flag[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+
+    WarpStream<BITS, D> ws;
+    if (lane == 0) {
+        ws.item = blockIdx.x;
+        ws.seek(a, n_items, n_splits, tps, tpw, warp);
+        for (int k = 0; k < 2 && ws.item < n_items; k++) {
+            ws.issue(a, slots + k * GG::SLOT, mybar + k);
+            ws.advance(a, n_items, n_splits, tps, tpw, warp);
+        }
+    }
+
+    int j = 0;  // chunks consumed by this warp
+    bool failed = false;
+    // wait for chunk j; afterwards lane 0 refills its slot with the chunk two ahead
+    auto wait_chunk = [&](int jj) {
+        if (!failed && !mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1))) {
+            failed = true;
+            atomicOr(a.dev_status, 1);
+            s_flag[1] = 1;
+        }
+    };
+    auto release_chunk = [&](int jj) {
+        __syncwarp();
+        if (lane == 0 && ws.item < n_items) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            ws.issue(a, slots + (jj & 1) * GG::SLOT, mybar + (jj & 1));
+            ws.advance(a, n_items, n_splits, tps, tpw, warp);
+        }
+    };
+
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const ItemGeo ig = item_geo(a, item, n_splits, tps);
+        const int n_w = warp_tokens(ig.n_tok, warp, tpw);
+        const int nk = (n_w + CT - 1) / CT;
+        float Rp = -INFINITY, Lp = 0.0f, Zp = 0.0f;
+        int pacc[GG::NTV][4];
+#pragma unroll
+        for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
+
+        if (n_w > 0) {
+            uint32_t bq[GG::QW];
+            {
+                const uint4 *src = reinterpret_cast<const uint4 *>(qfrag + (ig.u * 32 + lane) * GG::QW);
+#pragma unroll
+                for (int v = 0; v < GG::QW / 4; v++) {
+                    const uint4 x = src[v];
+                    bq[4 * v] = x.x;
+                    bq[4 * v + 1] = x.y;
+                    bq[4 * v + 2] = x.z;
+                    bq[4 * v + 3] = x.w;
+                }
+            }
+            const float c1 = qscal[ig.u * 8 + q], c2 = qscal[ig.u * 8 + 4 + q];
+
+            // ---------------- phase 1: scores s' = s + log2(vscale) ----------------
+            float rmax = -INFINITY;
+            for (int cc = 0; cc < nk; cc++, j++) {
+                wait_chunk(j);
+                const unsigned char *st = slots + (j & 1) * GG::SLOT;
+                const float *kms = reinterpret_cast<const float *>(st + CT * KB);
+                const float *vms = kms + 2 * CT;
+#pragma unroll
+                for (int mt = 0; mt < CT / 16; mt++) {
+                    uint32_t w[2][GG::SEGW];
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        const unsigned char *p = st + (16 * mt + r + 8 * hf) * KB + q * (KB / 4);
+                        if constexpr (GG::SEGW == 2) {
+                            const uint2 x = *reinterpret_cast<const uint2 *>(p);
+                            w[hf][0] = x.x;
+                            w[hf][1] = x.y;
+                        } else {
+#pragma unroll
+                            for (int v = 0; v < GG::SEGW / 4; v++) {
+                                const uint4 x = reinterpret_cast<const uint4 *>(p)[v];
+                                w[hf][4 * v] = x.x;
+                                w[hf][4 * v + 1] = x.y;
+                                w[hf][4 * v + 2] = x.z;
+                                w[hf][4 * v + 3] = x.w;
+                            }
+                        }
+                    }
+                    int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+                    for (int k = 0; k < GG::NCH; k++) {
+                        uint32_t a0, a1, a2, a3;
+                        if constexpr (BITS == 4) {
+                            a0 = w[0][k] & 0x0F0F0F0Fu;
+                            a1 = w[1][k] & 0x0F0F0F0Fu;
+                            a2 = (w[0][k] >> 4) & 0x0F0F0F0Fu;
+                            a3 = (w[1][k] >> 4) & 0x0F0F0F0Fu;
+                        } else {
+                            a0 = w[0][2 * k];
+                            a1 = w[1][2 * k];
+                            a2 = w[0][2 * k + 1];
+                            a3 = w[1][2 * k + 1];
+                        }
+                        mma_u8s8(acc[0], a0, a1, a2, a3, bq[k * 4 + 0], bq[k * 4 + 1]);
+                        mma_u8s8(acc[1], a0, a1, a2, a3, bq[k * 4 + 2], bq[k * 4 + 3]);
+                    }
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        const int row = 16 * mt + r + 8 * hf;  // token within the chunk
+                        const int tl = cc * CT + row;          // token within the warp's range
+                        const float dot = fmaf((float)acc[0][2 * hf], 65536.0f,
+                                               (float)(acc[0][2 * hf + 1] * 256 + acc[1][2 * hf]));
+                        const float2 km = *reinterpret_cast<const float2 *>(kms + 2 * row);
+                        const float s = fmaf(km.x * c1, dot, km.y * c2);
+                        const float sp = s + __log2f(vms[2 * row]);
+                        if (tl < n_w && my_head) {
+                            scw[q * kScStride + tl] = sp;
+                            rmax = fmaxf(rmax, fmaxf(s, sp));
+                        }
+                    }
+                }
+                release_chunk(j);
+            }
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 4));
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 8));
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 16));
+            Rp = __shfl_sync(0xffffffffu, rmax, ph);  // lane ph holds head ph's max
+
+            // ---------------- phase 2: values ----------------
+            for (int cc = 0; cc < nk; cc++, j++) {
+                wait_chunk(j);
+                const unsigned char *st = slots + (j & 1) * GG::SLOT;
+                const float *vms = reinterpret_cast<const float *>(st + CT * KB);
+#pragma unroll
+                for (int sp = 0; sp < CT / 32; sp++) {
+                    const int tc = 32 * sp + 4 * tq;  // this lane's first token within the chunk
+                    const int tb = cc * CT + tc;      // ... within the warp's range
+                    uint32_t U[4] = {0u, 0u, 0u, 0u};
+                    if (ph < G && tb < n_w) {
+                        const float4 s4 = *reinterpret_cast<const float4 *>(scw + ph * kScStride + tb);
+                        const float4 m01 = *reinterpret_cast<const float4 *>(vms + 2 * tc);
+                        const float4 m23 = *reinterpret_cast<const float4 *>(vms + 2 * tc + 4);
+                        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                        const float vs[4] = {m01.x, m01.z, m23.x, m23.z}, vz[4] = {m01.y, m01.w, m23.y, m23.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            if (tb + e < n_w) {
+                                const float u = fminf(ex2_approx(sv[e] - Rp), 1.0f);
+                                const float iv = __frcp_rn(vs[e]);
+                                Lp = fmaf(u, iv, Lp);
+                                Zp = fmaf(u, vz[e] * iv, Zp);
+                                U[e] = __float2uint_rn(u * kUMax);
+                            }
+                        }
+                    }
+                    // digit j of the 4 tokens -> one A-fragment word (row 4j + head, token quad tq)
+                    const uint32_t lo0 = __byte_perm(U[0], U[1], 0x0062), hi0 = __byte_perm(U[2], U[3], 0x0062);
+                    const uint32_t lo1 = __byte_perm(U[0], U[1], 0x0051), hi1 = __byte_perm(U[2], U[3], 0x0051);
+                    const uint32_t lo2 = __byte_perm(U[0], U[1], 0x0040), hi2 = __byte_perm(U[2], U[3], 0x0040);
+                    tile[(0 + ph) * kTileW + tq] = __byte_perm(lo0, hi0, 0x5410);
+                    tile[(4 + ph) * kTileW + tq] = __byte_perm(lo1, hi1, 0x5410);
+                    tile[(8 + ph) * kTileW + tq] = __byte_perm(lo2, hi2, 0x5410);
+                    __syncwarp();
+                    const uint32_t pa0 = tile[r * kTileW + q], pa2 = tile[r * kTileW + 4 + q];
+                    const uint32_t pa1 = r < 4 ? tile[(r + 8) * kTileW + q] : 0u;
+                    const uint32_t pa3 = r < 4 ? tile[(r + 8) * kTileW + 4 + q] : 0u;
+                    __syncwarp();
+                    // V words of token group q of 16-token blocks 2sp (b0) and 2sp+1 (b1)
+#pragma unroll
+                    for (int v = 0; v < GG::VV; v++) {
+                        const unsigned char *vb0 = st + (2 * sp) * (KB * kVBlock) + (8 * v + r) * 64 + 16 * q;
+                        const uint4 x0 = *reinterpret_cast<const uint4 *>(vb0);
+                        const uint4 x1 = *reinterpret_cast<const uint4 *>(vb0 + KB * kVBlock);
+                        const uint32_t y0[4] = {x0.x, x0.y, x0.z, x0.w}, y1[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                        for (int jj = 0; jj < 4; jj++) {
+                            const int i = 4 * v + jj;
+                            if constexpr (BITS == 4) {
+                                // high nibbles used in place (16 * code): n-tile 2i+1 sums 16x, scaled at the end
+                                mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj] & 0x0F0F0F0Fu, y1[jj] & 0x0F0F0F0Fu);
+                                mma_u8u8(pacc[2 * i + 1], pa0, pa1, pa2, pa3, y0[jj] & 0xF0F0F0F0u,
+                                         y1[jj] & 0xF0F0F0F0u);
+                            } else {
+                                mma_u8u8(pacc[i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
+                            }
+                        }
+                    }
+                }
+                release_chunk(j);
+            }
+        }
+
+        // ---------------- warp partial -> its merge area ----------------
+        Lp += __shfl_xor_sync(0xffffffffu, Lp, 1);
+        Lp += __shfl_xor_sync(0xffffffffu, Lp, 2);
+        Lp += __shfl_xor_sync(0xffffffffu, Lp, 4);
+        Zp += __shfl_xor_sync(0xffffffffu, Zp, 1);
+        Zp += __shfl_xor_sync(0xffffffffu, Zp, 2);
+        Zp += __shfl_xor_sync(0xffffffffu, Zp, 4);
+        __syncwarp();  // scw (scores) becomes the merge area
+        {
+            // rows: r < 4 -> (digit 0, head r) in c0/c1 and (digit 2, head r) in c2/c3;
+            // r >= 4 -> (digit 1, head r - 4) in c0/c1.  value = (d0*2^16 + d1*2^8 + d2) / (2^24 - 1).
+            // Lanes r < 4 store head r's value of column 2q+cc of n-tile nt at
+            // (nt*2 + cc)*16 + lane: 16 consecutive words per store, no bank conflicts.
+            const float w_lo = (r < 4) ? 65536.0f / kUMax : 256.0f / kUMax;
+            const float w_d2 = 1.0f / kUMax;
+#pragma unroll
+            for (int nt = 0; nt < GG::NTV; nt++) {
+                const float ntw = (BITS == 4 && (nt & 1)) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    float f = (float)pacc[nt][cc] * w_lo;
+                    if (r < 4) f = fmaf((float)pacc[nt][2 + cc], w_d2, f);
+                    const float mid = __shfl_down_sync(0xffffffffu, f, 16);
+                    if (r < 4) scw[(nt * 2 + cc) * 16 + lane] = (f + mid) * ntw;
+                }
+            }
+        }
+        if (tq == 0) {
+            rlz[(warp * 4 + ph) * 3 + 0] = (n_w > 0 && ph < G) ? Rp : -INFINITY;
+            rlz[(warp * 4 + ph) * 3 + 1] = Lp;
+            rlz[(warp * 4 + ph) * 3 + 2] = Zp;
+        }
+        __syncthreads();
+
+        // ---------------- merge the warps: warp g finishes head g ----------------
+        // Splits are merged afterwards by attend_combine_kernel.
+        const bool fail_now = *reinterpret_cast<volatile int *>(&s_flag[1]) != 0;
+        if (warp < G && !fail_now) {
+            const int g = warp;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w2 = 0; w2 < kNW; w2++) M = fmaxf(M, rlz[(w2 * 4 + g) * 3]);
+            int idx[EPL];
+#pragma unroll
+            for (int rr = 0; rr < EPL; rr++) {
+                int nt, col;
+                v_inv<BITS, D>(lane * EPL + rr, nt, col);
+                idx[rr] = (nt * 2 + (col & 1)) * 16 + 4 * g + (col >> 1);
+            }
+            float L = 0.0f, Z = 0.0f, x[EPL];
+#pragma unroll
+            for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
+#pragma unroll
+            for (int w2 = 0; w2 < kNW; w2++) {
+                const float Rw = rlz[(w2 * 4 + g) * 3];
+                if (Rw == -INFINITY) continue;
+                const float wt = exp2f(Rw - M);
+                L = fmaf(wt, rlz[(w2 * 4 + g) * 3 + 1], L);
+                Z = fmaf(wt, rlz[(w2 * 4 + g) * 3 + 2], Z);
+                const float *mw = scw_all + w2 * GG::SCW;
+#pragma unroll
+                for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wt, mw[idx[rr]], x[rr]);
+            }
+            if (n_splits == 1) {
+                const float *sg = a.signs + (int64_t)ig.h * D;
+                const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+                for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
+                warp_wht_butterfly<EPL>(x, lane, D);
+                T *dst = static_cast<T *>(a.out) + ((int64_t)ig.b * a.heads * G + ig.h * G + g) * D;
+#pragma unroll
+                for (int rr = 0; rr < EPL; rr++)
+                    st_from_f32(dst + lane * EPL + rr, x[rr] * a.wht_scale * sg[lane * EPL + rr]);
+            } else {
+                float *wsp = a.workspace + ((ig.u * n_splits + ig.split) * G + g) * (D + 4);
+                if (EPL == 4) {
+                    *reinterpret_cast<float4 *>(wsp + lane * 4) = make_float4(x[0], x[1 % EPL], x[2 % EPL], x[3 % EPL]);
+                } else {
+#pragma unroll
+                    for (int rr = 0; rr < EPL; rr++) wsp[lane * EPL + rr] = x[rr];
+                }
+                if (lane == 0) {
+                    wsp[D] = M;
+                    wsp[D + 1] = L;
+                    wsp[D + 2] = Z;
+                }
+            }
+        }
+        __syncthreads();  // merge areas and flags are reused by the next item
+    }
+
+    if (failed && lane == 0) {
+        // a wait gave up: let the (at most two) copies this warp still has in flight land (bounded)
+        for (int jj = j; jj < j + 2; jj++) mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
+    }
 }
 
 template <typename T, int BITS, int D>
-int launch_decode(const AttendArgs &a, int n_splits, int tps, int tpw, cudaStream_t stream) {
-    auto kern = decode_mma_kernel<T, BITS, D>;
-    const size_t smem = decode_smem_bytes(D);
-    static int configured[64];  // per device: the shared-memory opt-in is set once
+int launch_shape(const AttendArgs &a, const AppendArgs *ap, int n_splits, int tps, cudaStream_t stream) {
+    uint32_t *qfrag = a.qprep;
+    float *qscal = reinterpret_cast<float *>(a.qprep + (size_t)a.batch * a.heads * 32 * 16);
+    const int do_append = ap != nullptr;
+    AppendArgs apv{};
+    if (ap) apv = *ap;
+    const int prep_warps = (do_append ? 2 : 0) + a.group;
+    decode_prep_kernel<T, BITS, D><<<dim3(a.heads, a.batch), 32 * prep_warps, 0, stream>>>(a, apv, do_append,
+                                                                                            qfrag, qscal);
+    count_launch();
+    int rc = check_cuda(cudaGetLastError(), "gqa decode prep launch");
+    if (rc != SA_OK) return rc;
+
+    using GG = WGeo<BITS, D>;
+    auto kern = decode_stream_kernel<T, BITS, D>;
+    const size_t smem = GG::SMEM;
+    static int configured[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return check_cuda(e, "gqa_decode_mma smem attribute");
+        if (e != cudaSuccess) return check_cuda(e, "gqa decode smem attribute");
         if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
     }
-    dim3 grid(n_splits, a.heads, a.batch);
-    kern<<<grid, kNW * 32, smem, stream>>>(a, n_splits, tps, tpw);
+    const int n_items = a.batch * a.heads * n_splits;
+    int grid = 2 * a.sm_count;
+    if (grid > n_items) grid = n_items;
+    const int tpw = tps / kNW;
+    kern<<<grid, kNW * 32, smem, stream>>>(a, n_splits, tps, tpw, n_items, qfrag, qscal);
     count_launch();
-    int rc = check_cuda(cudaGetLastError(), "gqa_decode_mma launch");
-    if (rc != SA_OK || n_splits == 1) return rc;
+    int rc2 = check_cuda(cudaGetLastError(), "gqa decode launch");
+    if (rc2 != SA_OK || n_splits == 1) return rc2;
     return launch_gqa_combine(a, n_splits, stream);
 }
 
 template <typename T>
-int launch_by_shape(const AttendArgs &a, int n_splits, int tps, int tpw, cudaStream_t stream) {
-    if (a.bits == 4 && a.head_dim == 128) return launch_decode<T, 4, 128>(a, n_splits, tps, tpw, stream);
-    if (a.bits == 8 && a.head_dim == 128) return launch_decode<T, 8, 128>(a, n_splits, tps, tpw, stream);
-    if (a.bits == 4 && a.head_dim == 64) return launch_decode<T, 4, 64>(a, n_splits, tps, tpw, stream);
-    return launch_decode<T, 8, 64>(a, n_splits, tps, tpw, stream);
+int launch_dtype(const AttendArgs &a, const AppendArgs *ap, int n_splits, int tps, cudaStream_t stream) {
+    if (a.bits == 4 && a.head_dim == 128) return launch_shape<T, 4, 128>(a, ap, n_splits, tps, stream);
+    if (a.bits == 8 && a.head_dim == 128) return launch_shape<T, 8, 128>(a, ap, n_splits, tps, stream);
+    if (a.bits == 4 && a.head_dim == 64) return launch_shape<T, 4, 64>(a, ap, n_splits, tps, stream);
+    return launch_shape<T, 8, 64>(a, ap, n_splits, tps, stream);
 }
 
 }  // namespace
 
-int launch_gqa_decode_fast(const AttendArgs &a, cudaStream_t stream, bool *handled) {
-    *handled = false;
-    if (a.seq_len != 1 || a.group > 4 || (a.bits != 4 && a.bits != 8) || (a.head_dim != 64 && a.head_dim != 128))
-        return SA_OK;
-    if (a.capacity % 64 != 0) return SA_OK;
+// Whether the tensor-core decode handles this call.
+bool decode_fast_eligible(const AttendArgs &a) {
+    if (a.seq_len != 1 || a.group < 1 || a.group > 4) return false;
+    if ((a.bits != 4 && a.bits != 8) || (a.head_dim != 64 && a.head_dim != 128)) return false;
+    if (a.capacity % 64 != 0 || a.qprep == nullptr || a.dev_status == nullptr)
+        return false;
+    const int64_t total = a.pos0 + 1;
+    if (total > (int64_t)kMaxSplits * kNW * kTPW) return false;
+    // every split's partial must fit the workspace
+    const int64_t units = (int64_t)a.batch * a.heads;
+    return (size_t)((int64_t)kMaxSplits * units * a.group * (a.head_dim + 4)) <= a.workspace_floats;
+}
+
+// Prep (+ append when `ap` is given) and decode of one query token per row.
+int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream) {
     const int64_t total = a.pos0 + 1;
     const int64_t units = (int64_t)a.batch * a.heads;
-    // splits: every warp holds at most kTPW tokens; enough CTAs for ~7 waves
-    // of 2 CTAs per SM; partials must fit the workspace.
-    int64_t n_min = (total + (int64_t)kNW * kTPW - 1) / ((int64_t)kNW * kTPW);
-    int64_t n_want = (14LL * a.sm_count + units - 1) / units;
-    int64_t n_len = (total + kNW * 16 - 1) / (kNW * 16);  // at least 16 tokens per warp
-    int64_t n = n_want < n_len ? n_want : n_len;
-    if (n < n_min) n = n_min;
+    // splits: at most kNW * kTPW tokens each, a multiple of kNW * 64 (whole
+    // chunks per warp); enough work items for ~8 per persistent CTA.
+    const int64_t grain = (int64_t)kNW * 64, cap_tok = (int64_t)kNW * kTPW;
+    int64_t n = (total + cap_tok - 1) / cap_tok;
+    const int64_t want = (16LL * a.sm_count + units - 1) / units;
+    const int64_t by_len = (total + grain - 1) / grain;
+    const int64_t more = want < by_len ? want : by_len;
+    if (n < more) n = more;
     if (n > kMaxSplits) n = kMaxSplits;
-    if (n < n_min) return SA_OK;  // context too long for the split limit: generic path
-    const int64_t per_split = (int64_t)a.group * (a.head_dim + 4) * units;
-    if (n > 1 && (size_t)(n * per_split) > a.workspace_floats) {
-        n = (int64_t)(a.workspace_floats / (size_t)per_split);
-        if (n < n_min || n < 1) return SA_OK;
-    }
-    // tokens per warp: multiple of 16; tokens per split = kNW * tokens per warp
-    int64_t tpw = (total + n * kNW - 1) / (n * kNW);
-    tpw = (tpw + 15) / 16 * 16;
-    if (tpw > kTPW) return SA_OK;
-    const int64_t tps = tpw * kNW;
+    int64_t tps = (total + n - 1) / n;
+    tps = (tps + grain - 1) / grain * grain;
     n = (total + tps - 1) / tps;
-    *handled = true;
     switch (a.dtype) {
-        case SA_DTYPE_FLOAT: return launch_by_shape<float>(a, (int)n, (int)tps, (int)tpw, stream);
-        case SA_DTYPE_FLOAT16: return launch_by_shape<__half>(a, (int)n, (int)tps, (int)tpw, stream);
-        default: return launch_by_shape<__nv_bfloat16>(a, (int)n, (int)tps, (int)tpw, stream);
+        case SA_DTYPE_FLOAT: return launch_dtype<float>(a, ap, (int)n, (int)tps, stream);
+        case SA_DTYPE_FLOAT16: return launch_dtype<__half>(a, ap, (int)n, (int)tps, stream);
+        default: return launch_dtype<__nv_bfloat16>(a, ap, (int)n, (int)tps, stream);
     }
 }
 

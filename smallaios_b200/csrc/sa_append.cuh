@@ -1,0 +1,136 @@
+// Quantize-on-append of one vector: RoPE (K only) + PolarQuant encode + bit
+// packing by one warp.  Bit-exact with PolarQuantizer::encode
+// (kv_compression.rs:216-267) on the f32 value of the input: every float
+// operation is an explicitly rounded intrinsic in the reference's order, so
+// nvcc cannot contract or reassociate it.  Shared by the append kernel and
+// the decode prep kernel.
+#pragma once
+
+#include "sa_common.cuh"
+#include "sa_internal.h"
+
+namespace sa {
+
+// RoPE of element e of a vector at `pos` (rotate_rope_block,
+// ops/microsoft.rs:137-160): y0 = c*x0 - s*x1, y1 = s*x0 + c*x1, each product
+// rounded before the add.  `x` is element e, `src` the whole input vector.
+template <typename T>
+__device__ __forceinline__ float rope_element(const T *src, float x, int e, int d, int64_t pos, const float *cos_cache,
+                                              const float *sin_cache, int interleaved) {
+    const int half = d / 2;
+    int pair, partner;
+    bool first;
+    if (interleaved) {
+        pair = e >> 1;
+        first = (e & 1) == 0;
+        partner = first ? e + 1 : e - 1;
+    } else {
+        first = e < half;
+        pair = first ? e : e - half;
+        partner = first ? e + half : e - half;
+    }
+    const float c = cos_cache[pos * half + pair], sn = sin_cache[pos * half + pair];
+    const float xo = ld_f32(src + partner);
+    return first ? __fsub_rn(__fmul_rn(c, x), __fmul_rn(sn, xo)) : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x));
+}
+
+// Encode and store vector (b, s, h, which) of an append (which: 0 = K, 1 = V).
+// All 32 lanes of the warp must call it; s_codes holds >= head_dim bytes.
+template <typename T, int EPL>
+__device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b, int s, int h, int which, int lane,
+                                                     uint8_t *s_codes) {
+    const int d = a.head_dim;
+    const int64_t pos = a.pos0 + s;
+    const bool active = lane * EPL < d;
+    const T *src = static_cast<const T *>(which ? a.value : a.key) + (((int64_t)b * a.seq_len + s) * a.heads + h) * d;
+    float x[EPL];
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = active ? ld_f32(src + lane * EPL + r) : 0.0f;
+    if (which == 0 && a.do_rotary && active) {
+#pragma unroll
+        for (int r = 0; r < EPL; r++)
+            x[r] = rope_element(src, x[r], lane * EPL + r, d, pos, a.cos_cache, a.sin_cache, a.interleaved);
+    }
+
+    // apply_signs + butterfly + 1/sqrt_approx(n) (kv_compression.rs:81-123).
+    const float *sg = a.signs + (int64_t)h * d;
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = __fmul_rn(x[r], active ? sg[lane * EPL + r] : 1.0f);
+    warp_wht_butterfly<EPL>(x, lane, d);
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = __fmul_rn(x[r], a.wht_scale);
+
+    // min / max with strict comparisons in index order: the first occurrence
+    // wins, as in the sequential loop of encode (this matters for +-0).
+    float mn = INFINITY, mx = -INFINITY;
+    int imn = 0x7fffffff, imx = 0x7fffffff;
+    if (active) {
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            const int e = lane * EPL + r;
+            if (x[r] < mn) {
+                mn = x[r];
+                imn = e;
+            }
+            if (x[r] > mx) {
+                mx = x[r];
+                imx = e;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float omn = __shfl_xor_sync(0xffffffffu, mn, o);
+        const int oimn = __shfl_xor_sync(0xffffffffu, imn, o);
+        const float omx = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oimx = __shfl_xor_sync(0xffffffffu, imx, o);
+        if (omn < mn || (omn == mn && oimn < imn)) {
+            mn = omn;
+            imn = oimn;
+        }
+        if (omx > mx || (omx == mx && oimx < imx)) {
+            mx = omx;
+            imx = oimx;
+        }
+    }
+
+    const uint32_t levels = (1u << a.bits) - 1u;
+    const float range = __fsub_rn(mx, mn);
+    const float scale = range > 0.0f ? __fdiv_rn(range, (float)levels) : 1.0f;
+    const float zp = mn;
+#pragma unroll
+    for (int r = 0; r < EPL; r++) {
+        if (active) {
+            uint32_t q = 0u;
+            if (scale > 0.0f) q = __float2uint_rz(rust_round_f32(__fdiv_rn(__fsub_rn(x[r], zp), scale)));
+            s_codes[lane * EPL + r] = (uint8_t)(q < levels ? q : levels);
+        }
+    }
+    __syncwarp();
+
+    // pack_bits (kv_compression.rs:294-312): LSB-first contiguous bit stream.
+    const int cb = a.code_bytes;
+    const int64_t row = ((int64_t)b * a.heads + h);
+    for (int j = lane; j < cb; j += 32) {
+        uint32_t byte = 0;
+#pragma unroll
+        for (int bit = 0; bit < 8; bit++) {
+            const int g = 8 * j + bit;
+            const int e = g / a.bits, eb = g % a.bits;
+            if (e < d) byte |= ((uint32_t)(s_codes[e] >> eb) & 1u) << bit;
+        }
+        if (which == 0) {
+            a.k_codes[(row * a.capacity + pos) * cb + j] = (uint8_t)byte;
+        } else {
+            a.v_codes[row * a.capacity * cb + v_byte_offset(pos, j, cb)] = (uint8_t)byte;
+        }
+    }
+    if (lane == 0) {
+        float *meta = (which == 0 ? a.k_meta : a.v_meta) + (row * a.capacity + pos) * 2;
+        meta[0] = scale;
+        meta[1] = zp;
+    }
+    __syncwarp();
+}
+
+}  // namespace sa

@@ -9,7 +9,17 @@
 namespace sa {
 
 constexpr int kCapacityAlign = 64;   // token capacity is padded to this
-constexpr int kVGroup = 4;           // V codes are byte-interleaved by 4 tokens
+constexpr int kVGroup = 4;           // V codes are byte-interleaved by 4 tokens ...
+constexpr int kVBlock = 16;          // ... and 16-byte chunks of 4 such groups interleave in 16-token blocks
+
+// Byte offset, within one (row, head)'s V codes, of byte j of token t
+// (cb = code bytes per token, a multiple of 4): 16-token blocks of 16*cb
+// bytes; inside a block, 16-byte chunk c of token group g (4 tokens) sits at
+// c*64 + g*16, and a group's bytes are ordered k = 4*j + t%4.
+__host__ __device__ __forceinline__ int64_t v_byte_offset(int64_t t, int j, int cb) {
+    const int k = 4 * j + (int)(t & 3);
+    return (t >> 4) * (int64_t)(16 * cb) + (k >> 4) * 64 + ((t >> 2) & 3) * 16 + (k & 15);
+}
 constexpr int kMaxSplits = 64;       // split-K partitions per (row, kv head)
 
 struct kv_cache_impl {
@@ -31,6 +41,8 @@ struct kv_cache_impl {
     float *signs;      // [L][H][D]  +-1.0f
     float *workspace;  // split-K partials
     size_t workspace_floats;
+    uint32_t *qprep;   // [B*H*32*16] q-digit words + [B*H*8] score constants
+    int *dev_status;   // one int: device-side status bits
     size_t layer_codes_bytes;  // B*H*T*CB
     size_t layer_meta_floats;  // B*H*T*2
 };
@@ -67,10 +79,14 @@ struct AttendArgs {
     float *workspace;
     size_t workspace_floats;
     int sm_count;
+    uint32_t *qprep;  // decode prep area: per (row, head) q-digit fragments + constants
+    int *dev_status;  // device-side status word (bounded waits that gave up)
 };
 
 int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
+bool decode_fast_eligible(const AttendArgs &a);
+int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
                         int block_size, cudaStream_t stream);

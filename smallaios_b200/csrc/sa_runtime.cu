@@ -73,7 +73,7 @@ static void make_signs(uint64_t seed, int dim, float *out) {
 }
 
 int launch_gqa_attend_generic(const AttendArgs &a, cudaStream_t stream);
-int launch_gqa_decode_fast(const AttendArgs &a, cudaStream_t stream, bool *handled);
+
 
 }  // namespace sa
 
@@ -118,6 +118,10 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
         return set_error(SA_ERR_INVALID_ATTRIBUTE, "bits must be 3, 4, or 8");
     if (c.head_dim < 16 || c.head_dim > 256)
         return set_error(SA_ERR_UNSUPPORTED, "kv_cache_create: head_dim %d outside 16..256", c.head_dim);
+    if ((c.head_dim * c.bits / 8) % 4 != 0)
+        return set_error(SA_ERR_UNSUPPORTED, "kv_cache_create: head_dim %d at %d bits packs to %d bytes, not a "
+                         "multiple of 4 (the V layout interleaves 4-byte words)", c.head_dim, c.bits,
+                         c.head_dim * c.bits / 8);
     if (c.num_heads <= 0 || c.num_heads % c.num_kv_heads != 0)
         return set_error(SA_ERR_INVALID_ATTRIBUTE, "num_heads must be a positive multiple of num_kv_heads");
     if (c.kv_head_count <= 0 || c.kv_head_begin < 0 || c.kv_head_begin + c.kv_head_count > c.num_kv_heads)
@@ -148,7 +152,9 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     const size_t meta = up(L * k->layer_meta_floats * sizeof(float));
     const size_t signs = up(L * H * D * sizeof(float));
     const size_t ws = up(k->workspace_floats * sizeof(float));
-    k->base_bytes = 2 * codes + 2 * meta + signs + ws;
+    const size_t qp = up(B * H * (32 * 16 + 8) * sizeof(uint32_t));
+    const size_t st = 256;
+    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st;
     const size_t k_bytes = k->base_bytes;
     cudaError_t e = cudaMalloc(&k->base, k->base_bytes);
     if (e != cudaSuccess) {
@@ -169,6 +175,10 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->signs = reinterpret_cast<float *>(p);
     p += signs;
     k->workspace = reinterpret_cast<float *>(p);
+    p += ws;
+    k->qprep = reinterpret_cast<uint32_t *>(p);
+    p += qp;
+    k->dev_status = reinterpret_cast<int *>(p);
     // Zero-initialise like GpuKvCache::allocate (kv_cache.rs:171-175).
     e = cudaMemset(k->base, 0, k->base_bytes);
     if (e == cudaSuccess) {
@@ -232,6 +242,18 @@ int sa_kv_cache_advance(sa_kv_cache *cache, int64_t n) {
         return set_error(SA_ERR_CAPACITY, "kv_cache_advance:position_overflow");
     k->position += n;
     return SA_OK;
+}
+
+int sa_kv_cache_device_status(sa_kv_cache *cache, int32_t *status, int32_t clear) {
+    if (!cache || !status) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_device_status: NULL argument");
+    kv_cache_impl *k = reinterpret_cast<kv_cache_impl *>(cache);
+    int v = 0;
+    int rc = check_cuda(cudaMemcpy(&v, k->dev_status, sizeof(int), cudaMemcpyDeviceToHost),
+                        "kv_cache_device_status read");
+    if (rc != SA_OK) return rc;
+    *status = v;
+    if (clear && v) rc = check_cuda(cudaMemset(k->dev_status, 0, sizeof(int)), "kv_cache_device_status clear");
+    return rc;
 }
 
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config) {
@@ -324,10 +346,14 @@ int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void 
     return launch_kv_append(a, static_cast<cudaStream_t>(stream));
 }
 
+// Attention of `seq_len` query tokens over the cache.  When `key`/`value`
+// are given, the tokens are appended first (the operator); the tensor-core
+// decode path fuses that append into its prep kernel.
 static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void *attn_out, int32_t dtype,
                        int32_t batch, int32_t seq_len, int64_t num_heads, int32_t has_scale, float scale,
                        const float *cos_cache, const float *sin_cache, int32_t cache_rows, int32_t do_rotary,
-                       int32_t rotary_interleaved, cudaStream_t stream) {
+                       int32_t rotary_interleaved, cudaStream_t stream, const void *key = nullptr,
+                       const void *value = nullptr) {
     if (layer < 0 || layer >= k->cfg.num_layers)
         return set_error(SA_ERR_INVALID_ARGUMENT, "gqa_attend: layer_idx %d", layer);
     if (!dtype_ok(dtype)) return set_error(SA_ERR_UNSUPPORTED, "gqa_attend: dtype %d not supported", dtype);
@@ -374,9 +400,38 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
     a.workspace = k->workspace;
     a.workspace_floats = k->workspace_floats;
     a.sm_count = k->sm_count;
-    bool handled = false;
-    rc = launch_gqa_decode_fast(a, stream, &handled);
-    if (rc != SA_OK || handled) return rc;
+    a.qprep = k->qprep;
+    a.dev_status = k->dev_status;
+    AppendArgs ap;
+    if (key) {
+        ap.key = key;
+        ap.value = value;
+        ap.dtype = dtype;
+        ap.batch = batch;
+        ap.seq_len = seq_len;
+        ap.heads = v.kv_heads;
+        ap.head_dim = v.head_dim;
+        ap.bits = v.bits;
+        ap.code_bytes = v.code_bytes;
+        ap.capacity = v.capacity;
+        ap.pos0 = k->position;
+        ap.k_codes = v.k_codes;
+        ap.v_codes = v.v_codes;
+        ap.k_meta = v.k_meta;
+        ap.v_meta = v.v_meta;
+        ap.signs = v.signs;
+        ap.wht_scale = v.wht_scale;
+        ap.cos_cache = cos_cache;
+        ap.sin_cache = sin_cache;
+        ap.cache_rows = cache_rows;
+        ap.do_rotary = a.do_rotary;
+        ap.interleaved = a.interleaved;
+    }
+    if (decode_fast_eligible(a)) return launch_gqa_decode_fast(a, key ? &ap : nullptr, stream);
+    if (key) {
+        rc = launch_kv_append(ap, stream);
+        if (rc != SA_OK) return rc;
+    }
     return launch_gqa_attend_generic(a, stream);
 }
 
@@ -424,11 +479,13 @@ int sa_group_query_attention(sa_kv_cache *cache, int32_t layer, const void *quer
     int rc = check_rope("GroupQueryAttention", do_rotary, cos_cache, sin_cache, cache_rows,
                         k->position + seq_len - 1);
     if (rc != SA_OK) return rc;
-    rc = sa_kv_append(cache, layer, key, value, dtype, batch, seq_len, cos_cache, sin_cache, cache_rows,
-                      do_rotary, rotary_interleaved, stream);
-    if (rc != SA_OK) return rc;
+    if (!dtype_ok(dtype)) return set_error(SA_ERR_UNSUPPORTED, "GroupQueryAttention: dtype %d not supported", dtype);
+    if (layer < 0 || layer >= k->cfg.num_layers)
+        return set_error(SA_ERR_INVALID_ARGUMENT, "GroupQueryAttention: layer_idx %d", layer);
+    if (seq_len == 0) return SA_OK;
     return attend_impl(k, layer, query, attn_out, dtype, batch, seq_len, num_heads, has_scale, scale, cos_cache,
-                       sin_cache, cache_rows, do_rotary, rotary_interleaved, static_cast<cudaStream_t>(stream));
+                       sin_cache, cache_rows, do_rotary, rotary_interleaved, static_cast<cudaStream_t>(stream), key,
+                       value);
 }
 
 int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zero_points,

@@ -37,7 +37,7 @@ class LayerView:
     """GpuKvCache::view_at (kv_cache.rs:336-378), as torch tensors."""
 
     k_codes: torch.Tensor  # uint8 (B, H, T, CB)
-    v_codes: torch.Tensor  # uint8 (B, H, T/4, CB, 4)  (4-token byte interleave)
+    v_codes: torch.Tensor  # uint8 (B, H, T/16, CB/4, 4, 4, 4): 16-token blocks, see v_codes_tokens
     k_meta: torch.Tensor   # f32 (B, H, T, 2) {scale, zero_point}
     v_meta: torch.Tensor   # f32 (B, H, T, 2)
     signs: torch.Tensor    # f32 (H, D) +-1
@@ -47,9 +47,15 @@ class LayerView:
     capacity: int
 
     def v_codes_tokens(self) -> torch.Tensor:
-        """V codes in per-token pack_bits order (B, H, T, CB)."""
-        b, h, tg, cb, g = self.v_codes.shape
-        return self.v_codes.permute(0, 1, 2, 4, 3).reshape(b, h, tg * g, cb)
+        """V codes in per-token pack_bits order (B, H, T, CB).
+
+        Library layout: per 16-token block, [chunk c][group g][byte jj][token tt]
+        holds byte 4*c + jj of token 4*g + tt (16-byte chunks of the four
+        4-token groups interleave, so a quarter-warp's tensor-core fragment
+        loads hit 32 distinct shared-memory banks).
+        """
+        b, h, nblk, c4, g, jj, tt = self.v_codes.shape
+        return self.v_codes.permute(0, 1, 2, 4, 6, 3, 5).reshape(b, h, nblk * g * tt, c4 * jj)
 
 
 class GpuKvCache:
@@ -137,7 +143,7 @@ class GpuKvCache:
         dev = self.device
         return LayerView(
             k_codes=_view(v.k_codes, (B, H, T, CB), "|u1", dev),
-            v_codes=_view(v.v_codes, (B, H, T // 4, CB, 4), "|u1", dev),
+            v_codes=_view(v.v_codes, (B, H, T // 16, CB // 4, 4, 4, 4), "|u1", dev),
             k_meta=_view(v.k_meta, (B, H, T, 2), "<f4", dev),
             v_meta=_view(v.v_meta, (B, H, T, 2), "<f4", dev),
             signs=_view(v.signs, (H, D), "<f4", dev),

@@ -59,6 +59,11 @@ def oracle_attend(q_bshd: np.ndarray, kc, km, vc, vm, signs_hd, bits, pos0, scal
 
 
 def interleave_v(vc_tokens: np.ndarray) -> np.ndarray:
-    """(B, H, T, CB) per-token codes -> (B, H, T/4, CB, 4) library layout."""
+    """(B, H, T, CB) per-token codes -> the library's V layout, flattened per (B, H).
+
+    16-token blocks; in a block, byte 4*c + jj of token 4*g + tt sits at
+    ((c*4 + g)*4 + jj)*4 + tt (16-byte chunks of the four token groups interleave).
+    """
     b, h, t, cb = vc_tokens.shape
-    return np.ascontiguousarray(vc_tokens.reshape(b, h, t // 4, 4, cb).transpose(0, 1, 2, 4, 3))
+    x = vc_tokens.reshape(b, h, t // 16, 4, 4, cb // 4, 4)  # blk, g, tt, c, jj
+    return np.ascontiguousarray(x.transpose(0, 1, 2, 5, 3, 6, 4)).reshape(b, h, t * cb)

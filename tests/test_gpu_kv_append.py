@@ -63,8 +63,17 @@ def _assert_bit_exact(got, want):
 
 
 @pytest.mark.parametrize("bits", [3, 4, 8])
-@pytest.mark.parametrize("d", [16, 64, 128])
+@pytest.mark.parametrize("d", [16, 32, 64, 128])
 def test_append_bit_exact_bits_dims(cuda_device, bits, d):
+    if d * bits // 8 % 4:
+        # a V row must pack into whole 4-byte words (D=16 at 3 bits is 6 bytes)
+        import smallaios_b200 as sa
+        from smallaios_b200._lib import SA_ERR_UNSUPPORTED, SaError
+
+        with pytest.raises(SaError) as e:
+            sa.GpuKvCache(1, 2, d, 8, bits=bits, device=cuda_device)
+        assert e.value.status == SA_ERR_UNSUPPORTED
+        return
     got, want = _run_append_case(cuda_device, b=2, s=5, h=3, d=d, bits=bits, dtype="f32", rotary=True,
                                  interleaved=False, pos0=3, seed=bits * 100 + d)
     _assert_bit_exact(got, want)

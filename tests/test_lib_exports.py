@@ -56,6 +56,7 @@ def _cfg(**kw):
     (dict(num_heads=7), 1, b"num_heads must be a positive multiple of num_kv_heads"),
     (dict(kv_head_begin=1, kv_head_count=2), 1, b"kv head range"),
     (dict(head_dim=512), 3, b"head_dim 512 outside 16..256"),
+    (dict(head_dim=16, bits=3), 3, b"not a multiple of 4"),
 ])
 def test_cache_config_validation_without_gpu(kw, status, msg):
     from smallaios_b200._lib import lib
