@@ -484,7 +484,7 @@ extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t pas
     int rc = static_scratch_for_current_device(&slot);
     if (rc != SA_OK) return rc;
 
-    AttendArgs a;
+    AttendArgs a{};
     a.query = query;
     a.out = attn_out;
     a.dtype = dtype;

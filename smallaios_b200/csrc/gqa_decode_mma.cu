@@ -1,7 +1,7 @@
 // Tensor-core decode attention over the PolarQuant cache: one query token per
 // sequence, 4/8-bit codes, head_dim 64/128, up to 4 query heads per KV head.
 //
-// Two launches per step:
+// Three launches per step:
 //
 //  decode_prep_kernel, one CTA per (KV head, batch row):
 //    - quantize-on-append of the new token's K and V (same bit-exact encoder
@@ -11,32 +11,32 @@
 //      q' ~= sigma * (d0*2^16 + d1*2^8 + d2), |d| <= 127, stored already
 //      arranged as each lane's mma B-fragment words.
 //
-//  decode_persistent_kernel, two CTAs per SM, each looping over work items
-//  (batch row, KV head, split of the context).  Warp 8 is the producer: one
-//  thread streams every item's K then V chunks (256 tokens each) into a ring
-//  of shared-memory slots with 1-D bulk copies (cp.async.bulk + mbarrier, no
-//  multicast), running ahead across items as far as free slots allow.
-//  Warps 0-7 consume:
+//  decode_stream_kernel, two CTAs of 8 independent warps per SM.  Each warp
+//  owns an equal share of all (row, KV head, chunk) work laid end to end and
+//  streams it through two shared-memory slots of its own with 1-D bulk copies
+//  (cp.async.bulk + mbarrier, no multicast), in sub-segments of 128 tokens:
 //    phase 1 (K): K codes are unpacked to u8 in registers and contracted with
 //      the q' digits by mma.m16n8k32 u8 x s8 -> exact int32 dots q'.c; the
 //      score s = scale_t*sigma*(q'.c) + zp_t*sum(q') (log2 units) goes to
 //      shared memory.
-//    phase 2 (V): with the item's reference R = max over max(s, s + log2
-//      vscale), every token gets u = 2^(s + log2 vscale - R) in (0, 1] as a
-//      24-bit fixed-point number (three unsigned digits) and sum_t u_t * c_t
-//      is an exact int32 mma.m16n8k32 u8 x u8 whose B fragments are single
-//      32-bit words of the 4-token interleaved V layout.  L = sum u/vscale and
-//      Z = sum u*vzp/vscale are float sums.  No rescaling: R is known before
-//      phase 2 starts.
-//    The last CTA to finish a (row, head) merges its splits (counter per
-//    (row, head)), normalises, applies the inverse rotation and stores.
+//    phase 2 (V): with a reference R >= max(s) + log2(max vscale) (running
+//      over the sub-segments), every token gets e = 2^(s - R) and
+//      u = e * vscale in (0, 1] as a 24-bit fixed-point number (three
+//      unsigned digits); sum_t u_t * c_t is an exact int32 mma.m16n8k32
+//      u8 x u8 over the 16-token-block V layout, L = sum e and
+//      Z = sum e * vzp are float sums.  After the sub-segment the integer
+//      sums are folded into float sums in the frame of R.
+//    A warp leaves one partial record per unit its range touches.
+//
+//
+//  decode_merge_kernel: per unit, merges the records, normalises, applies the
+//  inverse rotation and stores.
+//
 //  Every mbarrier wait is bounded; a wait that gives up sets the cache's
-//  device status, the CTA stops writing and drains its own copies.
+//  device status, the warp stops issuing and writing and drains its copies.
 #include "sa_append.cuh"
 
 namespace sa {
-
-int launch_gqa_combine(const AttendArgs &a, int n_splits, cudaStream_t stream);
 
 namespace {
 
@@ -45,7 +45,8 @@ constexpr int kTileW = 12;        // u32 words per row of a warp's P-digit tile
 constexpr float kLog2eF = 1.4426950408889634f;
 constexpr float kQMax = 8355711.0f;   // 127*65536 + 127*256 + 127
 constexpr float kUMax = 16777215.0f;  // 2^24 - 1
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint32_t kWaitLimit = 20000;       // bounded waits: at most kWaitLimit tries ...
+constexpr uint32_t kWaitHintNs = 100000;     // ... each suspending the thread for up to 100 us
 
 // ---- PTX helpers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -61,12 +62,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  : "memory");
 }
 
+// The thread sleeps until the phase completes or the hint elapses, so a
+// waiting warp takes no issue slots from the warps that compute.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
         : "memory");
     return ok != 0;
 }
@@ -105,6 +108,15 @@ __device__ __forceinline__ void mma_u8u8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+
+// Programmatic dependent launch: let the next kernel of the stream start
+// early / wait until the previous kernel has completed and its writes are
+// visible (a no-op when the launch carries no programmatic dependency).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -168,6 +180,9 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     const int G = a.group;
     const int q0w = do_append ? 2 : 0;
     const float *sg = a.signs + (int64_t)h * D;
+    // the decode kernel may start now: it waits for this grid before it
+    // reads the q digits or the appended token
+    griddep_launch_dependents();
     if (do_append && warp < 2) {
         encode_append_vector<T, EPL>(ap, b, 0, h, warp, lane, s_codes[warp]);
     } else if (warp >= q0w && warp - q0w < G) {
@@ -240,182 +255,204 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     }
 }
 
-// ---- decode: independent warp streams -------------------------------------------
-// Each warp owns a contiguous range of up to kTPW tokens of an item and streams
-// it through its own two shared-memory slots (K chunks, then V chunks), so no
-// warp ever waits for another inside an item.
-constexpr int kTPW = 128;           // tokens per warp per item
+// ---- decode: stream-K warp ranges ----------------------------------------------
+// The context of every (row, KV head) unit is cut into chunks of CT tokens and
+// the chunks of all units are laid end to end (F chunks).  Warp w of the grid
+// (W warps) owns the contiguous range [w*F/W, (w+1)*F/W): every warp streams
+// the same number of chunks whatever the batch, heads and context length, and
+// no warp ever waits for another.  A range may start or end inside a unit and
+// may cover several units; for each unit it touches the warp leaves one
+// partial record (running max R, sums L and Z, un-normalised value sums) at
+// record index w + u, and decode_merge_kernel merges each unit's records.
+//
+// Inside a unit the warp walks sub-segments of up to kTPW tokens through its
+// own two shared-memory slots: phase 1 streams their K chunks (scores to
+// shared memory), phase 2 their V chunks with the running max as the
+// fixed-point reference; the integer accumulators are folded into float sums
+// after every sub-segment.
+constexpr int kTPW = 128;            // tokens per sub-segment
 constexpr int kScStride = kTPW + 8;  // floats per head row of a warp's score buffer (bank offset)
 
 template <int BITS, int D>
 struct WGeo {
     static constexpr int KB = D * BITS / 8;             // code bytes per token
     static constexpr int CT = (KB > 64) ? 32 : 64;       // tokens per chunk
+    static constexpr int SUB = kTPW / CT;                // chunks per sub-segment
     static constexpr int SLOT = CT * (KB + 16);          // K chunk: codes + K meta + V meta (a V chunk is smaller)
     static constexpr int SEGW = KB / 16;                 // K words per quad per row
     static constexpr int NCH = D / 32;                   // QK k-chunks
     static constexpr int NTV = D / 8;                    // PV n-tiles
+    static constexpr int NF = NTV;                       // float value sums per lane
     static constexpr int VV = ((BITS == 4) ? NTV / 2 : NTV) / 4;  // 16-byte V loads per 16-token block
     static constexpr int QW = NCH * 4;                   // q-digit words per lane
-    static constexpr int SCW = 4 * kScStride;            // floats of a warp's score buffer / merge area
-    static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 1024;
-    static_assert(4 * D <= SCW, "merge area must fit the score buffer");
+    static constexpr int SCW = 4 * kScStride;            // floats of a warp's score buffer
+    static constexpr int REC = 4 * D + 16;               // floats per partial record: [4][D] values, R/L/Z x 4
+    static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 512;
 };
 
-struct ItemGeo {
-    int64_t u;  // b * heads + h
-    int b, h, split;
-    int64_t s_begin;
-    int n_tok;
-};
-
-__device__ __forceinline__ ItemGeo item_geo(const AttendArgs &a, int item, int n_splits, int tps) {
-    ItemGeo g;
-    g.u = item / n_splits;
-    g.split = item % n_splits;
-    g.b = (int)(g.u / a.heads);
-    g.h = (int)(g.u % a.heads);
-    g.s_begin = (int64_t)g.split * tps;
-    const int64_t total = a.pos0 + 1;
-    const int64_t e = g.s_begin + tps < total ? g.s_begin + tps : total;
-    g.n_tok = (int)(e - g.s_begin);
-    return g;
+// Warp owning flat chunk f when F chunks are cut into W ranges
+// [w*F/W, (w+1)*F/W): the largest w with w*F/W <= f.
+__host__ __device__ __forceinline__ int warp_of_chunk(int f, int F, int W) {
+    return (int)((((int64_t)f + 1) * W - 1) / F);
 }
 
-// Tokens of warp `warp` in an item (0 if the item ends before its range).
-__device__ __forceinline__ int warp_tokens(int n_tok, int warp, int tpw) {
-    const int n = n_tok - warp * tpw;
-    return n <= 0 ? 0 : (n < tpw ? n : tpw);
-}
-
-// The chunk schedule of one warp over the CTA's items: for every item with a
-// non-empty range, its K chunks then its V chunks.  Lane 0 keeps the cursor
-// of the next chunk to issue, two chunks ahead of consumption.
+// The chunk schedule of one warp: for every sub-segment of its range, the K
+// chunks then the V chunks.  Lane 0 keeps the cursor of the next chunk to
+// issue, two chunks ahead of consumption.
 template <int BITS, int D>
-struct WarpStream {
+struct ChunkStream {
     using GG = WGeo<BITS, D>;
-    int item, c, nk, n;
-    int64_t u, t0;
+    int f, f_end, ubase, u;  // sub-segment start (flat chunk), range end, unit's first chunk, unit
+    int ns, idx;             // chunks in the sub-segment, next chunk in its 2*ns schedule
+    int done, n_issued;      // schedule exhausted; chunks issued so far
 
-    __device__ __forceinline__ void seek(const AttendArgs &a, int n_items, int n_splits, int tps, int tpw, int warp) {
-        for (; item < n_items; item += gridDim.x) {
-            const ItemGeo g = item_geo(a, item, n_splits, tps);
-            n = warp_tokens(g.n_tok, warp, tpw);
-            if (n > 0) {
-                u = g.u;
-                t0 = g.s_begin + (int64_t)warp * tpw;
-                nk = (n + GG::CT - 1) / GG::CT;
-                c = 0;
-                return;
-            }
+    __device__ __forceinline__ void start_sub(int fs, int ncu) {
+        if (fs >= f_end) {
+            done = 1;
+            return;
         }
+        u = fs / ncu;
+        ubase = u * ncu;
+        const int lim = min(f_end, ubase + ncu);
+        ns = min(lim - fs, GG::SUB);
+        f = fs;
+        idx = 0;
     }
 
-    __device__ __forceinline__ void issue(const AttendArgs &a, unsigned char *dst, uint64_t *bar) const {
+    __device__ __forceinline__ void issue(const AttendArgs &a, int total, unsigned char *dst, uint64_t *bar) const {
         constexpr int KB = GG::KB, CT = GG::CT;
-        const int64_t cap = a.capacity;
-        const int cc = c < nk ? c : c - nk;
-        const int cnt = n - cc * CT < CT ? n - cc * CT : CT;
+        const bool is_k = idx < ns;
+        const int g0 = (f - ubase + (is_k ? idx : idx - ns)) * CT;  // first token, a multiple of CT
+        const int cnt = min(total - g0, CT);
         const int mcnt = (cnt + 1) & ~1;  // meta rows rounded to even: 16-byte copies
-        const int64_t g0 = t0 + cc * CT;  // multiple of CT (>= 32)
+        const int64_t row = (int64_t)u * a.capacity + g0;
         const uint32_t mb = (uint32_t)(mcnt * 8);
-        if (c < nk) {  // K chunk: codes, K meta, V meta
+        if (is_k) {  // K chunk: codes, K meta, V meta
             const uint32_t cb = (uint32_t)(cnt * KB);
             mbar_expect_tx(bar, cb + 2 * mb);
-            bulk_g2s(dst, a.k_codes + (u * cap + g0) * KB, cb, bar);
-            bulk_g2s(dst + CT * KB, a.k_meta + (u * cap + g0) * 2, mb, bar);
-            bulk_g2s(dst + CT * KB + CT * 8, a.v_meta + (u * cap + g0) * 2, mb, bar);
+            bulk_g2s(dst, a.k_codes + row * KB, cb, bar);
+            bulk_g2s(dst + CT * KB, a.k_meta + row * 2, mb, bar);
+            bulk_g2s(dst + CT * KB + CT * 8, a.v_meta + row * 2, mb, bar);
         } else {  // V chunk: whole 16-token blocks of codes, V meta
             const uint32_t vb = (uint32_t)(((cnt + kVBlock - 1) / kVBlock) * KB * kVBlock);
             mbar_expect_tx(bar, vb + mb);
-            bulk_g2s(dst, a.v_codes + (u * cap + g0) * KB, vb, bar);
-            bulk_g2s(dst + CT * KB, a.v_meta + (u * cap + g0) * 2, mb, bar);
+            bulk_g2s(dst, a.v_codes + row * KB, vb, bar);
+            bulk_g2s(dst + CT * KB, a.v_meta + row * 2, mb, bar);
         }
     }
 
-    __device__ __forceinline__ void advance(const AttendArgs &a, int n_items, int n_splits, int tps, int tpw,
-                                            int warp) {
-        if (++c == 2 * nk) {
-            item += gridDim.x;
-            seek(a, n_items, n_splits, tps, tpw, warp);
-        }
+    __device__ __forceinline__ void advance(int ncu) {
+        if (++idx == 2 * ns) start_sub(f + ns, ncu);
+    }
+
+    // Whether the next chunk holds the unit's newest token (the one the
+    // prep kernel appends).
+    __device__ __forceinline__ bool at_newest(int ncu) const {
+        return f - ubase + (idx < ns ? idx : idx - ns) == ncu - 1;
     }
 };
 
 template <typename T, int BITS, int D>
 __global__ void __launch_bounds__(kNW * 32, 2)
-    decode_stream_kernel(AttendArgs a, int n_splits, int tps, int tpw, int n_items, const uint32_t *__restrict__ qfrag,
+    decode_stream_kernel(AttendArgs a, int ncu, int F, int W, const uint32_t *__restrict__ qfrag,
                          const float *__restrict__ qscal) {
     using GG = WGeo<BITS, D>;
     constexpr int KB = GG::KB, CT = GG::CT;
-    constexpr int EPL = D / 32;
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned char *slots = smem + warp * 2 * GG::SLOT;                              // this warp's 2 slots
-    float *scw_all = reinterpret_cast<float *>(smem + kNW * 2 * GG::SLOT);          // [kNW][4][kScStride]
-    float *scw = scw_all + warp * GG::SCW;                                          // s' scores, then merge area
-    uint32_t *tile = reinterpret_cast<uint32_t *>(scw_all + kNW * GG::SCW) + warp * 12 * kTileW;
-    float *rlz = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(scw_all + kNW * GG::SCW) + kNW * 12 * kTileW);
-    int *s_flag = reinterpret_cast<int *>(rlz + kNW * 4 * 3);                       // [1] failure
-    uint64_t *bars = reinterpret_cast<uint64_t *>(rlz + 128);                      // [kNW][2]
+    float *scw = reinterpret_cast<float *>(smem + kNW * 2 * GG::SLOT) + warp * GG::SCW;  // scores of the sub-segment
+    uint32_t *tile = reinterpret_cast<uint32_t *>(smem + kNW * 2 * GG::SLOT + kNW * GG::SCW * 4) +
+                     warp * 12 * kTileW;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kNW * 2 * GG::SLOT + kNW * GG::SCW * 4 +
+                                                  kNW * 12 * kTileW * 4);  // [kNW][2]
     uint64_t *mybar = bars + 2 * warp;
+    // issue cursor of this warp's chunk schedule: used by lane 0 only, kept out of registers
+    ChunkStream<BITS, D> *cs = reinterpret_cast<ChunkStream<BITS, D> *>(bars + 2 * kNW) + warp;
 
     const int G = a.group;
     const int r = lane >> 2, q = lane & 3;
     const int ph = lane >> 3, tq = lane & 7;  // P-digit role: head ph, token quad tq of a 32-token step
     const bool my_head = q < G;
+    const bool lo = lane < 16;                // value sums: lanes < 16 keep even n-tiles, the rest odd ones
 
     if (tid == 0) {
         for (int i = 0; i < 2 * kNW; i++) mbar_init(bars + i, 1);
-        s_flag[0] = 0;
-        s_flag[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    __syncthreads();
+    __syncthreads();  // the only block-wide barrier: warps are independent from here on
+    const int w = blockIdx.x * kNW + warp;
+    if (w >= W) return;
+    const int f0 = (int)((int64_t)w * F / W), f1 = (int)((int64_t)(w + 1) * F / W);
+    const int total = (int)a.pos0 + 1;
 
-    WarpStream<BITS, D> ws;
+    // The merge kernel may launch now (it waits for this grid).  Chunks of
+    // tokens older than the appended one are fetched before waiting for the
+    // prep kernel; the q digits and the newest token only after.
+    griddep_launch_dependents();
     if (lane == 0) {
-        ws.item = blockIdx.x;
-        ws.seek(a, n_items, n_splits, tps, tpw, warp);
-        for (int k = 0; k < 2 && ws.item < n_items; k++) {
-            ws.issue(a, slots + k * GG::SLOT, mybar + k);
-            ws.advance(a, n_items, n_splits, tps, tpw, warp);
+        cs->f_end = f1;
+        cs->done = 0;
+        cs->n_issued = 0;
+        cs->start_sub(f0, ncu);
+        while (cs->n_issued < 2 && !cs->done && !cs->at_newest(ncu)) {
+            cs->issue(a, total, slots + cs->n_issued * GG::SLOT, mybar + cs->n_issued);
+            cs->advance(ncu);
+            cs->n_issued++;
+        }
+    }
+    griddep_wait();
+    if (lane == 0) {
+        while (cs->n_issued < 2 && !cs->done) {
+            cs->issue(a, total, slots + cs->n_issued * GG::SLOT, mybar + cs->n_issued);
+            cs->advance(ncu);
+            cs->n_issued++;
         }
     }
 
     int j = 0;  // chunks consumed by this warp
     bool failed = false;
-    // wait for chunk j; afterwards lane 0 refills its slot with the chunk two ahead
+    int failed_at = 0;
+    // wait for chunk j (warp-uniform outcome); afterwards lane 0 refills its
+    // slot with the chunk two ahead
     auto wait_chunk = [&](int jj) {
-        if (!failed && !mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1))) {
+        if (failed) return;
+        const bool ok = mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
+        if (__any_sync(0xffffffffu, !ok)) {
             failed = true;
-            atomicOr(a.dev_status, 1);
-            s_flag[1] = 1;
+            failed_at = jj;
+            if (lane == 0) atomicOr(a.dev_status, 1);
         }
     };
     auto release_chunk = [&](int jj) {
         __syncwarp();
-        if (lane == 0 && ws.item < n_items) {
+        if (lane == 0 && !failed && !cs->done) {
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            ws.issue(a, slots + (jj & 1) * GG::SLOT, mybar + (jj & 1));
-            ws.advance(a, n_items, n_splits, tps, tpw, warp);
+            cs->issue(a, total, slots + (jj & 1) * GG::SLOT, mybar + (jj & 1));
+            cs->advance(ncu);
+            cs->n_issued++;
         }
     };
 
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const ItemGeo ig = item_geo(a, item, n_splits, tps);
-        const int n_w = warp_tokens(ig.n_tok, warp, tpw);
-        const int nk = (n_w + CT - 1) / CT;
-        float Rp = -INFINITY, Lp = 0.0f, Zp = 0.0f;
-        int pacc[GG::NTV][4];
+    for (int f = f0; f < f1;) {
+        const int u = f / ncu, ubase = u * ncu;
+        const int seg_end = min(f1, ubase + ncu);
+        const float c1 = qscal[(int64_t)u * 8 + q], c2 = qscal[(int64_t)u * 8 + 4 + q];
+        float Rr = -INFINITY, Lr = 0.0f, Zr = 0.0f;  // head ph: reference R, sum 2^(s-R), sum 2^(s-R)*vzp
+        float facc[GG::NF];                           // head (lane>>2)&3: value sums in the frame of Rr
 #pragma unroll
-        for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
+        for (int k = 0; k < GG::NF; k++) facc[k] = 0.0f;
 
-        if (n_w > 0) {
-            uint32_t bq[GG::QW];
+        for (int fs = f; fs < seg_end;) {
+            const int ns = min(seg_end - fs, GG::SUB);
+            const int n_w = min(total - (fs - ubase) * CT, ns * CT);  // tokens in the sub-segment
+
+            // ---------------- phase 1: scores ----------------
+            float rmax = -INFINITY, vmax = 0.0f;  // max score of head q, max vscale
             {
-                const uint4 *src = reinterpret_cast<const uint4 *>(qfrag + (ig.u * 32 + lane) * GG::QW);
+                uint32_t bq[GG::QW];
+                const uint4 *src = reinterpret_cast<const uint4 *>(qfrag + ((int64_t)u * 32 + lane) * GG::QW);
 #pragma unroll
                 for (int v = 0; v < GG::QW / 4; v++) {
                     const uint4 x = src[v];
@@ -424,86 +461,100 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                     bq[4 * v + 2] = x.z;
                     bq[4 * v + 3] = x.w;
                 }
-            }
-            const float c1 = qscal[ig.u * 8 + q], c2 = qscal[ig.u * 8 + 4 + q];
-
-            // ---------------- phase 1: scores s' = s + log2(vscale) ----------------
-            float rmax = -INFINITY;
-            for (int cc = 0; cc < nk; cc++, j++) {
-                wait_chunk(j);
-                const unsigned char *st = slots + (j & 1) * GG::SLOT;
-                const float *kms = reinterpret_cast<const float *>(st + CT * KB);
-                const float *vms = kms + 2 * CT;
+                for (int cc = 0; cc < ns; cc++, j++) {
+                    wait_chunk(j);
+                    const unsigned char *st = slots + (j & 1) * GG::SLOT;
+                    const float *kms = reinterpret_cast<const float *>(st + CT * KB);
+                    const float *vms = kms + 2 * CT;
 #pragma unroll
-                for (int mt = 0; mt < CT / 16; mt++) {
-                    uint32_t w[2][GG::SEGW];
+                    for (int mt = 0; mt < CT / 16; mt++) {
+                        uint32_t wv[2][GG::SEGW];
 #pragma unroll
-                    for (int hf = 0; hf < 2; hf++) {
-                        const unsigned char *p = st + (16 * mt + r + 8 * hf) * KB + q * (KB / 4);
-                        if constexpr (GG::SEGW == 2) {
-                            const uint2 x = *reinterpret_cast<const uint2 *>(p);
-                            w[hf][0] = x.x;
-                            w[hf][1] = x.y;
-                        } else {
+                        for (int hf = 0; hf < 2; hf++) {
+                            const unsigned char *p = st + (16 * mt + r + 8 * hf) * KB + q * (KB / 4);
+                            if constexpr (GG::SEGW == 2) {
+                                const uint2 x = *reinterpret_cast<const uint2 *>(p);
+                                wv[hf][0] = x.x;
+                                wv[hf][1] = x.y;
+                            } else {
 #pragma unroll
-                            for (int v = 0; v < GG::SEGW / 4; v++) {
-                                const uint4 x = reinterpret_cast<const uint4 *>(p)[v];
-                                w[hf][4 * v] = x.x;
-                                w[hf][4 * v + 1] = x.y;
-                                w[hf][4 * v + 2] = x.z;
-                                w[hf][4 * v + 3] = x.w;
+                                for (int v = 0; v < GG::SEGW / 4; v++) {
+                                    const uint4 x = reinterpret_cast<const uint4 *>(p)[v];
+                                    wv[hf][4 * v] = x.x;
+                                    wv[hf][4 * v + 1] = x.y;
+                                    wv[hf][4 * v + 2] = x.z;
+                                    wv[hf][4 * v + 3] = x.w;
+                                }
+                            }
+                        }
+                        int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+                        for (int k = 0; k < GG::NCH; k++) {
+                            uint32_t a0, a1, a2, a3;
+                            if constexpr (BITS == 4) {
+                                a0 = wv[0][k] & 0x0F0F0F0Fu;
+                                a1 = wv[1][k] & 0x0F0F0F0Fu;
+                                a2 = (wv[0][k] >> 4) & 0x0F0F0F0Fu;
+                                a3 = (wv[1][k] >> 4) & 0x0F0F0F0Fu;
+                            } else {
+                                a0 = wv[0][2 * k];
+                                a1 = wv[1][2 * k];
+                                a2 = wv[0][2 * k + 1];
+                                a3 = wv[1][2 * k + 1];
+                            }
+                            mma_u8s8(acc[0], a0, a1, a2, a3, bq[k * 4 + 0], bq[k * 4 + 1]);
+                            mma_u8s8(acc[1], a0, a1, a2, a3, bq[k * 4 + 2], bq[k * 4 + 3]);
+                        }
+#pragma unroll
+                        for (int hf = 0; hf < 2; hf++) {
+                            const int row = 16 * mt + r + 8 * hf;  // token within the chunk
+                            const int tl = cc * CT + row;          // token within the sub-segment
+                            const float dot = fmaf((float)acc[0][2 * hf], 65536.0f,
+                                                   (float)(acc[0][2 * hf + 1] * 256 + acc[1][2 * hf]));
+                            const float2 km = *reinterpret_cast<const float2 *>(kms + 2 * row);
+                            const float s = fmaf(km.x * c1, dot, km.y * c2);
+                            if (tl < n_w) {
+                                vmax = fmaxf(vmax, vms[2 * row]);
+                                if (my_head) {
+                                    scw[q * kScStride + tl] = s;
+                                    rmax = fmaxf(rmax, s);
+                                }
                             }
                         }
                     }
-                    int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-#pragma unroll
-                    for (int k = 0; k < GG::NCH; k++) {
-                        uint32_t a0, a1, a2, a3;
-                        if constexpr (BITS == 4) {
-                            a0 = w[0][k] & 0x0F0F0F0Fu;
-                            a1 = w[1][k] & 0x0F0F0F0Fu;
-                            a2 = (w[0][k] >> 4) & 0x0F0F0F0Fu;
-                            a3 = (w[1][k] >> 4) & 0x0F0F0F0Fu;
-                        } else {
-                            a0 = w[0][2 * k];
-                            a1 = w[1][2 * k];
-                            a2 = w[0][2 * k + 1];
-                            a3 = w[1][2 * k + 1];
-                        }
-                        mma_u8s8(acc[0], a0, a1, a2, a3, bq[k * 4 + 0], bq[k * 4 + 1]);
-                        mma_u8s8(acc[1], a0, a1, a2, a3, bq[k * 4 + 2], bq[k * 4 + 3]);
-                    }
-#pragma unroll
-                    for (int hf = 0; hf < 2; hf++) {
-                        const int row = 16 * mt + r + 8 * hf;  // token within the chunk
-                        const int tl = cc * CT + row;          // token within the warp's range
-                        const float dot = fmaf((float)acc[0][2 * hf], 65536.0f,
-                                               (float)(acc[0][2 * hf + 1] * 256 + acc[1][2 * hf]));
-                        const float2 km = *reinterpret_cast<const float2 *>(kms + 2 * row);
-                        const float s = fmaf(km.x * c1, dot, km.y * c2);
-                        const float sp = s + __log2f(vms[2 * row]);
-                        if (tl < n_w && my_head) {
-                            scw[q * kScStride + tl] = sp;
-                            rmax = fmaxf(rmax, fmaxf(s, sp));
-                        }
-                    }
+                    release_chunk(j);
                 }
-                release_chunk(j);
             }
-            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 4));
-            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 8));
-            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 16));
-            Rp = __shfl_sync(0xffffffffu, rmax, ph);  // lane ph holds head ph's max
+#pragma unroll
+            for (int m = 4; m < 32; m <<= 1) {
+                rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, m));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, m));
+            }
+            // new reference of head ph (lane ph holds head ph's max; u = 2^(s - R) * vscale <= 1)
+            // and the factor that moves earlier sums to it
+            const float Rp = fmaxf(Rr, __shfl_sync(0xffffffffu, rmax, ph) + __log2f(vmax));
+            const float fac = (Rr == -INFINITY) ? 0.0f : exp2f(Rr - Rp);
+            Rr = Rp;
+            Lr *= fac;
+            Zr *= fac;
+            {
+                const float fh = __shfl_sync(0xffffffffu, fac, 8 * ((lane >> 2) & 3));
+#pragma unroll
+                for (int k = 0; k < GG::NF; k++) facc[k] *= fh;
+            }
 
             // ---------------- phase 2: values ----------------
-            for (int cc = 0; cc < nk; cc++, j++) {
+            int pacc[GG::NTV][4];
+#pragma unroll
+            for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
+            for (int cc = 0; cc < ns; cc++, j++) {
                 wait_chunk(j);
                 const unsigned char *st = slots + (j & 1) * GG::SLOT;
                 const float *vms = reinterpret_cast<const float *>(st + CT * KB);
 #pragma unroll
                 for (int sp = 0; sp < CT / 32; sp++) {
                     const int tc = 32 * sp + 4 * tq;  // this lane's first token within the chunk
-                    const int tb = cc * CT + tc;      // ... within the warp's range
+                    const int tb = cc * CT + tc;      // ... within the sub-segment
                     uint32_t U[4] = {0u, 0u, 0u, 0u};
                     if (ph < G && tb < n_w) {
                         const float4 s4 = *reinterpret_cast<const float4 *>(scw + ph * kScStride + tb);
@@ -514,11 +565,10 @@ __global__ void __launch_bounds__(kNW * 32, 2)
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
                             if (tb + e < n_w) {
-                                const float u = fminf(ex2_approx(sv[e] - Rp), 1.0f);
-                                const float iv = __frcp_rn(vs[e]);
-                                Lp = fmaf(u, iv, Lp);
-                                Zp = fmaf(u, vz[e] * iv, Zp);
-                                U[e] = __float2uint_rn(u * kUMax);
+                                const float ee = ex2_approx(sv[e] - Rp);  // 2^(s - R)
+                                Lr += ee;
+                                Zr = fmaf(ee, vz[e], Zr);
+                                U[e] = __float2uint_rn(fminf(ee * vs[e], 1.0f) * kUMax);
                             }
                         }
                     }
@@ -545,8 +595,9 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                         for (int jj = 0; jj < 4; jj++) {
                             const int i = 4 * v + jj;
                             if constexpr (BITS == 4) {
-                                // high nibbles used in place (16 * code): n-tile 2i+1 sums 16x, scaled at the end
-                                mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj] & 0x0F0F0F0Fu, y1[jj] & 0x0F0F0F0Fu);
+                                // n-tile 2i sums the raw bytes (lo + 16 hi), n-tile 2i+1 the high
+                                // nibbles in place (16 hi); the fold separates them
+                                mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
                                 mma_u8u8(pacc[2 * i + 1], pa0, pa1, pa2, pa3, y0[jj] & 0xF0F0F0F0u,
                                          y1[jj] & 0xF0F0F0F0u);
                             } else {
@@ -557,107 +608,139 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                 }
                 release_chunk(j);
             }
+
+            // ---------------- fold the digit sums into the float sums ----------------
+            // Accumulator rows: r < 4 -> (digit 0, head r) in c0/c1 and (digit 2,
+            // head r) in c2/c3; r >= 4 -> (digit 1, head r - 4) in c0/c1.  value =
+            // (d0*2^16 + d1*2^8 + d2) / (2^24 - 1).  Lanes L and L^16 hold the
+            // pieces of the same (head, column): each keeps one n-tile of every
+            // pair and sends the other's piece across.
+            {
+                const float w_a = lo ? 65536.0f / kUMax : 256.0f / kUMax;
+                const float w_d2 = 1.0f / kUMax;
+                const float ntw = (BITS == 4 && !lo) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
+#pragma unroll
+                for (int np = 0; np < GG::NTV / 2; np++) {
+                    if constexpr (BITS == 4) {
+#pragma unroll
+                        for (int x = 0; x < 4; x++) pacc[2 * np][x] -= pacc[2 * np + 1][x];  // low nibbles
+                    }
+#pragma unroll
+                    for (int cc = 0; cc < 2; cc++) {
+                        float fe = (float)pacc[2 * np][cc] * w_a, fo = (float)pacc[2 * np + 1][cc] * w_a;
+                        if (lo) {
+                            fe = fmaf((float)pacc[2 * np][2 + cc], w_d2, fe);
+                            fo = fmaf((float)pacc[2 * np + 1][2 + cc], w_d2, fo);
+                        }
+                        const float recv = __shfl_xor_sync(0xffffffffu, lo ? fo : fe, 16);
+                        facc[2 * np + cc] = fmaf((lo ? fe : fo) + recv, ntw, facc[2 * np + cc]);
+                    }
+                }
+            }
+            fs += ns;
         }
 
-        // ---------------- warp partial -> its merge area ----------------
-        Lp += __shfl_xor_sync(0xffffffffu, Lp, 1);
-        Lp += __shfl_xor_sync(0xffffffffu, Lp, 2);
-        Lp += __shfl_xor_sync(0xffffffffu, Lp, 4);
-        Zp += __shfl_xor_sync(0xffffffffu, Zp, 1);
-        Zp += __shfl_xor_sync(0xffffffffu, Zp, 2);
-        Zp += __shfl_xor_sync(0xffffffffu, Zp, 4);
-        __syncwarp();  // scw (scores) becomes the merge area
-        {
-            // rows: r < 4 -> (digit 0, head r) in c0/c1 and (digit 2, head r) in c2/c3;
-            // r >= 4 -> (digit 1, head r - 4) in c0/c1.  value = (d0*2^16 + d1*2^8 + d2) / (2^24 - 1).
-            // Lanes r < 4 store head r's value of column 2q+cc of n-tile nt at
-            // (nt*2 + cc)*16 + lane: 16 consecutive words per store, no bank conflicts.
-            const float w_lo = (r < 4) ? 65536.0f / kUMax : 256.0f / kUMax;
-            const float w_d2 = 1.0f / kUMax;
+        // ---------------- the unit's partial record ----------------
+        Lr += __shfl_xor_sync(0xffffffffu, Lr, 1);
+        Lr += __shfl_xor_sync(0xffffffffu, Lr, 2);
+        Lr += __shfl_xor_sync(0xffffffffu, Lr, 4);
+        Zr += __shfl_xor_sync(0xffffffffu, Zr, 1);
+        Zr += __shfl_xor_sync(0xffffffffu, Zr, 2);
+        Zr += __shfl_xor_sync(0xffffffffu, Zr, 4);
+        if (!failed) {
+            // record: value sums [head][dim], then R, L, Z of the four heads
+            float *rec = a.workspace + (int64_t)(w + u) * GG::REC;
+            const int hr = (lane >> 2) & 3;
+            if (hr < G) {
 #pragma unroll
-            for (int nt = 0; nt < GG::NTV; nt++) {
-                const float ntw = (BITS == 4 && (nt & 1)) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
-#pragma unroll
-                for (int cc = 0; cc < 2; cc++) {
-                    float f = (float)pacc[nt][cc] * w_lo;
-                    if (r < 4) f = fmaf((float)pacc[nt][2 + cc], w_d2, f);
-                    const float mid = __shfl_down_sync(0xffffffffu, f, 16);
-                    if (r < 4) scw[(nt * 2 + cc) * 16 + lane] = (f + mid) * ntw;
-                }
+                for (int k = 0; k < GG::NF; k++)
+                    rec[hr * D + v_dim<BITS, D>(2 * (k >> 1) + (lo ? 0 : 1), 2 * q + (k & 1))] = facc[k];
+            }
+            if (tq == 0) {
+                rec[4 * D + ph] = ph < G ? Rr : -INFINITY;
+                rec[4 * D + 4 + ph] = Lr;
+                rec[4 * D + 8 + ph] = Zr;
             }
         }
-        if (tq == 0) {
-            rlz[(warp * 4 + ph) * 3 + 0] = (n_w > 0 && ph < G) ? Rp : -INFINITY;
-            rlz[(warp * 4 + ph) * 3 + 1] = Lp;
-            rlz[(warp * 4 + ph) * 3 + 2] = Zp;
-        }
-        __syncthreads();
-
-        // ---------------- merge the warps: warp g finishes head g ----------------
-        // Splits are merged afterwards by attend_combine_kernel.
-        const bool fail_now = *reinterpret_cast<volatile int *>(&s_flag[1]) != 0;
-        if (warp < G && !fail_now) {
-            const int g = warp;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w2 = 0; w2 < kNW; w2++) M = fmaxf(M, rlz[(w2 * 4 + g) * 3]);
-            int idx[EPL];
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) {
-                int nt, col;
-                v_inv<BITS, D>(lane * EPL + rr, nt, col);
-                idx[rr] = (nt * 2 + (col & 1)) * 16 + 4 * g + (col >> 1);
-            }
-            float L = 0.0f, Z = 0.0f, x[EPL];
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
-#pragma unroll
-            for (int w2 = 0; w2 < kNW; w2++) {
-                const float Rw = rlz[(w2 * 4 + g) * 3];
-                if (Rw == -INFINITY) continue;
-                const float wt = exp2f(Rw - M);
-                L = fmaf(wt, rlz[(w2 * 4 + g) * 3 + 1], L);
-                Z = fmaf(wt, rlz[(w2 * 4 + g) * 3 + 2], Z);
-                const float *mw = scw_all + w2 * GG::SCW;
-#pragma unroll
-                for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wt, mw[idx[rr]], x[rr]);
-            }
-            if (n_splits == 1) {
-                const float *sg = a.signs + (int64_t)ig.h * D;
-                const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-#pragma unroll
-                for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
-                warp_wht_butterfly<EPL>(x, lane, D);
-                T *dst = static_cast<T *>(a.out) + ((int64_t)ig.b * a.heads * G + ig.h * G + g) * D;
-#pragma unroll
-                for (int rr = 0; rr < EPL; rr++)
-                    st_from_f32(dst + lane * EPL + rr, x[rr] * a.wht_scale * sg[lane * EPL + rr]);
-            } else {
-                float *wsp = a.workspace + ((ig.u * n_splits + ig.split) * G + g) * (D + 4);
-                if (EPL == 4) {
-                    *reinterpret_cast<float4 *>(wsp + lane * 4) = make_float4(x[0], x[1 % EPL], x[2 % EPL], x[3 % EPL]);
-                } else {
-#pragma unroll
-                    for (int rr = 0; rr < EPL; rr++) wsp[lane * EPL + rr] = x[rr];
-                }
-                if (lane == 0) {
-                    wsp[D] = M;
-                    wsp[D + 1] = L;
-                    wsp[D + 2] = Z;
-                }
-            }
-        }
-        __syncthreads();  // merge areas and flags are reused by the next item
+        f = seg_end;
     }
 
     if (failed && lane == 0) {
-        // a wait gave up: let the (at most two) copies this warp still has in flight land (bounded)
-        for (int jj = j; jj < j + 2; jj++) mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
+        // a wait gave up and no copy was issued since: let this warp's copies still in flight land (bounded)
+        for (int jj = failed_at; jj < cs->n_issued; jj++) mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
     }
 }
 
+// Merge of each unit's partial records (one warp per query head), then
+// normalisation, inverse rotation and the store.
 template <typename T, int BITS, int D>
-int launch_shape(const AttendArgs &a, const AppendArgs *ap, int n_splits, int tps, cudaStream_t stream) {
+__global__ void __launch_bounds__(128) decode_merge_kernel(AttendArgs a, int ncu, int F, int W) {
+    using GG = WGeo<BITS, D>;
+    constexpr int EPL = D / 32;
+    const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+    griddep_wait();  // the decode grid's records
+    if (g >= a.group) return;
+    const int u = blockIdx.x;
+    const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
+    const float *base = a.workspace + (int64_t)u * GG::REC;  // record w + u
+    float M = -INFINITY;
+    for (int w = w_lo; w <= w_hi; w++) M = fmaxf(M, base[(int64_t)w * GG::REC + 4 * D + g]);
+    float x[EPL], L = 0.0f, Z = 0.0f;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
+    for (int w = w_lo; w <= w_hi; w++) {
+        const float *rec = base + (int64_t)w * GG::REC;
+        const float Rw = rec[4 * D + g];
+        if (Rw == -INFINITY) continue;
+        const float wt = exp2f(Rw - M);
+        L = fmaf(wt, rec[4 * D + 4 + g], L);
+        Z = fmaf(wt, rec[4 * D + 8 + g], Z);
+        float v[EPL];
+        if constexpr (EPL == 4) {
+            const float4 t = *reinterpret_cast<const float4 *>(rec + g * D + lane * 4);
+            v[0] = t.x;
+            v[1 % EPL] = t.y;
+            v[2 % EPL] = t.z;
+            v[3 % EPL] = t.w;
+        } else {
+            const float2 t = *reinterpret_cast<const float2 *>(rec + g * D + lane * 2);
+            v[0] = t.x;
+            v[1 % EPL] = t.y;
+        }
+#pragma unroll
+        for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wt, v[rr], x[rr]);
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
+    warp_wht_butterfly<EPL>(x, lane, D);
+    const int h = u % a.heads;
+    const float *sg = a.signs + (int64_t)h * D;
+    T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++)
+        st_from_f32(dst + lane * EPL + rr, x[rr] * a.wht_scale * sg[lane * EPL + rr]);
+}
+
+// Grid of the decode kernel: two CTAs per SM, no more warps than chunks.
+struct DecodeGrid {
+    int ncu, F, W, ctas;
+};
+
+template <int BITS, int D>
+DecodeGrid decode_grid(const AttendArgs &a) {
+    using GG = WGeo<BITS, D>;
+    DecodeGrid g;
+    const int64_t total = a.pos0 + 1;
+    g.ncu = (int)((total + GG::CT - 1) / GG::CT);
+    g.F = a.batch * a.heads * g.ncu;  // fits int: decode_fast_eligible bounds it
+    g.W = min(2 * a.sm_count * kNW, g.F);
+    g.ctas = (g.W + kNW - 1) / kNW;
+    return g;
+}
+
+template <typename T, int BITS, int D>
+int launch_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream) {
     uint32_t *qfrag = a.qprep;
     float *qscal = reinterpret_cast<float *>(a.qprep + (size_t)a.batch * a.heads * 32 * 16);
     const int do_append = ap != nullptr;
@@ -681,60 +764,64 @@ int launch_shape(const AttendArgs &a, const AppendArgs *ap, int n_splits, int tp
         if (e != cudaSuccess) return check_cuda(e, "gqa decode smem attribute");
         if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
     }
-    const int n_items = a.batch * a.heads * n_splits;
-    int grid = 2 * a.sm_count;
-    if (grid > n_items) grid = n_items;
-    const int tpw = tps / kNW;
-    kern<<<grid, kNW * 32, smem, stream>>>(a, n_splits, tps, tpw, n_items, qfrag, qscal);
+    const DecodeGrid dg = decode_grid<BITS, D>(a);
+    // decode and merge are launched as programmatic dependents of the kernel
+    // before them, so their launch overlaps its tail
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)dg.ctas);
+    cfg.blockDim = dim3(kNW * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    rc = check_cuda(cudaLaunchKernelEx(&cfg, kern, a, dg.ncu, dg.F, dg.W, (const uint32_t *)qfrag, (const float *)qscal),
+                    "gqa decode launch");
     count_launch();
-    int rc2 = check_cuda(cudaGetLastError(), "gqa decode launch");
-    if (rc2 != SA_OK || n_splits == 1) return rc2;
-    return launch_gqa_combine(a, n_splits, stream);
+    if (rc != SA_OK) return rc;
+    cfg.gridDim = dim3((unsigned)(a.batch * a.heads));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    rc = check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, BITS, D>, a, dg.ncu, dg.F, dg.W),
+                    "gqa decode merge launch");
+    count_launch();
+    return rc;
 }
 
 template <typename T>
-int launch_dtype(const AttendArgs &a, const AppendArgs *ap, int n_splits, int tps, cudaStream_t stream) {
-    if (a.bits == 4 && a.head_dim == 128) return launch_shape<T, 4, 128>(a, ap, n_splits, tps, stream);
-    if (a.bits == 8 && a.head_dim == 128) return launch_shape<T, 8, 128>(a, ap, n_splits, tps, stream);
-    if (a.bits == 4 && a.head_dim == 64) return launch_shape<T, 4, 64>(a, ap, n_splits, tps, stream);
-    return launch_shape<T, 8, 64>(a, ap, n_splits, tps, stream);
+int launch_dtype(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream) {
+    if (a.bits == 4 && a.head_dim == 128) return launch_shape<T, 4, 128>(a, ap, stream);
+    if (a.bits == 8 && a.head_dim == 128) return launch_shape<T, 8, 128>(a, ap, stream);
+    if (a.bits == 4 && a.head_dim == 64) return launch_shape<T, 4, 64>(a, ap, stream);
+    return launch_shape<T, 8, 64>(a, ap, stream);
 }
 
 }  // namespace
+
+// Floats of partial records the decode needs: one per warp of the grid plus
+// one per unit (a warp's range touches one unit more than it crosses).
+size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim) {
+    return (size_t)((int64_t)2 * sm_count * kNW + units) * (size_t)(4 * head_dim + 16);
+}
 
 // Whether the tensor-core decode handles this call.
 bool decode_fast_eligible(const AttendArgs &a) {
     if (a.seq_len != 1 || a.group < 1 || a.group > 4) return false;
     if ((a.bits != 4 && a.bits != 8) || (a.head_dim != 64 && a.head_dim != 128)) return false;
-    if (a.capacity % 64 != 0 || a.qprep == nullptr || a.dev_status == nullptr)
-        return false;
-    const int64_t total = a.pos0 + 1;
-    if (total > (int64_t)kMaxSplits * kNW * kTPW) return false;
-    // every split's partial must fit the workspace
+    if (a.capacity % 64 != 0 || a.qprep == nullptr || a.dev_status == nullptr) return false;
     const int64_t units = (int64_t)a.batch * a.heads;
-    return (size_t)((int64_t)kMaxSplits * units * a.group * (a.head_dim + 4)) <= a.workspace_floats;
+    if (units * ((a.pos0 + 32) / 32) >= ((int64_t)1 << 31)) return false;  // flat chunk indices are int
+    return decode_workspace_floats(a.sm_count, units, a.head_dim) <= a.workspace_floats;
 }
 
-// Prep (+ append when `ap` is given) and decode of one query token per row.
+// Prep (+ append when `ap` is given), decode and merge of one query token per row.
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream) {
-    const int64_t total = a.pos0 + 1;
-    const int64_t units = (int64_t)a.batch * a.heads;
-    // splits: at most kNW * kTPW tokens each, a multiple of kNW * 64 (whole
-    // chunks per warp); enough work items for ~8 per persistent CTA.
-    const int64_t grain = (int64_t)kNW * 64, cap_tok = (int64_t)kNW * kTPW;
-    int64_t n = (total + cap_tok - 1) / cap_tok;
-    const int64_t want = (16LL * a.sm_count + units - 1) / units;
-    const int64_t by_len = (total + grain - 1) / grain;
-    const int64_t more = want < by_len ? want : by_len;
-    if (n < more) n = more;
-    if (n > kMaxSplits) n = kMaxSplits;
-    int64_t tps = (total + n - 1) / n;
-    tps = (tps + grain - 1) / grain * grain;
-    n = (total + tps - 1) / tps;
     switch (a.dtype) {
-        case SA_DTYPE_FLOAT: return launch_dtype<float>(a, ap, (int)n, (int)tps, stream);
-        case SA_DTYPE_FLOAT16: return launch_dtype<__half>(a, ap, (int)n, (int)tps, stream);
-        default: return launch_dtype<__nv_bfloat16>(a, ap, (int)n, (int)tps, stream);
+        case SA_DTYPE_FLOAT: return launch_dtype<float>(a, ap, stream);
+        case SA_DTYPE_FLOAT16: return launch_dtype<__half>(a, ap, stream);
+        default: return launch_dtype<__nv_bfloat16>(a, ap, stream);
     }
 }
 

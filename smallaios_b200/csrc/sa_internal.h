@@ -86,6 +86,7 @@ struct AttendArgs {
 int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
 bool decode_fast_eligible(const AttendArgs &a);
+size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim);
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,

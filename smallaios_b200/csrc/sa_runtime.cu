@@ -147,6 +147,8 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->layer_codes_bytes = B * H * T * k->code_bytes;
     k->layer_meta_floats = B * H * T * 2;
     k->workspace_floats = B * H * (size_t)kMaxSplits * k->group * (D + 4);
+    const size_t dec_ws = decode_workspace_floats(k->sm_count, (int64_t)(B * H), (int)D);
+    if (dec_ws > k->workspace_floats) k->workspace_floats = dec_ws;
     auto up = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t codes = up(L * k->layer_codes_bytes);
     const size_t meta = up(L * k->layer_meta_floats * sizeof(float));
@@ -371,7 +373,7 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
     if (rc != SA_OK) return rc;
     sa_kv_layer_view v;
     sa_kv_cache_layer_view(reinterpret_cast<sa_kv_cache *>(k), layer, &v);
-    AttendArgs a;
+    AttendArgs a{};
     a.query = query;
     a.out = attn_out;
     a.dtype = dtype;
