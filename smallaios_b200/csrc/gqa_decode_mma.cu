@@ -64,6 +64,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 
 // The thread sleeps until the phase completes or the hint elapses, so a
 // waiting warp takes no issue slots from the warps that compute.
+// Arrival without data: completes the current phase of a count-1 barrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -265,19 +270,21 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
 // partial record (running max R, sums L and Z, un-normalised value sums) at
 // record index w + u, and decode_merge_kernel merges each unit's records.
 //
-// Inside a unit the warp walks sub-segments of up to kTPW tokens through its
-// own two shared-memory slots: phase 1 streams their K chunks (scores to
-// shared memory), phase 2 their V chunks with the running max as the
-// fixed-point reference; the integer accumulators are folded into float sums
-// after every sub-segment.
-constexpr int kTPW = 128;            // tokens per sub-segment
-constexpr int kScStride = kTPW + 8;  // floats per head row of a warp's score buffer (bank offset)
-
+// Inside a unit the warp walks sub-segments of two chunks through its own two
+// shared-memory slots: slot s holds K chunk s of a sub-segment, then its V
+// chunk s, then K chunk s of the next sub-segment, and so on, so a slot's
+// mbarrier always completes an even phase for a K chunk and an odd phase for
+// a V chunk.  A sub-segment with a single chunk gives slot 1 empty phases (an
+// arrive without data).  Phase 1 computes the scores from the K chunks
+// (kept in shared memory), phase 2 streams the V chunks with the running
+// reference R as the fixed-point frame; the integer accumulators are folded
+// into float sums after every sub-segment.
 template <int BITS, int D>
 struct WGeo {
     static constexpr int KB = D * BITS / 8;             // code bytes per token
     static constexpr int CT = (KB > 64) ? 32 : 64;       // tokens per chunk
-    static constexpr int SUB = kTPW / CT;                // chunks per sub-segment
+    static constexpr int TPW = 2 * CT;                   // tokens per sub-segment
+    static constexpr int SCS = TPW + 8;                  // floats per head row of a warp's score buffer (bank offset)
     static constexpr int SLOT = CT * (KB + 16);          // K chunk: codes + K meta + V meta (a V chunk is smaller)
     static constexpr int SEGW = KB / 16;                 // K words per quad per row
     static constexpr int NCH = D / 32;                   // QK k-chunks
@@ -285,9 +292,9 @@ struct WGeo {
     static constexpr int NF = NTV;                       // float value sums per lane
     static constexpr int VV = ((BITS == 4) ? NTV / 2 : NTV) / 4;  // 16-byte V loads per 16-token block
     static constexpr int QW = NCH * 4;                   // q-digit words per lane
-    static constexpr int SCW = 4 * kScStride;            // floats of a warp's score buffer
+    static constexpr int SCW = 4 * SCS;                  // floats of a warp's score buffer
     static constexpr int REC = 4 * D + 16;               // floats per partial record: [4][D] values, R/L/Z x 4
-    static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 512;
+    static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 256;
 };
 
 // Warp owning flat chunk f when F chunks are cut into W ranges
@@ -296,80 +303,22 @@ __host__ __device__ __forceinline__ int warp_of_chunk(int f, int F, int W) {
     return (int)((((int64_t)f + 1) * W - 1) / F);
 }
 
-// The chunk schedule of one warp: for every sub-segment of its range, the K
-// chunks then the V chunks.  Lane 0 keeps the cursor of the next chunk to
-// issue, two chunks ahead of consumption.
-template <int BITS, int D>
-struct ChunkStream {
-    using GG = WGeo<BITS, D>;
-    int f, f_end, ubase, u;  // sub-segment start (flat chunk), range end, unit's first chunk, unit
-    int ns, idx;             // chunks in the sub-segment, next chunk in its 2*ns schedule
-    int done, n_issued;      // schedule exhausted; chunks issued so far
-
-    __device__ __forceinline__ void start_sub(int fs, int ncu) {
-        if (fs >= f_end) {
-            done = 1;
-            return;
-        }
-        u = fs / ncu;
-        ubase = u * ncu;
-        const int lim = min(f_end, ubase + ncu);
-        ns = min(lim - fs, GG::SUB);
-        f = fs;
-        idx = 0;
-    }
-
-    __device__ __forceinline__ void issue(const AttendArgs &a, int total, unsigned char *dst, uint64_t *bar) const {
-        constexpr int KB = GG::KB, CT = GG::CT;
-        const bool is_k = idx < ns;
-        const int g0 = (f - ubase + (is_k ? idx : idx - ns)) * CT;  // first token, a multiple of CT
-        const int cnt = min(total - g0, CT);
-        const int mcnt = (cnt + 1) & ~1;  // meta rows rounded to even: 16-byte copies
-        const int64_t row = (int64_t)u * a.capacity + g0;
-        const uint32_t mb = (uint32_t)(mcnt * 8);
-        if (is_k) {  // K chunk: codes, K meta, V meta
-            const uint32_t cb = (uint32_t)(cnt * KB);
-            mbar_expect_tx(bar, cb + 2 * mb);
-            bulk_g2s(dst, a.k_codes + row * KB, cb, bar);
-            bulk_g2s(dst + CT * KB, a.k_meta + row * 2, mb, bar);
-            bulk_g2s(dst + CT * KB + CT * 8, a.v_meta + row * 2, mb, bar);
-        } else {  // V chunk: whole 16-token blocks of codes, V meta
-            const uint32_t vb = (uint32_t)(((cnt + kVBlock - 1) / kVBlock) * KB * kVBlock);
-            mbar_expect_tx(bar, vb + mb);
-            bulk_g2s(dst, a.v_codes + row * KB, vb, bar);
-            bulk_g2s(dst + CT * KB, a.v_meta + row * 2, mb, bar);
-        }
-    }
-
-    __device__ __forceinline__ void advance(int ncu) {
-        if (++idx == 2 * ns) start_sub(f + ns, ncu);
-    }
-
-    // Whether the next chunk holds the unit's newest token (the one the
-    // prep kernel appends).
-    __device__ __forceinline__ bool at_newest(int ncu) const {
-        return f - ubase + (idx < ns ? idx : idx - ns) == ncu - 1;
-    }
-};
-
 template <typename T, int BITS, int D>
 __global__ void __launch_bounds__(kNW * 32, 2)
     decode_stream_kernel(AttendArgs a, int ncu, int F, int W, const uint32_t *__restrict__ qfrag,
                          const float *__restrict__ qscal) {
     using GG = WGeo<BITS, D>;
-    constexpr int KB = GG::KB, CT = GG::CT;
+    constexpr int KB = GG::KB, CT = GG::CT, SCS = GG::SCS;
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    unsigned char *slots = smem + warp * 2 * GG::SLOT;                              // this warp's 2 slots
+    unsigned char *slots = smem + warp * 2 * GG::SLOT;                                   // this warp's 2 slots
     float *scw = reinterpret_cast<float *>(smem + kNW * 2 * GG::SLOT) + warp * GG::SCW;  // scores of the sub-segment
     uint32_t *tile = reinterpret_cast<uint32_t *>(smem + kNW * 2 * GG::SLOT + kNW * GG::SCW * 4) +
                      warp * 12 * kTileW;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kNW * 2 * GG::SLOT + kNW * GG::SCW * 4 +
                                                   kNW * 12 * kTileW * 4);  // [kNW][2]
     uint64_t *mybar = bars + 2 * warp;
-    // issue cursor of this warp's chunk schedule: used by lane 0 only, kept out of registers
-    ChunkStream<BITS, D> *cs = reinterpret_cast<ChunkStream<BITS, D> *>(bars + 2 * kNW) + warp;
 
     const int G = a.group;
     const int r = lane >> 2, q = lane & 3;
@@ -382,88 +331,122 @@ __global__ void __launch_bounds__(kNW * 32, 2)
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     __syncthreads();  // the only block-wide barrier: warps are independent from here on
+    // The merge kernel may launch now (it waits for this grid).
+    griddep_launch_dependents();
     const int w = blockIdx.x * kNW + warp;
     if (w >= W) return;
     const int f0 = (int)((int64_t)w * F / W), f1 = (int)((int64_t)(w + 1) * F / W);
     const int total = (int)a.pos0 + 1;
 
-    // The merge kernel may launch now (it waits for this grid).  Chunks of
-    // tokens older than the appended one are fetched before waiting for the
-    // prep kernel; the q digits and the newest token only after.
-    griddep_launch_dependents();
-    if (lane == 0) {
-        cs->f_end = f1;
-        cs->done = 0;
-        cs->n_issued = 0;
-        cs->start_sub(f0, ncu);
-        while (cs->n_issued < 2 && !cs->done && !cs->at_newest(ncu)) {
-            cs->issue(a, total, slots + cs->n_issued * GG::SLOT, mybar + cs->n_issued);
-            cs->advance(ncu);
-            cs->n_issued++;
-        }
-    }
-    griddep_wait();
-    if (lane == 0) {
-        while (cs->n_issued < 2 && !cs->done) {
-            cs->issue(a, total, slots + cs->n_issued * GG::SLOT, mybar + cs->n_issued);
-            cs->advance(ncu);
-            cs->n_issued++;
-        }
-    }
-
-    int j = 0;  // chunks consumed by this warp
+    // Copies of a chunk, one per lane: K chunk = codes (lane 0), K meta
+    // (lane 1), V meta (lane 2); V chunk = codes (lane 0), V meta (lane 1).
+    // `pend` has bit 2*slot + kind (0 = K, 1 = V) set while a phase is issued
+    // and not yet waited for.
+    unsigned pend = 0;
     bool failed = false;
-    int failed_at = 0;
-    // wait for chunk j (warp-uniform outcome); afterwards lane 0 refills its
-    // slot with the chunk two ahead
-    auto wait_chunk = [&](int jj) {
-        if (failed) return;
-        const bool ok = mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
+    auto issue = [&](int s, int uu, int c, int kind) {
+        const int g0 = c * CT;  // first token of the chunk
+        const int cnt = min(total - g0, CT);
+        const uint32_t mb = (uint32_t)(((cnt + 1) & ~1) * 8);  // meta rows rounded to even: 16-byte copies
+        const uint32_t cb = kind == 0 ? (uint32_t)(cnt * KB) : (uint32_t)(((cnt + kVBlock - 1) / kVBlock) * kVBlock * KB);
+        const int64_t row = (int64_t)uu * a.capacity + g0;
+        uint64_t *bar = mybar + s;
+        if (lane == 0) mbar_expect_tx(bar, cb + (kind == 0 ? 2 * mb : mb));
+        if (lane < 3 - kind) {
+            const void *src;
+            uint32_t nb = mb, off;
+            if (lane == 0) {
+                src = (kind == 0 ? a.k_codes : a.v_codes) + row * KB;
+                nb = cb;
+                off = 0;
+            } else if (lane == 1) {
+                src = (kind == 0 ? a.k_meta : a.v_meta) + row * 2;
+                off = CT * KB;
+            } else {
+                src = a.v_meta + row * 2;
+                off = CT * KB + CT * 8;
+            }
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // after the warp's reads of the slot
+            bulk_g2s(slots + s * GG::SLOT + off, src, nb, bar);
+        }
+        pend |= 1u << (2 * s + kind);
+    };
+    auto issue_empty = [&](int s, int kind) {
+        if (lane == 0) mbar_arrive(mybar + s);
+        pend |= 1u << (2 * s + kind);
+    };
+    auto wait = [&](int s, int kind) {
+        const bool ok = mbar_wait_bounded(mybar + s, (uint32_t)kind);
         if (__any_sync(0xffffffffu, !ok)) {
             failed = true;
-            failed_at = jj;
             if (lane == 0) atomicOr(a.dev_status, 1);
-        }
-    };
-    auto release_chunk = [&](int jj) {
-        __syncwarp();
-        if (lane == 0 && !failed && !cs->done) {
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            cs->issue(a, total, slots + (jj & 1) * GG::SLOT, mybar + (jj & 1));
-            cs->advance(ncu);
-            cs->n_issued++;
+        } else {
+            pend &= ~(1u << (2 * s + kind));
         }
     };
 
-    for (int f = f0; f < f1;) {
-        const int u = f / ncu, ubase = u * ncu;
-        const int seg_end = min(f1, ubase + ncu);
-        const float c1 = qscal[(int64_t)u * 8 + q], c2 = qscal[(int64_t)u * 8 + 4 + q];
-        float Rr = -INFINITY, Lr = 0.0f, Zr = 0.0f;  // head ph: reference R, sum 2^(s-R), sum 2^(s-R)*vzp
-        float facc[GG::NF];                           // head (lane>>2)&3: value sums in the frame of Rr
-#pragma unroll
-        for (int k = 0; k < GG::NF; k++) facc[k] = 0.0f;
+    int u = f0 / ncu, ubase = u * ncu, fs = f0;
+    int ns = min(2, min(f1, ubase + ncu) - fs);
+    {
+        // The first K chunks; one that holds the newest token (appended by
+        // the prep kernel) is fetched after waiting for that kernel, the
+        // older ones before.
+        const bool new0 = fs - ubase == ncu - 1, new1 = ns > 1 && fs - ubase + 1 == ncu - 1;
+        if (!new0) issue(0, u, fs - ubase, 0);
+        if (ns < 2) issue_empty(1, 0);
+        else if (!new1) issue(1, u, fs - ubase + 1, 0);
+        griddep_wait();
+        if (new0) issue(0, u, fs - ubase, 0);
+        if (new1) issue(1, u, fs - ubase + 1, 0);
+    }
 
-        for (int fs = f; fs < seg_end;) {
-            const int ns = min(seg_end - fs, GG::SUB);
-            const int n_w = min(total - (fs - ubase) * CT, ns * CT);  // tokens in the sub-segment
-
-            // ---------------- phase 1: scores ----------------
-            float rmax = -INFINITY, vmax = 0.0f;  // max score of head q, max vscale
-            {
-                uint32_t bq[GG::QW];
-                const uint4 *src = reinterpret_cast<const uint4 *>(qfrag + ((int64_t)u * 32 + lane) * GG::QW);
+    float c1 = 0.0f, c2 = 0.0f;
+    float Rr = -INFINITY, Lr = 0.0f, Zr = 0.0f;  // head ph: reference R, sum 2^(s-R), sum 2^(s-R)*vzp
+    float facc[GG::NF];                           // head (lane>>2)&3: value sums in the frame of Rr
+    bool fresh = true;
+    while (!failed) {
+        if (fresh) {  // first sub-segment of a unit
+            c1 = qscal[(int64_t)u * 8 + q];
+            c2 = qscal[(int64_t)u * 8 + 4 + q];
+            Rr = -INFINITY;
+            Lr = 0.0f;
+            Zr = 0.0f;
 #pragma unroll
-                for (int v = 0; v < GG::QW / 4; v++) {
-                    const uint4 x = src[v];
-                    bq[4 * v] = x.x;
-                    bq[4 * v + 1] = x.y;
-                    bq[4 * v + 2] = x.z;
-                    bq[4 * v + 3] = x.w;
-                }
-                for (int cc = 0; cc < ns; cc++, j++) {
-                    wait_chunk(j);
-                    const unsigned char *st = slots + (j & 1) * GG::SLOT;
+            for (int k = 0; k < GG::NF; k++) facc[k] = 0.0f;
+            fresh = false;
+        }
+        // the next sub-segment (nsn = 0: none)
+        const int fn = fs + ns;
+        int un = u, ubn = ubase, nsn = 0;
+        if (fn < f1) {
+            if (fn == ubase + ncu) {
+                un = u + 1;
+                ubn = ubase + ncu;
+            }
+            nsn = min(2, min(f1, ubn + ncu) - fn);
+        }
+        const int c0 = fs - ubase;                           // first chunk within the unit
+        const int n_w = min(total - c0 * CT, ns * CT);       // tokens in the sub-segment
+
+        // ---------------- phase 1: scores ----------------
+        float rmax = -INFINITY, vmax = 0.0f;  // max score of head q, max vscale
+        {
+            uint32_t bq[GG::QW];
+            const uint4 *src = reinterpret_cast<const uint4 *>(qfrag + ((int64_t)u * 32 + lane) * GG::QW);
+#pragma unroll
+            for (int v = 0; v < GG::QW / 4; v++) {
+                const uint4 x = src[v];
+                bq[4 * v] = x.x;
+                bq[4 * v + 1] = x.y;
+                bq[4 * v + 2] = x.z;
+                bq[4 * v + 3] = x.w;
+            }
+#pragma unroll
+            for (int cc = 0; cc < 2; cc++) {
+                wait(cc, 0);
+                if (failed) break;
+                if (cc < ns) {
+                    const unsigned char *st = slots + cc * GG::SLOT;
                     const float *kms = reinterpret_cast<const float *>(st + CT * KB);
                     const float *vms = kms + 2 * CT;
 #pragma unroll
@@ -516,40 +499,47 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                             if (tl < n_w) {
                                 vmax = fmaxf(vmax, vms[2 * row]);
                                 if (my_head) {
-                                    scw[q * kScStride + tl] = s;
+                                    scw[q * SCS + tl] = s;
                                     rmax = fmaxf(rmax, s);
                                 }
                             }
                         }
                     }
-                    release_chunk(j);
                 }
+                __syncwarp();
+                if (cc < ns) issue(cc, u, c0 + cc, 1);
+                else issue_empty(cc, 1);
             }
+        }
+        if (failed) break;
 #pragma unroll
-            for (int m = 4; m < 32; m <<= 1) {
-                rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, m));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, m));
-            }
-            // new reference of head ph (lane ph holds head ph's max; u = 2^(s - R) * vscale <= 1)
-            // and the factor that moves earlier sums to it
-            const float Rp = fmaxf(Rr, __shfl_sync(0xffffffffu, rmax, ph) + __log2f(vmax));
-            const float fac = (Rr == -INFINITY) ? 0.0f : exp2f(Rr - Rp);
-            Rr = Rp;
-            Lr *= fac;
-            Zr *= fac;
-            {
-                const float fh = __shfl_sync(0xffffffffu, fac, 8 * ((lane >> 2) & 3));
+        for (int m = 4; m < 32; m <<= 1) {
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, m));
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, m));
+        }
+        // new reference of head ph (lane ph holds head ph's max; u = 2^(s - R) * vscale <= 1)
+        // and the factor that moves earlier sums to it
+        const float Rp = fmaxf(Rr, __shfl_sync(0xffffffffu, rmax, ph) + __log2f(vmax));
+        const float fac = (Rr == -INFINITY) ? 0.0f : exp2f(Rr - Rp);
+        Rr = Rp;
+        Lr *= fac;
+        Zr *= fac;
+        {
+            const float fh = __shfl_sync(0xffffffffu, fac, 8 * ((lane >> 2) & 3));
 #pragma unroll
-                for (int k = 0; k < GG::NF; k++) facc[k] *= fh;
-            }
+            for (int k = 0; k < GG::NF; k++) facc[k] *= fh;
+        }
 
-            // ---------------- phase 2: values ----------------
-            int pacc[GG::NTV][4];
+        // ---------------- phase 2: values ----------------
+        int pacc[GG::NTV][4];
 #pragma unroll
-            for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
-            for (int cc = 0; cc < ns; cc++, j++) {
-                wait_chunk(j);
-                const unsigned char *st = slots + (j & 1) * GG::SLOT;
+        for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            wait(cc, 1);
+            if (failed) break;
+            if (cc < ns) {
+                const unsigned char *st = slots + cc * GG::SLOT;
                 const float *vms = reinterpret_cast<const float *>(st + CT * KB);
 #pragma unroll
                 for (int sp = 0; sp < CT / 32; sp++) {
@@ -557,7 +547,7 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                     const int tb = cc * CT + tc;      // ... within the sub-segment
                     uint32_t U[4] = {0u, 0u, 0u, 0u};
                     if (ph < G && tb < n_w) {
-                        const float4 s4 = *reinterpret_cast<const float4 *>(scw + ph * kScStride + tb);
+                        const float4 s4 = *reinterpret_cast<const float4 *>(scw + ph * SCS + tb);
                         const float4 m01 = *reinterpret_cast<const float4 *>(vms + 2 * tc);
                         const float4 m23 = *reinterpret_cast<const float4 *>(vms + 2 * tc + 4);
                         const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -606,68 +596,79 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                         }
                     }
                 }
-                release_chunk(j);
             }
+            __syncwarp();
+            if (nsn > 0) {
+                if (cc < nsn) issue(cc, un, fn - ubn + cc, 0);
+                else issue_empty(cc, 0);
+            }
+        }
+        if (failed) break;
 
-            // ---------------- fold the digit sums into the float sums ----------------
-            // Accumulator rows: r < 4 -> (digit 0, head r) in c0/c1 and (digit 2,
-            // head r) in c2/c3; r >= 4 -> (digit 1, head r - 4) in c0/c1.  value =
-            // (d0*2^16 + d1*2^8 + d2) / (2^24 - 1).  Lanes L and L^16 hold the
-            // pieces of the same (head, column): each keeps one n-tile of every
-            // pair and sends the other's piece across.
-            {
-                const float w_a = lo ? 65536.0f / kUMax : 256.0f / kUMax;
-                const float w_d2 = 1.0f / kUMax;
-                const float ntw = (BITS == 4 && !lo) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
+        // ---------------- fold the digit sums into the float sums ----------------
+        // Accumulator rows: r < 4 -> (digit 0, head r) in c0/c1 and (digit 2,
+        // head r) in c2/c3; r >= 4 -> (digit 1, head r - 4) in c0/c1.  value =
+        // (d0*2^16 + d1*2^8 + d2) / (2^24 - 1).  Lanes L and L^16 hold the
+        // pieces of the same (head, column): each keeps one n-tile of every
+        // pair and sends the other's piece across.
+        {
+            const float w_a = lo ? 65536.0f / kUMax : 256.0f / kUMax;
+            const float w_d2 = 1.0f / kUMax;
+            const float ntw = (BITS == 4 && !lo) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
 #pragma unroll
-                for (int np = 0; np < GG::NTV / 2; np++) {
-                    if constexpr (BITS == 4) {
+            for (int np = 0; np < GG::NTV / 2; np++) {
+                if constexpr (BITS == 4) {
 #pragma unroll
-                        for (int x = 0; x < 4; x++) pacc[2 * np][x] -= pacc[2 * np + 1][x];  // low nibbles
+                    for (int x = 0; x < 4; x++) pacc[2 * np][x] -= pacc[2 * np + 1][x];  // low nibbles
+                }
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    float fe = (float)pacc[2 * np][cc] * w_a, fo = (float)pacc[2 * np + 1][cc] * w_a;
+                    if (lo) {
+                        fe = fmaf((float)pacc[2 * np][2 + cc], w_d2, fe);
+                        fo = fmaf((float)pacc[2 * np + 1][2 + cc], w_d2, fo);
                     }
-#pragma unroll
-                    for (int cc = 0; cc < 2; cc++) {
-                        float fe = (float)pacc[2 * np][cc] * w_a, fo = (float)pacc[2 * np + 1][cc] * w_a;
-                        if (lo) {
-                            fe = fmaf((float)pacc[2 * np][2 + cc], w_d2, fe);
-                            fo = fmaf((float)pacc[2 * np + 1][2 + cc], w_d2, fo);
-                        }
-                        const float recv = __shfl_xor_sync(0xffffffffu, lo ? fo : fe, 16);
-                        facc[2 * np + cc] = fmaf((lo ? fe : fo) + recv, ntw, facc[2 * np + cc]);
-                    }
+                    const float recv = __shfl_xor_sync(0xffffffffu, lo ? fo : fe, 16);
+                    facc[2 * np + cc] = fmaf((lo ? fe : fo) + recv, ntw, facc[2 * np + cc]);
                 }
             }
-            fs += ns;
         }
-
-        // ---------------- the unit's partial record ----------------
-        Lr += __shfl_xor_sync(0xffffffffu, Lr, 1);
-        Lr += __shfl_xor_sync(0xffffffffu, Lr, 2);
-        Lr += __shfl_xor_sync(0xffffffffu, Lr, 4);
-        Zr += __shfl_xor_sync(0xffffffffu, Zr, 1);
-        Zr += __shfl_xor_sync(0xffffffffu, Zr, 2);
-        Zr += __shfl_xor_sync(0xffffffffu, Zr, 4);
-        if (!failed) {
-            // record: value sums [head][dim], then R, L, Z of the four heads
-            float *rec = a.workspace + (int64_t)(w + u) * GG::REC;
-            const int hr = (lane >> 2) & 3;
-            if (hr < G) {
+        if (nsn == 0 || un != u) {
+            // ---------------- the unit's partial record ----------------
+            Lr += __shfl_xor_sync(0xffffffffu, Lr, 1);
+            Lr += __shfl_xor_sync(0xffffffffu, Lr, 2);
+            Lr += __shfl_xor_sync(0xffffffffu, Lr, 4);
+            Zr += __shfl_xor_sync(0xffffffffu, Zr, 1);
+            Zr += __shfl_xor_sync(0xffffffffu, Zr, 2);
+            Zr += __shfl_xor_sync(0xffffffffu, Zr, 4);
+            if (!failed) {
+                // record: value sums [head][dim], then R, L, Z of the four heads
+                float *rec = a.workspace + (int64_t)(w + u) * GG::REC;
+                const int hr = (lane >> 2) & 3;
+                if (hr < G) {
 #pragma unroll
-                for (int k = 0; k < GG::NF; k++)
-                    rec[hr * D + v_dim<BITS, D>(2 * (k >> 1) + (lo ? 0 : 1), 2 * q + (k & 1))] = facc[k];
+                    for (int k = 0; k < GG::NF; k++)
+                        rec[hr * D + v_dim<BITS, D>(2 * (k >> 1) + (lo ? 0 : 1), 2 * q + (k & 1))] = facc[k];
+                }
+                if (tq == 0) {
+                    rec[4 * D + ph] = ph < G ? Rr : -INFINITY;
+                    rec[4 * D + 4 + ph] = Lr;
+                    rec[4 * D + 8 + ph] = Zr;
+                }
             }
-            if (tq == 0) {
-                rec[4 * D + ph] = ph < G ? Rr : -INFINITY;
-                rec[4 * D + 4 + ph] = Lr;
-                rec[4 * D + 8 + ph] = Zr;
-            }
+            fresh = true;
         }
-        f = seg_end;
+        if (nsn == 0) break;
+        fs = fn;
+        u = un;
+        ubase = ubn;
+        ns = nsn;
     }
 
     if (failed && lane == 0) {
-        // a wait gave up and no copy was issued since: let this warp's copies still in flight land (bounded)
-        for (int jj = failed_at; jj < cs->n_issued; jj++) mbar_wait_bounded(mybar + (jj & 1), (uint32_t)((jj >> 1) & 1));
+        // a wait gave up and nothing was issued since: let this warp's copies still in flight land (bounded)
+        for (int b = 0; b < 4; b++)
+            if (pend & (1u << b)) mbar_wait_bounded(mybar + (b >> 1), (uint32_t)(b & 1));
     }
 }
 
