@@ -41,10 +41,11 @@ namespace sa {
 namespace {
 
 constexpr int kNW = 8;            // warps per decode CTA
-constexpr int kTileW = 12;        // u32 words per row of a warp's P-digit tile
+constexpr int kTileW = 8;         // u32 words per row of a warp's P-digit tile (12 rows)
 constexpr float kLog2eF = 1.4426950408889634f;
 constexpr float kQMax = 8355711.0f;   // 127*65536 + 127*256 + 127
 constexpr float kUMax = 16777215.0f;  // 2^24 - 1
+constexpr float kLog2UMax = 23.99999991400867f;  // log2(2^24 - 1)
 constexpr uint32_t kWaitLimit = 20000;       // bounded waits: at most kWaitLimit tries ...
 constexpr uint32_t kWaitHintNs = 100000;     // ... each suspending the thread for up to 100 us
 
@@ -344,20 +345,20 @@ __global__ void __launch_bounds__(kNW * 32, 2)
     // and not yet waited for.
     unsigned pend = 0;
     bool failed = false;
+    // Whole chunks are copied even past the context (the capacity is a
+    // multiple of 64, the cache is zero-initialised): the extra tokens are
+    // finite and masked by their -inf scores.
     auto issue = [&](int s, int uu, int c, int kind) {
-        const int g0 = c * CT;  // first token of the chunk
-        const int cnt = min(total - g0, CT);
-        const uint32_t mb = (uint32_t)(((cnt + 1) & ~1) * 8);  // meta rows rounded to even: 16-byte copies
-        const uint32_t cb = kind == 0 ? (uint32_t)(cnt * KB) : (uint32_t)(((cnt + kVBlock - 1) / kVBlock) * kVBlock * KB);
-        const int64_t row = (int64_t)uu * a.capacity + g0;
+        constexpr uint32_t kCodeBytes = CT * KB, kMetaBytes = CT * 8;
+        const int64_t row = (int64_t)uu * a.capacity + c * CT;  // first token of the chunk
         uint64_t *bar = mybar + s;
-        if (lane == 0) mbar_expect_tx(bar, cb + (kind == 0 ? 2 * mb : mb));
+        if (lane == 0) mbar_expect_tx(bar, kCodeBytes + (kind == 0 ? 2 * kMetaBytes : kMetaBytes));
         if (lane < 3 - kind) {
             const void *src;
-            uint32_t nb = mb, off;
+            uint32_t nb = kMetaBytes, off;
             if (lane == 0) {
                 src = (kind == 0 ? a.k_codes : a.v_codes) + row * KB;
-                nb = cb;
+                nb = kCodeBytes;
                 off = 0;
             } else if (lane == 1) {
                 src = (kind == 0 ? a.k_meta : a.v_meta) + row * 2;
@@ -495,13 +496,12 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                             const float dot = fmaf((float)acc[0][2 * hf], 65536.0f,
                                                    (float)(acc[0][2 * hf + 1] * 256 + acc[1][2 * hf]));
                             const float2 km = *reinterpret_cast<const float2 *>(kms + 2 * row);
-                            const float s = fmaf(km.x * c1, dot, km.y * c2);
-                            if (tl < n_w) {
-                                vmax = fmaxf(vmax, vms[2 * row]);
-                                if (my_head) {
-                                    scw[q * SCS + tl] = s;
-                                    rmax = fmaxf(rmax, s);
-                                }
+                            const bool in = tl < n_w;
+                            const float s = in ? fmaf(km.x * c1, dot, km.y * c2) : -INFINITY;
+                            vmax = fmaxf(vmax, in ? vms[2 * row] : 0.0f);
+                            if (my_head) {
+                                scw[q * SCS + tl] = s;
+                                rmax = fmaxf(rmax, s);
                             }
                         }
                     }
@@ -520,6 +520,7 @@ __global__ void __launch_bounds__(kNW * 32, 2)
         // new reference of head ph (lane ph holds head ph's max; u = 2^(s - R) * vscale <= 1)
         // and the factor that moves earlier sums to it
         const float Rp = fmaxf(Rr, __shfl_sync(0xffffffffu, rmax, ph) + __log2f(vmax));
+        const float Rq = Rp - kLog2UMax;  // sums and digits are kept in units of 1 / kUMax
         const float fac = (Rr == -INFINITY) ? 0.0f : exp2f(Rr - Rp);
         Rr = Rp;
         Lr *= fac;
@@ -545,8 +546,10 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                 for (int sp = 0; sp < CT / 32; sp++) {
                     const int tc = 32 * sp + 4 * tq;  // this lane's first token within the chunk
                     const int tb = cc * CT + tc;      // ... within the sub-segment
-                    uint32_t U[4] = {0u, 0u, 0u, 0u};
-                    if (ph < G && tb < n_w) {
+                    // Tokens past the context have score -inf (e = 0).  Rows of heads >= G
+                    // hold no scores; their sums are never read.
+                    uint32_t U[4];
+                    {
                         const float4 s4 = *reinterpret_cast<const float4 *>(scw + ph * SCS + tb);
                         const float4 m01 = *reinterpret_cast<const float4 *>(vms + 2 * tc);
                         const float4 m23 = *reinterpret_cast<const float4 *>(vms + 2 * tc + 4);
@@ -554,23 +557,24 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                         const float vs[4] = {m01.x, m01.z, m23.x, m23.z}, vz[4] = {m01.y, m01.w, m23.y, m23.w};
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
-                            if (tb + e < n_w) {
-                                const float ee = ex2_approx(sv[e] - Rp);  // 2^(s - R)
-                                Lr += ee;
-                                Zr = fmaf(ee, vz[e], Zr);
-                                U[e] = __float2uint_rn(fminf(ee * vs[e], 1.0f) * kUMax);
-                            }
+                            const float ee = ex2_approx(sv[e] - Rq);  // kUMax * 2^(s - R)
+                            Lr += ee;
+                            Zr = fmaf(ee, vz[e], Zr);
+                            U[e] = __float2uint_rn(fminf(ee * vs[e], kUMax));
                         }
                     }
                     // digit j of the 4 tokens -> one A-fragment word (row 4j + head, token quad tq)
                     const uint32_t lo0 = __byte_perm(U[0], U[1], 0x0062), hi0 = __byte_perm(U[2], U[3], 0x0062);
                     const uint32_t lo1 = __byte_perm(U[0], U[1], 0x0051), hi1 = __byte_perm(U[2], U[3], 0x0051);
                     const uint32_t lo2 = __byte_perm(U[0], U[1], 0x0040), hi2 = __byte_perm(U[2], U[3], 0x0040);
+                    // row R keeps column c at word R*8 + (c ^ (R & 4)): the stores of
+                    // rows x..x+3 and the fragment loads hit 32 distinct banks
                     tile[(0 + ph) * kTileW + tq] = __byte_perm(lo0, hi0, 0x5410);
-                    tile[(4 + ph) * kTileW + tq] = __byte_perm(lo1, hi1, 0x5410);
+                    tile[(4 + ph) * kTileW + (tq ^ 4)] = __byte_perm(lo1, hi1, 0x5410);
                     tile[(8 + ph) * kTileW + tq] = __byte_perm(lo2, hi2, 0x5410);
                     __syncwarp();
-                    const uint32_t pa0 = tile[r * kTileW + q], pa2 = tile[r * kTileW + 4 + q];
+                    const int sw = r & 4;
+                    const uint32_t pa0 = tile[r * kTileW + (q ^ sw)], pa2 = tile[r * kTileW + ((4 + q) ^ sw)];
                     const uint32_t pa1 = r < 4 ? tile[(r + 8) * kTileW + q] : 0u;
                     const uint32_t pa3 = r < 4 ? tile[(r + 8) * kTileW + 4 + q] : 0u;
                     __syncwarp();
@@ -612,8 +616,7 @@ __global__ void __launch_bounds__(kNW * 32, 2)
         // pieces of the same (head, column): each keeps one n-tile of every
         // pair and sends the other's piece across.
         {
-            const float w_a = lo ? 65536.0f / kUMax : 256.0f / kUMax;
-            const float w_d2 = 1.0f / kUMax;
+            const float w_a = lo ? 65536.0f : 256.0f;  // digit weights (sums are in units of 1 / kUMax)
             const float ntw = (BITS == 4 && !lo) ? 0.0625f : 1.0f;  // high-nibble tiles hold 16 * code
 #pragma unroll
             for (int np = 0; np < GG::NTV / 2; np++) {
@@ -625,8 +628,8 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                 for (int cc = 0; cc < 2; cc++) {
                     float fe = (float)pacc[2 * np][cc] * w_a, fo = (float)pacc[2 * np + 1][cc] * w_a;
                     if (lo) {
-                        fe = fmaf((float)pacc[2 * np][2 + cc], w_d2, fe);
-                        fo = fmaf((float)pacc[2 * np + 1][2 + cc], w_d2, fo);
+                        fe += (float)pacc[2 * np][2 + cc];
+                        fo += (float)pacc[2 * np + 1][2 + cc];
                     }
                     const float recv = __shfl_xor_sync(0xffffffffu, lo ? fo : fe, 16);
                     facc[2 * np + cc] = fmaf((lo ? fe : fo) + recv, ntw, facc[2 * np + cc]);
