@@ -124,6 +124,16 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
+// Same product with a zero accumulator input (starts a sum without zeroing registers).
+__device__ __forceinline__ void mma_u8u8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -179,7 +189,6 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     using GG = Geo<BITS, D>;
     constexpr int EPL = D / 32;
     __shared__ float s_q[4][D];
-    __shared__ float s_sig[4], s_qs[4];
     __shared__ uint8_t s_codes[2][256];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int h = blockIdx.x, b = blockIdx.y;
@@ -191,75 +200,80 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     griddep_launch_dependents();
     if (do_append && warp < 2) {
         encode_append_vector<T, EPL>(ap, b, 0, h, warp, lane, s_codes[warp]);
-    } else if (warp >= q0w && warp - q0w < G) {
-        const int g = warp - q0w;
-        const int qheads = a.heads * G;
-        const T *src = static_cast<const T *>(a.query) + ((int64_t)b * qheads + h * G + g) * D;
-        float x[EPL];
-#pragma unroll
-        for (int r = 0; r < EPL; r++) {
-            const int e = lane * EPL + r;
-            x[r] = ld_f32(src + e);
-            if (a.do_rotary) x[r] = rope_element(src, x[r], e, D, a.pos0, a.cos_cache, a.sin_cache, a.interleaved);
-            x[r] *= sg[e];
-        }
-        warp_wht_butterfly<EPL>(x, lane, D);
-        float sum = 0.0f, mabs = 0.0f;
-#pragma unroll
-        for (int r = 0; r < EPL; r++) {
-            x[r] *= a.wht_scale;
-            s_q[g][lane * EPL + r] = x[r];
-            sum += x[r];
-            mabs = fmaxf(mabs, fabsf(x[r]));
-        }
-        sum = warp_sum(sum);
-        mabs = warp_max(mabs);
-        if (lane == 0) {
-            s_qs[g] = sum;
-            s_sig[g] = mabs > 0.0f ? mabs / kQMax : 1.0f;
-        }
+        return;
     }
-    __syncthreads();
-    if (warp != 0) return;
-    // lane (r, q): B fragment words for k-chunk c, n-tile t, half.  n-tile 0
-    // column 2j -> (head j, digit 0), 2j+1 -> (head j, digit 1); n-tile 1
-    // column 2j -> (head j, digit 2), 2j+1 -> zero.  Column = r.
-    const int r = lane >> 2, q = lane & 3;
-    const int hh = r >> 1;
-    const bool has_head = hh < G;
-    const float inv_sigma = has_head ? 1.0f / s_sig[hh] : 0.0f;
+    const int g = warp - q0w;
+    if (g < 0 || g >= 4) return;
     const int64_t bh = (int64_t)b * a.heads + h;
-    uint32_t *dst = qfrag + (bh * 32 + lane) * GG::QW;
+    uint32_t *frag = qfrag + bh * 32 * GG::QW;
+    // Fragment lane fl = (r, q) holds column r of the QK B operand: head
+    // r >> 1; n-tile 0 column 2j -> (head j, digit 0), 2j+1 -> (head j,
+    // digit 1); n-tile 1 column 2j -> (head j, digit 2), 2j+1 -> zero.  Warp g
+    // writes the 8 fragment lanes of head g, each as four lanes of 4 words.
+    const int fl = 8 * g + (lane >> 2);  // fragment lane
+    const int fr = fl >> 2, fq = fl & 3;
+    uint32_t *dst = frag + fl * GG::QW + (lane & 3) * (GG::QW / 4);
+    if (g >= G) {  // no such head: zero columns
 #pragma unroll
-    for (int c = 0; c < GG::NCH; c++) {
-#pragma unroll
-        for (int half = 0; half < 2; half++) {
-            uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int k = 16 * half + 4 * q + e;
-                int qi = 0;
-                if (has_head) {
-                    qi = __float2int_rn(s_q[hh][k_dim<BITS, D>(c, q, k)] * inv_sigma);
-                    qi = min(max(qi, -(int)kQMax), (int)kQMax);  // keep the top digit within int8
-                }
-                const int d2 = (int)(int8_t)(qi & 0xff);
-                const int rest = (qi - d2) >> 8;
-                const int d1 = (int)(int8_t)(rest & 0xff);
-                const int d0 = (rest - d1) >> 8;
-                w0 |= ((uint32_t)(((r & 1) ? d1 : d0) & 0xff)) << (8 * e);
-                w1 |= ((uint32_t)(((r & 1) ? 0 : d2) & 0xff)) << (8 * e);
-            }
-            dst[c * 4 + 0 * 2 + half] = w0;  // n-tile 0
-            dst[c * 4 + 1 * 2 + half] = w1;  // n-tile 1
+        for (int i = 0; i < GG::QW / 4; i++) dst[i] = 0u;
+        if (lane == 0) {
+            qscal[bh * 8 + g] = 0.0f;
+            qscal[bh * 8 + 4 + g] = 0.0f;
         }
+        return;
     }
-    if (lane < 4) {
+    const int qheads = a.heads * G;
+    const T *src = static_cast<const T *>(a.query) + ((int64_t)b * qheads + h * G + g) * D;
+    float x[EPL];
+#pragma unroll
+    for (int r = 0; r < EPL; r++) {
+        const int e = lane * EPL + r;
+        x[r] = ld_f32(src + e);
+        if (a.do_rotary) x[r] = rope_element(src, x[r], e, D, a.pos0, a.cos_cache, a.sin_cache, a.interleaved);
+        x[r] *= sg[e];
+    }
+    warp_wht_butterfly<EPL>(x, lane, D);
+    float sum = 0.0f, mabs = 0.0f;
+#pragma unroll
+    for (int r = 0; r < EPL; r++) {
+        x[r] *= a.wht_scale;
+        s_q[g][lane * EPL + r] = x[r];
+        sum += x[r];
+        mabs = fmaxf(mabs, fabsf(x[r]));
+    }
+    sum = warp_sum(sum);
+    mabs = warp_max(mabs);
+    const float sigma = mabs > 0.0f ? mabs / kQMax : 1.0f;
+    const float inv_sigma = 1.0f / sigma;
+    if (lane == 0) {
         const float sl2 = a.scale * kLog2eF;
-        qscal[bh * 8 + lane] = lane < G ? s_sig[lane] * sl2 : 0.0f;
-        qscal[bh * 8 + 4 + lane] = lane < G ? s_qs[lane] * sl2 : 0.0f;
+        qscal[bh * 8 + g] = sigma * sl2;
+        qscal[bh * 8 + 4 + g] = sum * sl2;
+    }
+    __syncwarp();  // s_q[g] complete
+    // this lane's words: index i of fragment lane fl is c*4 + t*2 + half,
+    // for i in [(lane & 3) * QW/4, (lane & 3 + 1) * QW/4)
+#pragma unroll
+    for (int ii = 0; ii < GG::QW / 4; ii++) {
+        const int i = (lane & 3) * (GG::QW / 4) + ii;
+        const int c = i >> 2, t = (i >> 1) & 1, half = i & 1;
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int k = 16 * half + 4 * fq + e;
+            int qi = __float2int_rn(s_q[g][k_dim<BITS, D>(c, fq, k)] * inv_sigma);
+            qi = min(max(qi, -(int)kQMax), (int)kQMax);  // keep the top digit within int8
+            const int d2 = (int)(int8_t)(qi & 0xff);
+            const int rest = (qi - d2) >> 8;
+            const int d1 = (int)(int8_t)(rest & 0xff);
+            const int d0 = (rest - d1) >> 8;
+            const int dg = t == 0 ? ((fr & 1) ? d1 : d0) : ((fr & 1) ? 0 : d2);
+            word |= ((uint32_t)(dg & 0xff)) << (8 * e);
+        }
+        dst[ii] = word;
     }
 }
+
 
 // ---- decode: stream-K warp ranges ----------------------------------------------
 // The context of every (row, KV head) unit is cut into chunks of CT tokens and
@@ -446,7 +460,7 @@ __global__ void __launch_bounds__(kNW * 32, 2)
             for (int cc = 0; cc < 2; cc++) {
                 wait(cc, 0);
                 if (failed) break;
-                if (cc < ns) {
+                if (cc == 0 || cc < ns) {  // a sub-segment has at least one chunk
                     const unsigned char *st = slots + cc * GG::SLOT;
                     const float *kms = reinterpret_cast<const float *>(st + CT * KB);
                     const float *vms = kms + 2 * CT;
@@ -532,14 +546,12 @@ __global__ void __launch_bounds__(kNW * 32, 2)
         }
 
         // ---------------- phase 2: values ----------------
-        int pacc[GG::NTV][4];
-#pragma unroll
-        for (int nt = 0; nt < GG::NTV; nt++) pacc[nt][0] = pacc[nt][1] = pacc[nt][2] = pacc[nt][3] = 0;
+        int pacc[GG::NTV][4];  // started by the first 32-token step (chunk 0 always holds tokens)
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
             wait(cc, 1);
             if (failed) break;
-            if (cc < ns) {
+            if (cc == 0 || cc < ns) {  // a sub-segment has at least one chunk
                 const unsigned char *st = slots + cc * GG::SLOT;
                 const float *vms = reinterpret_cast<const float *>(st + CT * KB);
 #pragma unroll
@@ -591,11 +603,18 @@ __global__ void __launch_bounds__(kNW * 32, 2)
                             if constexpr (BITS == 4) {
                                 // n-tile 2i sums the raw bytes (lo + 16 hi), n-tile 2i+1 the high
                                 // nibbles in place (16 hi); the fold separates them
-                                mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
-                                mma_u8u8(pacc[2 * i + 1], pa0, pa1, pa2, pa3, y0[jj] & 0xF0F0F0F0u,
-                                         y1[jj] & 0xF0F0F0F0u);
+                                if (cc == 0 && sp == 0) {
+                                    mma_u8u8_z(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
+                                    mma_u8u8_z(pacc[2 * i + 1], pa0, pa1, pa2, pa3, y0[jj] & 0xF0F0F0F0u,
+                                               y1[jj] & 0xF0F0F0F0u);
+                                } else {
+                                    mma_u8u8(pacc[2 * i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
+                                    mma_u8u8(pacc[2 * i + 1], pa0, pa1, pa2, pa3, y0[jj] & 0xF0F0F0F0u,
+                                             y1[jj] & 0xF0F0F0F0u);
+                                }
                             } else {
-                                mma_u8u8(pacc[i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
+                                if (cc == 0 && sp == 0) mma_u8u8_z(pacc[i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
+                                else mma_u8u8(pacc[i], pa0, pa1, pa2, pa3, y0[jj], y1[jj]);
                             }
                         }
                     }
@@ -686,34 +705,44 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(AttendArgs a, int ncu
     if (g >= a.group) return;
     const int u = blockIdx.x;
     const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
-    const float *base = a.workspace + (int64_t)u * GG::REC;  // record w + u
+    const float *base = a.workspace + ((int64_t)u + w_lo) * GG::REC;  // record w_lo + u, then one per warp
+    const int nrec = w_hi - w_lo + 1;
+    // lane i handles the meta of records i, i + 32, ...
     float M = -INFINITY;
-    for (int w = w_lo; w <= w_hi; w++) M = fmaxf(M, base[(int64_t)w * GG::REC + 4 * D + g]);
+    for (int i = lane; i < nrec; i += 32) M = fmaxf(M, base[(int64_t)i * GG::REC + 4 * D + g]);
+    M = warp_max(M);
     float x[EPL], L = 0.0f, Z = 0.0f;
 #pragma unroll
     for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
-    for (int w = w_lo; w <= w_hi; w++) {
-        const float *rec = base + (int64_t)w * GG::REC;
-        const float Rw = rec[4 * D + g];
-        if (Rw == -INFINITY) continue;
-        const float wt = exp2f(Rw - M);
-        L = fmaf(wt, rec[4 * D + 4 + g], L);
-        Z = fmaf(wt, rec[4 * D + 8 + g], Z);
-        float v[EPL];
-        if constexpr (EPL == 4) {
-            const float4 t = *reinterpret_cast<const float4 *>(rec + g * D + lane * 4);
-            v[0] = t.x;
-            v[1 % EPL] = t.y;
-            v[2 % EPL] = t.z;
-            v[3 % EPL] = t.w;
-        } else {
-            const float2 t = *reinterpret_cast<const float2 *>(rec + g * D + lane * 2);
-            v[0] = t.x;
-            v[1 % EPL] = t.y;
+    for (int i0 = 0; i0 < nrec; i0 += 32) {
+        float wt = 0.0f;
+        if (i0 + lane < nrec) {
+            const float *m = base + (int64_t)(i0 + lane) * GG::REC + 4 * D;
+            const float Rw = m[g];
+            wt = Rw == -INFINITY ? 0.0f : exp2f(Rw - M);
+            L = fmaf(wt, m[4 + g], L);
+            Z = fmaf(wt, m[8 + g], Z);
         }
-#pragma unroll
-        for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wt, v[rr], x[rr]);
+        const int n = min(32, nrec - i0);
+#pragma unroll 4
+        for (int j = 0; j < n; j++) {
+            const float wj = __shfl_sync(0xffffffffu, wt, j);
+            const float *v = base + (int64_t)(i0 + j) * GG::REC + g * D + lane * EPL;
+            if constexpr (EPL == 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(v);
+                x[0] = fmaf(wj, t.x, x[0]);
+                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
+                x[2 % EPL] = fmaf(wj, t.z, x[2 % EPL]);
+                x[3 % EPL] = fmaf(wj, t.w, x[3 % EPL]);
+            } else {
+                const float2 t = *reinterpret_cast<const float2 *>(v);
+                x[0] = fmaf(wj, t.x, x[0]);
+                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
+            }
+        }
     }
+    L = warp_sum(L);
+    Z = warp_sum(Z);
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
 #pragma unroll
     for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
@@ -750,7 +779,7 @@ int launch_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream)
     const int do_append = ap != nullptr;
     AppendArgs apv{};
     if (ap) apv = *ap;
-    const int prep_warps = (do_append ? 2 : 0) + a.group;
+    const int prep_warps = (do_append ? 2 : 0) + 4;  // the append warps, then one warp per fragment head
     decode_prep_kernel<T, BITS, D><<<dim3(a.heads, a.batch), 32 * prep_warps, 0, stream>>>(a, apv, do_append,
                                                                                             qfrag, qscal);
     count_launch();
