@@ -12,7 +12,7 @@ no flush is needed between steps.
   value   tokens/s of the device-resident step (B / step time), max over ranks
   e2e     same metric through the same C-ABI call with q/k/v copied from
           pinned host memory and attn_out copied back inside the timed region
-  roofline  the attention kernel(s) alone: algorithmic bytes / launch time
+  roofline  the attention call alone (prep + decode + merge launches): algorithmic bytes / call time
   cpu_baseline  the CPU oracle (C restatement of the reference's Rust CPU
           path: encode + read_k/read_v + SDPA) on a bounded sample, rank 0
 
@@ -35,6 +35,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 B, HQ, HKV, D, T, BITS, THETA = 64, 32, 8, 128, 8192, 4, 500000.0
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention call on this
+# workload, from one ncu capture of its three launches: prep 0.56 MB, decode_stream
+# 606.68 + 5.75 MB, merge 5.97 MB (cold-cache reads of the partial records).
+NCU_TRAFFIC_PER_CALL = 618_963_456
+NCU_TRAFFIC_DECODE_STREAM = 612_429_312
 CB = D * BITS // 8
 METRIC = "GQA decode tokens/s over int4-compressed KV (Llama-3-8B layer, B=64, T=8192)"
 UNIT = "tokens/s"
@@ -354,7 +359,9 @@ def main():
                 "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
                 "d2h_bytes_per_step": int(out.numel() * 2)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "gqa attend (split + merge)", "launches_per_call": attend_launches,
+                     "traffic": NCU_TRAFFIC_PER_CALL, "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM,
+                     "kernel": "gqa attend call: decode_prep + decode_stream + decode_merge (decode_stream is 88% "
+                               "of the call's device time)", "launches_per_call": attend_launches,
                      "algorithmic_bytes": abytes, "ms_per_call": attend_ms,
                      "peak_source": f"{peak_kind} hbm_gbs"},
         "step_bytes": algorithmic_bytes(),
