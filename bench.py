@@ -116,12 +116,18 @@ def gpu_uuid(torch, dev):
         return str(dev.index)
 
 
-def build_workload(torch, sa, dev, seed):
-    """Cache filled with T-1 tokens (seeded), plus the step's q/k/v."""
+def build_workload(torch, sa, dev, seed, kv_begin=0, kv_count=HKV):
+    """Cache filled with T-1 tokens (seeded), plus the step's q/k/v.
+
+    ``kv_begin``/``kv_count`` select a shard of the KV heads (and their query
+    heads) for the head-sharded mode.
+    """
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     std = 1.28  # N(0,1) activations through N(0, 0.02) projections of width 4096
-    cache = sa.GpuKvCache(1, HKV, D, T, batch=B, num_heads=HQ, bits=BITS, device=dev)
+    hkv, hq = kv_count, kv_count * (HQ // HKV)
+    cache = sa.GpuKvCache(1, HKV, D, T, batch=B, num_heads=HQ, bits=BITS, kv_head_begin=kv_begin,
+                          kv_head_count=kv_count, device=dev)
     cos_np, sin_np = rope_np(T, D, THETA)
     cos = torch.from_numpy(cos_np).to(dev)
     sin = torch.from_numpy(sin_np).to(dev)
@@ -129,14 +135,14 @@ def build_workload(torch, sa, dev, seed):
     pos = 0
     while pos < T - 1:
         n = min(chunk, T - 1 - pos)
-        k = (torch.randn(B, n, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
-        v = (torch.randn(B, n, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+        k = (torch.randn(B, n, hkv * D, device=dev, generator=g) * std).to(torch.bfloat16)
+        v = (torch.randn(B, n, hkv * D, device=dev, generator=g) * std).to(torch.bfloat16)
         cache.append(0, k, v, cos_cache=cos, sin_cache=sin, do_rotary=True)
         cache.advance_position(n)
         pos += n
-    q = (torch.randn(B, 1, HQ * D, device=dev, generator=g) * std).to(torch.bfloat16)
-    k = (torch.randn(B, 1, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
-    v = (torch.randn(B, 1, HKV * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    q = (torch.randn(B, 1, hq * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    k = (torch.randn(B, 1, hkv * D, device=dev, generator=g) * std).to(torch.bfloat16)
+    v = (torch.randn(B, 1, hkv * D, device=dev, generator=g) * std).to(torch.bfloat16)
     torch.cuda.synchronize(dev)
     return cache, cos, sin, q, k, v
 
@@ -241,6 +247,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every step from the host instead of replaying a CUDA graph of one step")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="heads mode: peer = the decode epilogue stores every rank's copy over NVLink "
+                         "(symmetric memory) + one barrier; nccl = NCCL all-gather of attn_out")
+    ap.add_argument("--mode", default="batch", choices=["batch", "heads"],
+                    help="N>1: batch = every rank decodes its own 64 sequences (weak scaling, no collective); "
+                         "heads = the 64 sequences' KV heads split over the ranks, attn_out all-gathered over "
+                         "NCCL (strong scaling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -263,14 +278,36 @@ def main():
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
-    cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank)
+    heads = args.mode == "heads" and world > 1
+    if heads:
+        from smallaios_b200 import sharding
+
+        shard = sharding.head_shard(HQ, HKV, world, rank)
+        kv_count = shard.kv_count
+        cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank, kv_begin=shard.kv_begin,
+                                                  kv_count=kv_count)
+        gathered = torch.empty(B, 1, HQ * D, dtype=q.dtype, device=dev)
+        peer = sharding.PeerGather((B, 1, HQ * D), q.dtype, dev) if args.gather == "peer" else None
+    else:
+        kv_count = HKV
+        cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank)
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def gqa(q_, k_, v_):
         cache.set_position(T - 1)
-        sa.group_query_attention(q, k, v, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
-                                 sin_cache=sin, do_rotary=True, out=out)
+        if heads:
+            res = sharding.sharded_group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV,
+                                                         shard=shard, cos_cache=cos, sin_cache=sin, do_rotary=True,
+                                                         local_out=out, out=None if peer else gathered, gather=peer)
+            if peer is not None:
+                gathered.copy_(res)
+        else:
+            sa.group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
+                                     sin_cache=sin, do_rotary=True, out=out)
+
+    def step():
+        gqa(q, k, v)
 
     def barrier():
         if world > 1:
@@ -280,6 +317,19 @@ def main():
     for _ in range(args.warmup):
         step()
     barrier()
+    # One step captured as a CUDA graph (the library's calls are capturable:
+    # no host sync, no allocation); replays remove the host's per-launch cost.
+    run, graph_launches, graph = step, None, None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        c0 = lib.sa_kernel_launches()
+        with torch.cuda.graph(graph):
+            step()
+        graph_launches = lib.sa_kernel_launches() - c0
+        run = graph.replay
+        for _ in range(args.warmup):
+            run()
+        barrier()
 
     sampler = ClockSampler(gpu_uuid(torch, dev))
     sampler.start()
@@ -288,10 +338,10 @@ def main():
     barrier()
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        run()
     e1.record(stream)
     barrier()
-    launches = lib.sa_kernel_launches() - launches0
+    launches = lib.sa_kernel_launches() - launches0 if graph_launches is None else graph_launches * args.steps
     t_ms = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop()
 
@@ -317,14 +367,15 @@ def main():
     hout = torch.empty_like(out, device="cpu").pin_memory()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
+    if heads:
+        hout = torch.empty_like(gathered, device="cpu").pin_memory()
+
     def e2e_step():
         dq.copy_(hq_, non_blocking=True)
         dk.copy_(hk_, non_blocking=True)
         dv.copy_(hv_, non_blocking=True)
-        cache.set_position(T - 1)
-        sa.group_query_attention(dq, dk, dv, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
-                                 sin_cache=sin, do_rotary=True, out=out)
-        hout.copy_(out, non_blocking=True)
+        gqa(dq, dk, dv)
+        hout.copy_(gathered if heads else out, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -342,30 +393,39 @@ def main():
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     t_ms, e2e_ms, attend_ms = times.tolist()
+    rows_mult = 1 if heads else world  # sequences decoded per step = B * rows_mult
 
     peak, peak_kind = load_peaks()
-    abytes = attend_bytes()
+    abytes = attend_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV))  # this rank's share
     achieved = abytes / (attend_ms * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": B * world / (t_ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "metric": METRIC, "value": B * rows_mult / (t_ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True,
+        "scaling": "strong" if heads else "weak", "vs_baseline": None,
         "dtype": "int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
-        "config": {"workload": "llama3-8b-layer-decode (BASELINE config 3)", "batch_per_gpu": B,
-                   "global_batch": B * world, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
-                   "kv_bits": BITS, "rope_theta": THETA, "parallelism": f"batch-sharded x{world} (no collective)",
-                   "l2": "cache 604 MB > 126 MB L2 per step; no flush"},
+        "config": {"workload": "llama3-8b-layer-decode (BASELINE config 3)",
+                   "batch_per_gpu": B if not heads else f"{B} (kv heads {kv_count} of {HKV})",
+                   "global_batch": B * rows_mult, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
+                   "kv_bits": BITS, "rope_theta": THETA,
+                   "parallelism": ((f"kv-head-sharded x{world}, " + ("attn_out stored to every rank by the decode "
+                                                                      "epilogue over NVLink + barrier"
+                                                                      if args.gather == "peer" else
+                                                                      "NCCL all-gather of attn_out"))
+                                   if heads else f"batch-sharded x{world} (no collective)"),
+                   "l2": "cache 604 MB > 126 MB L2 per step; no flush",
+                   "launch": "host launches" if args.no_graph else "CUDA graph of one step, replayed"},
         "gpu_launches": int(launches),
-        "e2e": {"value": B * world / (e2e_ms * 1e-3), "unit": UNIT,
+        "e2e": {"value": B * rows_mult / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
-                "d2h_bytes_per_step": int(out.numel() * 2)},
+                "d2h_bytes_per_step": int(hout.numel() * 2)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": NCU_TRAFFIC_PER_CALL, "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM,
                      "kernel": "gqa attend call: decode_prep + decode_stream + decode_merge (decode_stream is 88% "
                                "of the call's device time)", "launches_per_call": attend_launches,
                      "algorithmic_bytes": abytes, "ms_per_call": attend_ms,
                      "peak_source": f"{peak_kind} hbm_gbs"},
-        "step_bytes": algorithmic_bytes(),
-        "step_gbs": algorithmic_bytes() / (t_ms * 1e-3) / 1e9,
+        "step_bytes": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)),  # per rank
+        "step_gbs": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)) / (t_ms * 1e-3) / 1e9,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -377,6 +437,11 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     cache.close()
+    # a graph that holds NCCL calls must be released before the process group
+    if graph is not None:
+        torch.cuda.synchronize(dev)
+        graph.reset()
+        del graph
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -138,6 +138,21 @@ int sa_kv_cache_set_position(sa_kv_cache *cache, int64_t position);
 int sa_kv_cache_advance(sa_kv_cache *cache, int64_t n);
 /* The layer's device pointers and layout. */
 int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_view *view);
+/* Head-sharded output (one rank of a KV-head-sharded layer).  Afterwards every
+ * attention call on `cache` stores the output of this rank's query heads into
+ * each of the `n` buffers -- this GPU's and its peers', all addressable from
+ * this process (IPC / virtual-memory peer mappings) -- at columns
+ * [q_head_offset*D, (q_head_offset + q_local)*D) of a [batch][seq_len]
+ * [q_heads_total*D] tensor, instead of writing attn_out (whose contents are
+ * then unspecified).  This replaces the all-gather of attn_out that follows
+ * the local operator in the head-sharded mode: the decode kernel's epilogue
+ * writes every rank's copy over NVLink.  q_heads_total must equal the cache's
+ * num_heads and q_head_offset its kv_head_begin * group.  n = 0 turns it off.
+ * The caller runs a cross-rank barrier after the call before any rank reads
+ * its buffer, and alternates buffers between steps so that no rank writes a
+ * buffer a peer may still be reading.  At most 8 buffers. */
+int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, int32_t q_head_offset,
+                           int32_t q_heads_total);
 /* Copy of the cache configuration. */
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config);
 /* Device-side status of the kernels that used this cache: 0, or bit 0 set when

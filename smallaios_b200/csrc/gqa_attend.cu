@@ -358,6 +358,32 @@ int launch_gqa_combine(const AttendArgs &a, int n_splits, cudaStream_t stream) {
     return check_cuda(cudaGetLastError(), "gqa_attend combine launch");
 }
 
+// Head-sharded output of the generic path: rows of attn_out [B][S][q_local*D]
+// copied into every gather buffer at the rank's columns (16-byte copies; the
+// column offset is col0*D elements, a multiple of 16 bytes for D >= 16).
+__global__ void __launch_bounds__(256) gather_scatter_kernel(const uint4 *src, GatherOut g, int row_vecs,
+                                                             int64_t dst_row_vecs, int64_t col_vecs) {
+    const int64_t row = blockIdx.x;
+    const uint4 *s = src + row * row_vecs;
+    for (int i = threadIdx.x; i < row_vecs; i += blockDim.x) {
+        const uint4 x = s[i];
+        for (int r = 0; r < g.n; r++) static_cast<uint4 *>(g.p[r])[row * dst_row_vecs + col_vecs + i] = x;
+    }
+}
+
+int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream) {
+    const int esz = a.dtype == SA_DTYPE_FLOAT ? 4 : 2;
+    const int64_t local_q = (int64_t)a.heads * a.group;
+    const int row_vecs = (int)(local_q * a.head_dim * esz / 16);
+    const int64_t dst_row_vecs = (int64_t)a.gather.cols * a.head_dim * esz / 16;
+    const int64_t col_vecs = (int64_t)a.gather.col0 * a.head_dim * esz / 16;
+    const unsigned rows = (unsigned)((int64_t)a.batch * a.seq_len);
+    gather_scatter_kernel<<<rows, 256, 0, stream>>>(static_cast<const uint4 *>(a.out), a.gather, row_vecs, dst_row_vecs,
+                                                   col_vecs);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "gqa gather scatter launch");
+}
+
 int launch_gqa_attend_generic(const AttendArgs &a, cudaStream_t stream) {
     const int64_t total = a.pos0 + a.seq_len;
     int n_splits, tps;

@@ -749,10 +749,22 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(AttendArgs a, int ncu
     warp_wht_butterfly<EPL>(x, lane, D);
     const int h = u % a.heads;
     const float *sg = a.signs + (int64_t)h * D;
-    T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
 #pragma unroll
-    for (int rr = 0; rr < EPL; rr++)
-        st_from_f32(dst + lane * EPL + rr, x[rr] * a.wht_scale * sg[lane * EPL + rr]);
+    for (int rr = 0; rr < EPL; rr++) x[rr] *= a.wht_scale * sg[lane * EPL + rr];
+    if (a.gather.n == 0) {
+        T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
+#pragma unroll
+        for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + lane * EPL + rr, x[rr]);
+    } else {
+        // head-sharded: row b, global query head col0 + h*G + g of every rank's buffer
+        const int64_t b = u / a.heads;
+        const int64_t off = (b * a.gather.cols + a.gather.col0 + (int64_t)h * a.group + g) * D + lane * EPL;
+        for (int r = 0; r < a.gather.n; r++) {
+            T *dst = static_cast<T *>(a.gather.p[r]) + off;
+#pragma unroll
+            for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + rr, x[rr]);
+        }
+    }
 }
 
 // Grid of the decode kernel: two CTAs per SM, no more warps than chunks.

@@ -21,6 +21,17 @@ __host__ __device__ __forceinline__ int64_t v_byte_offset(int64_t t, int j, int 
     return (t >> 4) * (int64_t)(16 * cb) + (k >> 4) * 64 + ((t >> 2) & 3) * 16 + (k & 15);
 }
 constexpr int kMaxSplits = 64;       // split-K partitions per (row, kv head)
+constexpr int kMaxGather = 8;        // ranks of one node in the head-sharded mode
+
+// Head-sharded output: the attention output of this rank's query heads goes
+// to every buffer p[0..n) (this GPU's and its peers', mapped into this
+// process) at columns [col0, col0 + heads*group) of a [B][S][cols*D] tensor.
+struct GatherOut {
+    void *p[kMaxGather];
+    int n;     // 0: plain attn_out
+    int col0;  // first global query head of this rank
+    int cols;  // query heads in total
+};
 
 struct kv_cache_impl {
     sa_kv_cache_config cfg;
@@ -43,6 +54,7 @@ struct kv_cache_impl {
     size_t workspace_floats;
     uint32_t *qprep;   // [B*H*32*16] q-digit words + [B*H*8] score constants
     int *dev_status;   // one int: device-side status bits
+    GatherOut gather;  // head-sharded output buffers (n = 0: off)
     size_t layer_codes_bytes;  // B*H*T*CB
     size_t layer_meta_floats;  // B*H*T*2
 };
@@ -81,10 +93,12 @@ struct AttendArgs {
     int sm_count;
     uint32_t *qprep;  // decode prep area: per (row, head) q-digit fragments + constants
     int *dev_status;  // device-side status word (bounded waits that gave up)
+    GatherOut gather;  // head-sharded output (n = 0: write `out`)
 };
 
 int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
+int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream);
 bool decode_fast_eligible(const AttendArgs &a);
 size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim);
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);

@@ -258,6 +258,36 @@ int sa_kv_cache_device_status(sa_kv_cache *cache, int32_t *status, int32_t clear
     return rc;
 }
 
+int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, int32_t q_head_offset,
+                           int32_t q_heads_total) {
+    if (!cache) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: NULL cache");
+    kv_cache_impl *k = reinterpret_cast<kv_cache_impl *>(cache);
+    if (n == 0) {
+        k->gather = GatherOut{};
+        return SA_OK;
+    }
+    if (n < 0 || n > kMaxGather || !buffers)
+        return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: %d buffers (1..%d)", n, kMaxGather);
+    const int local_q = k->cfg.kv_head_count * k->group;
+    if (q_heads_total != k->cfg.num_heads || q_head_offset < 0 || q_head_offset + local_q > q_heads_total ||
+        q_head_offset != k->cfg.kv_head_begin * k->group)
+        return set_error(SA_ERR_SHAPE_MISMATCH,
+                         "kv_cache_set_gather: query heads [%d, %d) of %d do not match the cache's KV heads "
+                         "[%d, %d) of %d",
+                         q_head_offset, q_head_offset + local_q, q_heads_total, k->cfg.kv_head_begin,
+                         k->cfg.kv_head_begin + k->cfg.kv_head_count, k->cfg.num_kv_heads);
+    GatherOut g{};
+    for (int i = 0; i < n; i++) {
+        if (!buffers[i]) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: NULL buffer %d", i);
+        g.p[i] = buffers[i];
+    }
+    g.n = n;
+    g.col0 = q_head_offset;
+    g.cols = q_heads_total;
+    k->gather = g;
+    return SA_OK;
+}
+
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config) {
     if (!cache || !config) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_get_config: NULL argument");
     *config = reinterpret_cast<const kv_cache_impl *>(cache)->cfg;
@@ -404,6 +434,7 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
     a.sm_count = k->sm_count;
     a.qprep = k->qprep;
     a.dev_status = k->dev_status;
+    a.gather = k->gather;
     AppendArgs ap;
     if (key) {
         ap.key = key;
@@ -434,7 +465,12 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         rc = launch_kv_append(ap, stream);
         if (rc != SA_OK) return rc;
     }
-    return launch_gqa_attend_generic(a, stream);
+    // the generic kernels write attn_out; a head-sharded output is copied out after
+    AttendArgs ga = a;
+    ga.gather.n = 0;
+    rc = launch_gqa_attend_generic(ga, stream);
+    if (rc != SA_OK || a.gather.n == 0) return rc;
+    return launch_gather_scatter(a, stream);
 }
 
 int sa_gqa_attend(sa_kv_cache *cache, int32_t layer, const void *query, void *attn_out, int32_t dtype,
