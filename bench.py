@@ -240,6 +240,70 @@ def run_reference(args):
     return 0
 
 
+# MatMulNBits: K=4096, N=14336, block 32, fp16 scales, zero point 8.
+MNB_K, MNB_N, MNB_BLOCK = 4096, 14336, 32
+
+
+def mnb_bytes(m, n=MNB_N, k=MNB_K, block=MNB_BLOCK):
+    """Codes + fp16 scales + fp16 A in + fp16 Y out."""
+    return n * k // 2 + n * (k // block) * 2 + m * k * 2 + m * n * 2
+
+
+def run_matmul_nbits(args):
+    """``--workload matmul_nbits``: one MatMulNBits call on config 2 per step (not the headline).
+
+    Six weight sets are cycled so that every call streams its 33 MB of codes
+    and scales from HBM (six sets, 198 MB, exceed the 126 MB L2).
+    """
+    import torch
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    m, n, k, blk = args.m, MNB_N, MNB_K, MNB_BLOCK
+    sets = []
+    for _ in range(6):
+        codes = torch.randint(0, 256, (n, k // blk, blk // 2), dtype=torch.uint8, device=dev, generator=g)
+        scales = (torch.rand(n, k // blk, device=dev, generator=g) * 0.015 + 0.005).half()
+        sets.append((codes, scales))
+    a = torch.randn(m, k, device=dev, generator=g).half()
+    y = torch.empty(m, n, dtype=torch.half, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        c, s = sets[i % 6]
+        sa.matmul_nbits(a, c, s, K=k, N=n, block_size=blk, out=y)
+    torch.cuda.synchronize(dev)
+    l0 = lib.sa_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        c, s = sets[i % 6]
+        sa.matmul_nbits(a, c, s, K=k, N=n, block_size=blk, out=y)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = lib.sa_kernel_launches() - l0
+    t_ms = e0.elapsed_time(e1) / args.steps
+    peak, peak_kind = load_peaks()
+    byts = mnb_bytes(m)
+    flops = 2.0 * m * n * k
+    achieved = byts / (t_ms * 1e-3) / 1e9
+    line = {"metric": f"MatMulNBits int4 GEMV/GEMM time (K={k}, N={n}, M={m}, block {blk}, fp16)",
+            "value": t_ms * 1e3, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": t_ms, "dtype": "int4-w/fp16-act/f32-acc",
+            "data": "synthetic (codes U{0..255} bytes, scales U[0.005, 0.02])",
+            "config": {"workload": "matmul-nbits (BASELINE config 2)", "m": m, "n": n, "k": k, "block": blk,
+                       "l2": "six weight sets cycled (198 MB > L2)"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "algorithmic_bytes": byts, "tflops": flops / (t_ms * 1e-3) / 1e12,
+                         "peak_source": f"{peak_kind} hbm_gbs"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -247,6 +311,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits"],
+                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2, one line, 1 GPU")
+    ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every step from the host instead of replaying a CUDA graph of one step")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
@@ -261,6 +328,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "matmul_nbits":
+        return run_matmul_nbits(args)
 
     import torch
     import torch.distributed as dist

@@ -1,12 +1,21 @@
 // MatMulNBits (ORT com.microsoft.MatMulNBits contract), int4 weights with
 // per-(column, k-block) scales and optional packed zero points.
 //
+// Tensor-core path (m <= 16, fp16/bf16 activations, block 32, default zero
+// point): see mnb_mma_kernel below.  Other shapes take the CUDA-core path:
+//
 // GEMV path (m <= 8 rows per pass): one warp per output column streams that
 // column's packed codes with 128-bit loads (16 bytes = 32 codes per lane per
 // step) and keeps the activation rows in registers/L1.  The block scale is
 // factored out of the inner sum: y = sum_blk s_blk * (sum_k a_k*(q_k - zp)),
 // so each code costs one integer extract and one FMA.  HBM-bound: the codes
 // and scales are read exactly once.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "sa_async.cuh"
 #include "sa_common.cuh"
 #include "sa_internal.h"
 
@@ -88,6 +97,290 @@ __global__ void __launch_bounds__(32 * kGemvWarps)
     }
 }
 
+// ---- tensor-core path ---------------------------------------------------------
+// One CTA owns a 16-column tile of N (the A operand of mma.m16n8k16: rows =
+// output columns, k = the reduction) and SPLIT warps; warp w reduces over
+// k-blocks [w*nbw, (w+1)*nbw).  Each warp streams its 16 columns' packed codes
+// and block scales through kMnbSlots shared-memory slots, 8 blocks (128 B of
+// codes per column) per chunk: one 2-D TMA copy of the 16 x 128 B code tile
+// (128-byte swizzle, so the fragment loads hit distinct banks) and one of the
+// 16 x 8 scales.  A 32-bit word of codes gives four fp16 (or bf16) pairs
+// (q - 8) with a shift, a logic op that ORs the nibble into the mantissa of
+// 1024 (128 for bf16), and a packed subtract: nibbles i and i+4 form one
+// pair, and the activations are fed in the same k order.  Products and the
+// per-block sums are exact fp32 (tensor-core accumulate); the block scale
+// multiplies each block's sum in fp32.  The activations (B operand, columns =
+// rows of A) come with each chunk too: a third TMA copy of the m x 256 tile.
+constexpr int kMnbMaxSplit = 4;                    // warps (K splits) per CTA, at most
+constexpr int kMnbChunk = 8;                       // k-blocks per chunk (128 B of codes per column)
+constexpr int kMnbCodeTile = 16 * kMnbChunk * 16;  // 2048 B, 1024-aligned in shared memory
+constexpr int kMnbScaleTile = 16 * kMnbChunk * 2;  // 256 B
+constexpr int kMnbActRow = kMnbChunk * 32 * 2;     // 512 B: one activation row of a chunk
+
+// Chunks in flight per warp (two: the CTA count is what keeps HBM busy).
+__host__ __device__ constexpr int mnb_slots(int mrows) { return 2 + 0 * mrows; }
+// K splits (warps) per CTA: more warps for one m-tile, fewer when the
+// activation tiles are large.
+__host__ __device__ constexpr int mnb_split(int mt) { return mt == 1 ? 4 : 2; }
+__host__ __device__ constexpr int mnb_slot_bytes(int mrows) {
+    return kMnbCodeTile + kMnbScaleTile + ((mrows * kMnbActRow + 127) / 128) * 128;
+}
+
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1, bool zero_c) {
+    if constexpr (std::is_same<T, __half>::value) {
+        if (zero_c)
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%10,%10,%10,%10};\n"
+                : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+        else
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};\n"
+                : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        if (zero_c)
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%10,%10,%10,%10};\n"
+                : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+        else
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};\n"
+                : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+// Nibbles i and i+4 of w as a packed pair (q - 8), exact in fp16 / bf16.
+template <typename T>
+__device__ __forceinline__ uint32_t dq_pair(uint32_t w, int i) {
+    uint32_t x;
+    if constexpr (std::is_same<T, __half>::value) {
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(0x64006400u));
+        __half2 h = *reinterpret_cast<__half2 *>(&x);
+        h = __hsub2(h, __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));  // 1032
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(0x43004300u));
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&x);
+        h = __hsub2(h, __halves2bfloat162(__ushort_as_bfloat16(0x4308), __ushort_as_bfloat16(0x4308)));  // 136
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+// 2-D tiled TMA load global -> shared (no multicast); x = inner coordinate.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <typename T, int MT, int NS, int SPLIT>
+__global__ void __launch_bounds__(32 * SPLIT)
+    mnb_mma_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
+                   const __grid_constant__ CUtensorMap tm_act, const T *__restrict__ bias, T *__restrict__ y, int m,
+                   int n, int k) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the 128-byte swizzle pattern assumes 1024-byte aligned tiles: align the base explicitly
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    // [SPLIT][NS] code tiles (1024-aligned for the swizzle), then the scale
+    // and activation tiles, barriers, the reduction area
+    const int mrows = m;
+    const int act_bytes = ((mrows * kMnbActRow + 127) / 128) * 128;
+    unsigned char *codes = smem + warp * NS * kMnbCodeTile;
+    unsigned char *scl = smem + SPLIT * NS * kMnbCodeTile + warp * NS * (kMnbScaleTile + act_bytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + SPLIT * NS * (kMnbCodeTile + kMnbScaleTile + act_bytes)) +
+                     warp * NS;
+    float *red = reinterpret_cast<float *>(smem + SPLIT * NS * (kMnbCodeTile + kMnbScaleTile + act_bytes) +
+                                           SPLIT * NS * 8);
+
+    const int n0 = blockIdx.x * 16;
+    const int nblk = k / 32;
+    const int nbw = nblk / SPLIT;  // a multiple of kMnbChunk
+    const int b0 = warp * nbw;
+    const int nchunks = nbw / kMnbChunk;
+    if (lane == 0) {
+        for (int i = 0; i < NS; i++) mbar_init(bars + i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncwarp();
+    auto issue = [&](int c) {  // lane 0: chunk c -> slot c % NS
+        const int s = c % NS;
+        const int blk = b0 + c * kMnbChunk;
+        unsigned char *st = scl + s * (kMnbScaleTile + act_bytes);
+        mbar_expect_tx(bars + s, kMnbCodeTile + kMnbScaleTile + mrows * kMnbActRow);
+        tma_load_2d(codes + s * kMnbCodeTile, &tm_codes, blk * 16, n0, bars + s);
+        tma_load_2d(st, &tm_scales, blk, n0, bars + s);
+        tma_load_2d(st + kMnbScaleTile, &tm_act, blk * 32, 0, bars + s);
+    };
+    if (lane == 0)
+        for (int c = 0; c < NS && c < nchunks; c++) issue(c);
+
+    float tot[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) tot[mt][0] = tot[mt][1] = tot[mt][2] = tot[mt][3] = 0.0f;
+    bool ok = true;
+    int c = 0;
+    for (; c < nchunks; c++) {
+        const int s = c % NS;
+        if (ok && !mbar_wait_bounded(bars + s, (uint32_t)((c / NS) & 1))) ok = false;
+        if (__any_sync(0xffffffffu, !ok)) break;  // a copy never landed: give up (output left unwritten)
+        const unsigned char *ct = codes + s * kMnbCodeTile;
+        const T *st = reinterpret_cast<const T *>(scl + s * (kMnbScaleTile + act_bytes));
+        const unsigned char *at = scl + s * (kMnbScaleTile + act_bytes) + kMnbScaleTile;  // [mrows][256] activations
+#pragma unroll 4
+        for (int bi = 0; bi < kMnbChunk; bi++) {
+            // rows g and g+8 of the 128-byte-swizzled tile: 16-byte unit bi sits at unit bi ^ (row & 7)
+            const int u = ((bi ^ g) & 7) * 16 + 4 * t;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + g * 128 + u);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (g + 8) * 128 + u);
+            const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
+                           p11 = dq_pair<T>(w1, 1);
+            const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
+                           p13 = dq_pair<T>(w1, 3);
+            const float sg = DT<T>::to_f32(st[g * kMnbChunk + bi]);
+            const float sg8 = DT<T>::to_f32(st[(g + 8) * kMnbChunk + bi]);
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                const int row = mt * 8 + g;
+                uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                if (row < m) x = *reinterpret_cast<const uint4 *>(at + row * kMnbActRow + bi * 64 + 16 * t);
+                float acc[4];
+                mma_16816<T>(acc, p00, p10, p01, p11, __byte_perm(x.x, x.z, 0x5410), __byte_perm(x.x, x.z, 0x7632),
+                             true);
+                mma_16816<T>(acc, p02, p12, p03, p13, __byte_perm(x.y, x.w, 0x5410), __byte_perm(x.y, x.w, 0x7632),
+                             false);
+                tot[mt][0] = fmaf(sg, acc[0], tot[mt][0]);
+                tot[mt][1] = fmaf(sg, acc[1], tot[mt][1]);
+                tot[mt][2] = fmaf(sg8, acc[2], tot[mt][2]);
+                tot[mt][3] = fmaf(sg8, acc[3], tot[mt][3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && c + NS < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            issue(c + NS);
+        }
+    }
+    if (!ok && lane == 0) {
+        // chunk c never landed: let this warp's copies still in flight land (bounded)
+        for (int cc = c; cc < c + NS && cc < nchunks; cc++)
+            mbar_wait_bounded(bars + cc % NS, (uint32_t)((cc / NS) & 1));
+    }
+    // sum the K splits: warps 1.. leave their sums in shared memory, warp 0 adds and stores
+    if (warp > 0) {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) red[((warp - 1) * 32 + lane) * MT * 4 + mt * 4 + j] = tot[mt][j];
+    }
+    __syncthreads();
+    if (warp != 0 || !ok) return;
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float v = tot[mt][j];
+            for (int w = 1; w < SPLIT; w++) v += red[((w - 1) * 32 + lane) * MT * 4 + mt * 4 + j];
+            const int row = mt * 8 + 2 * t + (j & 1);
+            const int col = n0 + g + ((j & 2) ? 8 : 0);
+            if (row < m) {
+                if (bias) v += DT<T>::to_f32(bias[col]);
+                st_from_f32(y + (int64_t)row * n + col, v);
+            }
+        }
+    }
+}
+
+constexpr size_t mnb_mma_smem(int mt, int ns, int split, int mrows) {
+    return 1024 + (size_t)split * ns * mnb_slot_bytes(mrows) + split * ns * 8 + (size_t)(split - 1) * 32 * mt * 4 * 4;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+template <typename T, int MT>
+int launch_mma(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
+               int64_t n, int64_t k, cudaStream_t stream) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap tm_codes, tm_scales;
+    const cuuint64_t cdim[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n}, cstride[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t cbox[2] = {kMnbChunk * 16, 16}, ones[2] = {1, 1};
+    CUresult r = encode(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(b), cdim, cstride, cbox,
+                        ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: code tensor map (%d)", (int)r);
+    const cuuint64_t sdim[2] = {(cuuint64_t)(k / 32), (cuuint64_t)n}, sstride[1] = {(cuuint64_t)(k / 32) * 2};
+    const cuuint32_t sbox[2] = {kMnbChunk, 16};
+    r = encode(&tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(scales), sdim, sstride, sbox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: scale tensor map (%d)", (int)r);
+    CUtensorMap tm_act;
+    const cuuint64_t adim[2] = {(cuuint64_t)k, (cuuint64_t)m}, astride[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t abox[2] = {kMnbChunk * 32, (cuuint32_t)m};
+    r = encode(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(a), adim, astride, abox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: activation tensor map (%d)", (int)r);
+    const int mrows = (int)m;
+    constexpr int SPLIT = mnb_split(MT);
+    const size_t smem = mnb_mma_smem(MT, mnb_slots(mrows), SPLIT, mrows);
+    auto kern = mnb_mma_kernel<T, MT, 2, SPLIT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return check_cuda(e, "MatMulNBits smem attribute");
+    }
+    kern<<<(unsigned)(n / 16), 32 * SPLIT, smem, stream>>>(tm_codes, tm_scales, tm_act, static_cast<const T *>(bias),
+                                                           static_cast<T *>(y), (int)m, (int)n, (int)k);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "MatMulNBits mma launch");
+}
+
+template <typename T>
+int launch_mma_rows(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
+                    int64_t n, int64_t k, cudaStream_t stream) {
+    if (m <= 8) return launch_mma<T, 1>(a, b, scales, bias, y, m, n, k, stream);
+    if (m <= 16) return launch_mma<T, 2>(a, b, scales, bias, y, m, n, k, stream);
+    if (m <= 32) return launch_mma<T, 4>(a, b, scales, bias, y, m, n, k, stream);
+    return launch_mma<T, 8>(a, b, scales, bias, y, m, n, k, stream);
+}
+
+// The tensor-core path takes fp16/bf16 activations with block 32, no zero
+// points, m <= 64, N a multiple of 16 and K a multiple of 1024 (whole chunks
+// per warp), the codes, activations and scales 16-byte aligned.
+bool mnb_mma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
+                      int64_t m, int64_t n, int64_t k, int block_size) {
+    if (dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16) return false;
+    if (zp || block_size != 32 || m < 1 || m > 64) return false;
+    if (n % 16 != 0 || k % (32 * kMnbMaxSplit * kMnbChunk) != 0 || n > (1 << 30) || k > (1 << 24)) return false;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(scales);
+    return (al & 15) == 0;
+}
+
 template <typename T>
 int launch_t(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, const void *bias, void *y,
              int64_t m, int64_t n, int64_t k, int block_size, cudaStream_t stream) {
@@ -121,6 +414,10 @@ int launch_t(const void *a, const uint8_t *b, const void *scales, const uint8_t 
 
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, const void *bias,
                         void *y, int dtype, int64_t m, int64_t n, int64_t k, int block_size, cudaStream_t stream) {
+    if (mnb_mma_eligible(a, b, scales, zp, dtype, m, n, k, block_size)) {
+        if (dtype == SA_DTYPE_FLOAT16) return launch_mma_rows<__half>(a, b, scales, bias, y, m, n, k, stream);
+        return launch_mma_rows<__nv_bfloat16>(a, b, scales, bias, y, m, n, k, stream);
+    }
     switch (dtype) {
         case SA_DTYPE_FLOAT: return launch_t<float>(a, b, scales, zp, bias, y, m, n, k, block_size, stream);
         case SA_DTYPE_FLOAT16: return launch_t<__half>(a, b, scales, zp, bias, y, m, n, k, block_size, stream);

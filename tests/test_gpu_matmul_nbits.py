@@ -70,6 +70,13 @@ def test_block_sizes_zero_points_bias(cuda_device, block):
     _run(cuda_device, 2, 200, 512, block=block, zp=True, bias=True, seed=block)
 
 
+@pytest.mark.parametrize("m", [1, 5, 8, 9, 16, 23, 33, 64])
+@pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
+def test_tensor_core_path(cuda_device, m, adtype):
+    """The mma.sync path (fp16/bf16, block 32, default zero point, K % 1024 == 0, m <= 64)."""
+    _run(cuda_device, m, 512, 2048, adtype=adtype, bias=True, seed=100 + m)
+
+
 def test_bf16(cuda_device):
     _run(cuda_device, 4, 256, 2048, adtype=torch.bfloat16, seed=5)
 
