@@ -359,11 +359,176 @@ int launch_mma(const void *a, const uint8_t *b, const void *scales, const void *
     return check_cuda(cudaGetLastError(), "MatMulNBits mma launch");
 }
 
+// ---- tensor-core path, 17..64 rows: the activation tile is shared by the CTA ----
+// One CTA = 4 warps = 64 output columns over the whole K.  Thread 0 fetches,
+// per chunk of 8 k-blocks, the 64 x 128 B code tile (128-byte swizzle), the
+// 64 x 8 scales and the activations as four m x 64 sub-tiles (128-byte
+// swizzle, so the fragment loads of 8 rows hit distinct banks); every warp
+// dequantizes its 16 columns once per block and runs the m-tiles against it.
+// A block-wide barrier after each chunk frees its slot for the next copy.
+constexpr int kMnbWideWarps = 4;
+constexpr int kMnbWideSlots = 2;
+
+template <typename T, int MT>
+__global__ void __launch_bounds__(32 * kMnbWideWarps)
+    mnb_mma_wide_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
+                        const __grid_constant__ CUtensorMap tm_act, const T *__restrict__ bias, T *__restrict__ y,
+                        int m, int n, int k) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int mpad = (m + 7) & ~7;
+    const int act_sub = mpad * 128;                         // one m x 64 activation sub-tile
+    const int code_bytes = 64 * 128, scale_bytes = 64 * kMnbChunk * 2;
+    const int slot_bytes = code_bytes + 4 * act_sub + ((scale_bytes + 1023) & ~1023);  // keeps 1024 alignment
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kMnbWideSlots * slot_bytes);
+    const int n0 = blockIdx.x * 64;
+    const int nchunks = k / (32 * kMnbChunk);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kMnbWideSlots; i++) mbar_init(full + i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    auto issue = [&](int c) {  // thread 0
+        const int sl = c % kMnbWideSlots;
+        unsigned char *base = smem + sl * slot_bytes;
+        const int blk = c * kMnbChunk;
+        mbar_expect_tx(full + sl, code_bytes + scale_bytes + 4 * m * 128);
+        tma_load_2d(base, &tm_codes, blk * 16, n0, full + sl);
+        for (int sb = 0; sb < 4; sb++) tma_load_2d(base + code_bytes + sb * act_sub, &tm_act, blk * 32 + sb * 64, 0, full + sl);
+        tma_load_2d(base + code_bytes + 4 * act_sub, &tm_scales, blk, n0, full + sl);
+    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < kMnbWideSlots && c < nchunks; c++) issue(c);
+
+    float tot[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) tot[mt][0] = tot[mt][1] = tot[mt][2] = tot[mt][3] = 0.0f;
+    const int r0 = 16 * warp + g;  // this lane's rows (output columns) of the 64-row tiles: r0, r0 + 8
+    bool ok = true;
+    int c = 0;
+    for (; c < nchunks; c++) {
+        const int sl = c % kMnbWideSlots;
+        if (ok && !mbar_wait_bounded(full + sl, (uint32_t)((c / kMnbWideSlots) & 1))) ok = false;
+        const int fail = __syncthreads_or(!ok);
+        if (fail) {
+            ok = false;
+            break;
+        }
+        const unsigned char *ct = smem + sl * slot_bytes;
+        const unsigned char *at = ct + code_bytes;
+        const T *st = reinterpret_cast<const T *>(ct + code_bytes + 4 * act_sub);
+#pragma unroll 2
+        for (int bi = 0; bi < kMnbChunk; bi++) {
+            const int u = ((bi ^ g) & 7) * 16 + 4 * t;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + r0 * 128 + u);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (r0 + 8) * 128 + u);
+            const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
+                           p11 = dq_pair<T>(w1, 1);
+            const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
+                           p13 = dq_pair<T>(w1, 3);
+            const float sg = DT<T>::to_f32(st[r0 * kMnbChunk + bi]);
+            const float sg8 = DT<T>::to_f32(st[(r0 + 8) * kMnbChunk + bi]);
+            // activation row r of block bi: sub-tile bi/2, 16-byte unit (bi&1)*4 + t, swizzled with r & 7
+            const unsigned char *ab = at + (bi >> 1) * act_sub + ((((bi & 1) * 4 + t) ^ g) & 7) * 16;
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                const int row = mt * 8 + g;
+                uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                if (row < m) x = *reinterpret_cast<const uint4 *>(ab + row * 128);
+                float acc[4];
+                mma_16816<T>(acc, p00, p10, p01, p11, __byte_perm(x.x, x.z, 0x5410), __byte_perm(x.x, x.z, 0x7632),
+                             true);
+                mma_16816<T>(acc, p02, p12, p03, p13, __byte_perm(x.y, x.w, 0x5410), __byte_perm(x.y, x.w, 0x7632),
+                             false);
+                tot[mt][0] = fmaf(sg, acc[0], tot[mt][0]);
+                tot[mt][1] = fmaf(sg, acc[1], tot[mt][1]);
+                tot[mt][2] = fmaf(sg8, acc[2], tot[mt][2]);
+                tot[mt][3] = fmaf(sg8, acc[3], tot[mt][3]);
+            }
+        }
+        __syncthreads();  // every warp is done with this slot
+        if (threadIdx.x == 0 && c + kMnbWideSlots < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            issue(c + kMnbWideSlots);
+        }
+    }
+    if (!ok) {
+        // chunk c never landed for some thread: let chunks c .. c + slots - 1 (issued, not consumed) land
+        if (threadIdx.x == 0)
+            for (int cc = c; cc < c + kMnbWideSlots && cc < nchunks; cc++)
+                mbar_wait_bounded(full + cc % kMnbWideSlots, (uint32_t)((cc / kMnbWideSlots) & 1));
+        return;
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int row = mt * 8 + 2 * t + (j & 1);
+            const int col = n0 + r0 + ((j & 2) ? 8 : 0);
+            if (row < m) {
+                float v = tot[mt][j];
+                if (bias) v += DT<T>::to_f32(bias[col]);
+                st_from_f32(y + (int64_t)row * n + col, v);
+            }
+        }
+    }
+}
+
+size_t mnb_wide_smem(int m) {
+    const int mpad = (m + 7) & ~7;
+    const size_t slot = 64 * 128 + 4 * (size_t)mpad * 128 + (((size_t)64 * kMnbChunk * 2 + 1023) & ~(size_t)1023);
+    return 1024 + kMnbWideSlots * slot + kMnbWideSlots * 8;
+}
+
+template <typename T, int MT>
+int launch_mma_wide(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
+                    int64_t n, int64_t k, cudaStream_t stream) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap tm_codes, tm_scales, tm_act;
+    const cuuint32_t ones[2] = {1, 1};
+    const cuuint64_t cdim[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n}, cstride[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t cbox[2] = {kMnbChunk * 16, 64};
+    CUresult r = encode(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(b), cdim, cstride, cbox,
+                        ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: code tensor map (%d)", (int)r);
+    const cuuint64_t sdim[2] = {(cuuint64_t)(k / 32), (cuuint64_t)n}, sstride[1] = {(cuuint64_t)(k / 32) * 2};
+    const cuuint32_t sbox[2] = {kMnbChunk, 64};
+    r = encode(&tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(scales), sdim, sstride, sbox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: scale tensor map (%d)", (int)r);
+    const cuuint64_t adim[2] = {(cuuint64_t)k, (cuuint64_t)m}, astride[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t abox[2] = {64, (cuuint32_t)m};
+    r = encode(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(a), adim, astride, abox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: activation tensor map (%d)", (int)r);
+    const size_t smem = mnb_wide_smem((int)m);
+    auto kern = mnb_mma_wide_kernel<T, MT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return check_cuda(e, "MatMulNBits smem attribute");
+    }
+    kern<<<(unsigned)(n / 64), 32 * kMnbWideWarps, smem, stream>>>(tm_codes, tm_scales, tm_act,
+                                                                  static_cast<const T *>(bias), static_cast<T *>(y),
+                                                                  (int)m, (int)n, (int)k);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "MatMulNBits wide mma launch");
+}
+
 template <typename T>
 int launch_mma_rows(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
                     int64_t n, int64_t k, cudaStream_t stream) {
     if (m <= 8) return launch_mma<T, 1>(a, b, scales, bias, y, m, n, k, stream);
     if (m <= 16) return launch_mma<T, 2>(a, b, scales, bias, y, m, n, k, stream);
+    if (n % 64 == 0) {  // the CTA shares one activation tile among 64 columns
+        if (m <= 32) return launch_mma_wide<T, 4>(a, b, scales, bias, y, m, n, k, stream);
+        return launch_mma_wide<T, 8>(a, b, scales, bias, y, m, n, k, stream);
+    }
     if (m <= 32) return launch_mma<T, 4>(a, b, scales, bias, y, m, n, k, stream);
     return launch_mma<T, 8>(a, b, scales, bias, y, m, n, k, stream);
 }

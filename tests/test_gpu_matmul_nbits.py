@@ -77,6 +77,12 @@ def test_tensor_core_path(cuda_device, m, adtype):
     _run(cuda_device, m, 512, 2048, adtype=adtype, bias=True, seed=100 + m)
 
 
+@pytest.mark.parametrize("m", [24, 64])
+def test_tensor_core_path_narrow_n(cuda_device, m):
+    """N a multiple of 16 but not of 64: the per-warp kernel instead of the CTA-shared one."""
+    _run(cuda_device, m, 272, 1024, adtype=torch.float16, bias=True, seed=200 + m)
+
+
 def test_bf16(cuda_device):
     _run(cuda_device, 4, 256, 2048, adtype=torch.bfloat16, seed=5)
 
