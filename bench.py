@@ -273,16 +273,23 @@ def run_matmul_nbits(args):
     a = torch.randn(m, k, device=dev, generator=g).half()
     y = torch.empty(m, n, dtype=torch.half, device=dev)
     stream = torch.cuda.current_stream(dev)
+    packed = [sa.PackedNBitsWeight(c, s, K=k, N=n, block_size=blk) for c, s in sets] if args.packed else None
+
+    def call(i):
+        if packed is not None:
+            sa.matmul_nbits_packed(a, packed[i % 6], out=y)
+        else:
+            c, s = sets[i % 6]
+            sa.matmul_nbits(a, c, s, K=k, N=n, block_size=blk, out=y)
+
     for i in range(max(args.warmup, 3)):
-        c, s = sets[i % 6]
-        sa.matmul_nbits(a, c, s, K=k, N=n, block_size=blk, out=y)
+        call(i)
     torch.cuda.synchronize(dev)
     l0 = lib.sa_kernel_launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        c, s = sets[i % 6]
-        sa.matmul_nbits(a, c, s, K=k, N=n, block_size=blk, out=y)
+        call(i)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     launches = lib.sa_kernel_launches() - l0
@@ -296,6 +303,7 @@ def run_matmul_nbits(args):
             "warmup": max(args.warmup, 3), "ms_per_step": t_ms, "dtype": "int4-w/fp16-act/f32-acc",
             "data": "synthetic (codes U{0..255} bytes, scales U[0.005, 0.02])",
             "config": {"workload": "matmul-nbits (BASELINE config 2)", "m": m, "n": n, "k": k, "block": blk,
+                       "weights": "prepacked (sa_matmul_nbits_prepack)" if args.packed else "ORT layout",
                        "l2": "six weight sets cycled (198 MB > L2)"},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -314,6 +322,7 @@ def main():
     ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits"],
                     help="gqa_decode = the headline (config 3); matmul_nbits = config 2, one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
+    ap.add_argument("--packed", action="store_true", help="matmul_nbits: weights prepacked once (m <= 8)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every step from the host instead of replaying a CUDA graph of one step")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],

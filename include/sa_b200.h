@@ -267,6 +267,28 @@ int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales,
                     int32_t dtype, int64_t m, int64_t n, int64_t k,
                     int32_t bits, int32_t block_size, sa_stream_t stream);
 
+/* Prepacked MatMulNBits weights (decode, m <= 8).  Model weights are
+ * constant, so the host repacks each one once at load time -- as ONNX
+ * Runtime's MatMulNBits PrePack does -- into a layout whose every chunk the
+ * kernel streams is one contiguous 9 KB run: per 32 output columns and per
+ * 512 k, the columns' codes (pre-swizzled for conflict-free fragment loads)
+ * followed by their scales.  Supported: 4-bit codes, block 32, fp16/bf16
+ * scales and activations, default zero point (8), n a multiple of 32 and k a
+ * multiple of 1024.
+ *
+ * sa_matmul_nbits_packed_bytes: size of the packed form; 0 if the shape,
+ * dtype or block size has no packed path.
+ * sa_matmul_nbits_prepack: writes the packed form of (b, scales) -- the same
+ * arguments as sa_matmul_nbits -- into `packed` (16-byte aligned, device).
+ * sa_matmul_nbits_packed: y = a . dequant(b)^T (+ bias) from the packed form;
+ * same numerics as sa_matmul_nbits (exact products, f32 accumulate). */
+int64_t sa_matmul_nbits_packed_bytes(int64_t n, int64_t k, int32_t bits, int32_t block_size, int32_t dtype);
+int sa_matmul_nbits_prepack(const uint8_t *b, const void *scales, void *packed, int32_t dtype,
+                            int64_t n, int64_t k, int32_t bits, int32_t block_size, sa_stream_t stream);
+int sa_matmul_nbits_packed(const void *a, const void *packed, const void *bias, void *y, int32_t dtype,
+                           int64_t m, int64_t n, int64_t k, int32_t bits, int32_t block_size,
+                           sa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

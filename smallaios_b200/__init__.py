@@ -7,12 +7,12 @@ MatMulNBits GEMV/GEMM, behind the C ABI in include/sa_b200.h
 operator interface; all compute runs in the CUDA library.
 """
 from .kv_cache import DEFAULT_SEED, GpuKvCache, LayerView
-from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatchCtx, OpError, ShapeMismatch,
-                  UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend, group_query_attention,
-                  matmul_nbits, supports_op)
+from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatchCtx, OpError, PackedNBitsWeight,
+                  ShapeMismatch, UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend,
+                  group_query_attention, matmul_nbits, matmul_nbits_packed, supports_op)
 
 __all__ = [
     "DEFAULT_SEED", "GpuKvCache", "LayerView", "CapacityError", "InternalError", "InvalidAttribute",
     "KvCacheDispatchCtx", "OpError", "ShapeMismatch", "UnsupportedOp", "dispatch_gpu_node", "finalize_kv_cache",
-    "gqa_attend", "group_query_attention", "matmul_nbits", "supports_op",
+    "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight", "supports_op",
 ]

@@ -35,6 +35,7 @@ EXPORTED = [
     "sa_kv_cache_set_position", "sa_kv_cache_advance", "sa_kv_cache_layer_view", "sa_kv_cache_get_config",
     "sa_kv_cache_device_status", "sa_kv_cache_set_gather",
     "sa_kv_append", "sa_gqa_attend", "sa_group_query_attention", "sa_matmul_nbits", "sa_gqa_attend_no_alloc",
+    "sa_matmul_nbits_packed_bytes", "sa_matmul_nbits_prepack", "sa_matmul_nbits_packed",
 ]
 SA_STATIC_SCRATCH_BYTES = 8 << 20
 
@@ -118,6 +119,12 @@ def _declare(l: ctypes.CDLL) -> None:
                                          _P, _P, _I32, _I32, _I32, _P]
     l.sa_matmul_nbits.restype = ctypes.c_int
     l.sa_matmul_nbits.argtypes = [_P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I64, _I32, _I32, _P]
+    l.sa_matmul_nbits_packed_bytes.restype = _I64
+    l.sa_matmul_nbits_packed_bytes.argtypes = [_I64, _I64, _I32, _I32, _I32]
+    l.sa_matmul_nbits_prepack.restype = ctypes.c_int
+    l.sa_matmul_nbits_prepack.argtypes = [_P, _P, _P, _I32, _I64, _I64, _I32, _I32, _P]
+    l.sa_matmul_nbits_packed.restype = ctypes.c_int
+    l.sa_matmul_nbits_packed.argtypes = [_P, _P, _P, _P, _I32, _I64, _I64, _I64, _I32, _I32, _P]
 
 
 def _load() -> ctypes.CDLL:

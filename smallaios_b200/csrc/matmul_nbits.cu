@@ -571,6 +571,191 @@ int launch_mma_wide(const void *a, const uint8_t *b, const void *scales, const v
     return check_cuda(cudaGetLastError(), "MatMulNBits wide mma launch");
 }
 
+// ---- prepacked weights -------------------------------------------------------
+// Model weights are constant, so a host framework can repack them once at load
+// (ONNX Runtime's MatMulNBits prepacks too).  The packed layout makes every
+// chunk a warp streams one contiguous 9 KB run of HBM: per 32-column tile and
+// per 16 k-blocks (512 codes), the 32 columns' 256-byte code runs followed by
+// their 32 x 16 fp16 scales.  Inside a column's run, 16-byte unit u is stored
+// at unit (u & 8) | ((u ^ column) & 7), so the fragment loads of 8 columns hit
+// 32 distinct shared-memory banks.  A tile's chunks are consecutive.
+constexpr int kPackCols = 32;                                 // columns per tile
+constexpr int kPackBlocks = 16;                               // k-blocks per chunk
+constexpr int kPackCodeBytes = kPackCols * kPackBlocks * 16;  // 8192
+constexpr int kPackChunkBytes = kPackCodeBytes + kPackCols * kPackBlocks * 2;  // + scales = 9216
+constexpr int kPackSplit = 2;                                 // warps (K splits) per CTA
+
+__host__ __device__ inline int64_t pack_chunk_offset(int64_t tile, int64_t chunk, int64_t nchunks) {
+    return (tile * nchunks + chunk) * kPackChunkBytes;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) mnb_prepack_kernel(const uint8_t *__restrict__ b, const T *__restrict__ scales,
+                                                          uint8_t *__restrict__ packed, int n, int k) {
+    const int64_t nchunks = k / (32 * kPackBlocks);
+    const int64_t tile = blockIdx.y, chunk = blockIdx.x;
+    uint8_t *dst = packed + pack_chunk_offset(tile, chunk, nchunks);
+    const int nblk = k / 32;
+    // codes: 32 columns x 16 units of 16 bytes
+    for (int i = threadIdx.x; i < kPackCols * kPackBlocks; i += blockDim.x) {
+        const int col = i / kPackBlocks, u = i % kPackBlocks;
+        const int64_t ncol = tile * kPackCols + col;
+        const uint4 v = *reinterpret_cast<const uint4 *>(b + ncol * (k / 2) + (chunk * kPackBlocks + u) * 16);
+        const int us = (u & 8) | ((u ^ col) & 7);
+        *reinterpret_cast<uint4 *>(dst + col * kPackBlocks * 16 + us * 16) = v;
+    }
+    // scales: [32 columns][16 blocks]
+    T *sd = reinterpret_cast<T *>(dst + kPackCodeBytes);
+    for (int i = threadIdx.x; i < kPackCols * kPackBlocks; i += blockDim.x) {
+        const int col = i / kPackBlocks, bi = i % kPackBlocks;
+        sd[i] = scales[(tile * kPackCols + col) * (int64_t)nblk + chunk * kPackBlocks + bi];
+    }
+}
+
+// m <= 8 rows against prepacked weights: one CTA = one 32-column tile and
+// kPackSplit warps splitting K; per chunk, one 1-D bulk copy of the packed
+// run and two TMA copies of the m x 256 activation halves.
+template <typename T>
+__global__ void __launch_bounds__(32 * kPackSplit)
+    mnb_packed_kernel(const uint8_t *__restrict__ packed, const __grid_constant__ CUtensorMap tm_act,
+                      const T *__restrict__ bias, T *__restrict__ y, int m, int n, int k) {
+    constexpr int NS = 2;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int act_row = kPackBlocks * 64;  // bytes of one activation row per chunk
+    const int slot_bytes = kPackChunkBytes + ((m * act_row + 127) / 128) * 128;
+    unsigned char *slots = smem + warp * NS * slot_bytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kPackSplit * NS * slot_bytes) + warp * NS;
+    float *red = reinterpret_cast<float *>(smem + kPackSplit * NS * slot_bytes + kPackSplit * NS * 8);
+
+    const int64_t tile = blockIdx.x;
+    const int n0 = (int)tile * kPackCols;
+    const int nchunks_all = k / (32 * kPackBlocks);
+    const int nchunks = nchunks_all / kPackSplit;
+    const int c0 = warp * nchunks;
+    if (lane == 0) {
+        for (int i = 0; i < NS; i++) mbar_init(bars + i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncwarp();
+    auto issue = [&](int c) {  // lane 0: chunk c -> slot c % NS
+        const int s = c % NS;
+        unsigned char *dst = slots + s * slot_bytes;
+        mbar_expect_tx(bars + s, kPackChunkBytes + m * act_row);
+        bulk_g2s(dst, packed + pack_chunk_offset(tile, c0 + c, nchunks_all), kPackChunkBytes, bars + s);
+        const int kk = (c0 + c) * kPackBlocks * 32;
+        tma_load_2d(dst + kPackChunkBytes, &tm_act, kk, 0, bars + s);
+        tma_load_2d(dst + kPackChunkBytes + m * 512, &tm_act, kk + 256, 0, bars + s);
+    };
+    if (lane == 0)
+        for (int c = 0; c < NS && c < nchunks; c++) issue(c);
+
+    float tot[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) tot[nt][0] = tot[nt][1] = tot[nt][2] = tot[nt][3] = 0.0f;
+    bool ok = true;
+    int c = 0;
+    for (; c < nchunks; c++) {
+        const int s = c % NS;
+        if (ok && !mbar_wait_bounded(bars + s, (uint32_t)((c / NS) & 1))) ok = false;
+        if (__any_sync(0xffffffffu, !ok)) break;
+        const unsigned char *ct = slots + s * slot_bytes;
+        const unsigned char *sc = ct + kPackCodeBytes;
+#pragma unroll
+        for (int sb = 0; sb < 2; sb++) {
+            const unsigned char *at = ct + kPackChunkBytes + sb * m * 512;  // [m][256] activations
+            uint4 srow[2][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                srow[nt][0] = *reinterpret_cast<const uint4 *>(sc + (16 * nt + g) * kPackBlocks * 2 + sb * 16);
+                srow[nt][1] = *reinterpret_cast<const uint4 *>(sc + (16 * nt + g + 8) * kPackBlocks * 2 + sb * 16);
+            }
+#pragma unroll
+            for (int bj = 0; bj < 8; bj++) {
+                const int bi = sb * 8 + bj;
+                uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                if (g < m) x = *reinterpret_cast<const uint4 *>(at + g * 512 + bj * 64 + 16 * t);
+                const uint32_t bf0 = __byte_perm(x.x, x.z, 0x5410), bf1 = __byte_perm(x.x, x.z, 0x7632);
+                const uint32_t bf2 = __byte_perm(x.y, x.w, 0x5410), bf3 = __byte_perm(x.y, x.w, 0x7632);
+                const int u = ((bi & 8) | ((bi ^ g) & 7)) * 16 + 4 * t;  // same unit for rows g and g + 8
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g) * 256 + u);
+                    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g + 8) * 256 + u);
+                    const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
+                                   p11 = dq_pair<T>(w1, 1);
+                    const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
+                                   p13 = dq_pair<T>(w1, 3);
+                    const uint32_t sw0 = (&srow[nt][0].x)[bj >> 1], sw1 = (&srow[nt][1].x)[bj >> 1];
+                    const T s0 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw0) + (bj & 1));
+                    const T s1 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw1) + (bj & 1));
+                    float acc[4];
+                    mma_16816<T>(acc, p00, p10, p01, p11, bf0, bf1, true);
+                    mma_16816<T>(acc, p02, p12, p03, p13, bf2, bf3, false);
+                    ffma2(tot[nt][0], tot[nt][1], DT<T>::to_f32(s0), acc[0], acc[1]);
+                    ffma2(tot[nt][2], tot[nt][3], DT<T>::to_f32(s1), acc[2], acc[3]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && c + NS < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            issue(c + NS);
+        }
+    }
+    if (!ok && lane == 0)
+        for (int cc = c; cc < c + NS && cc < nchunks; cc++)
+            mbar_wait_bounded(bars + cc % NS, (uint32_t)((cc / NS) & 1));
+    if (warp > 0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) red[((warp - 1) * 32 + lane) * 8 + nt * 4 + j] = tot[nt][j];
+    }
+    __syncthreads();
+    if (warp != 0 || !ok) return;
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float v = tot[nt][j];
+            for (int w = 1; w < kPackSplit; w++) v += red[((w - 1) * 32 + lane) * 8 + nt * 4 + j];
+            const int row = 2 * t + (j & 1);
+            const int col = n0 + 16 * nt + g + ((j & 2) ? 8 : 0);
+            if (row < m) {
+                if (bias) v += DT<T>::to_f32(bias[col]);
+                st_from_f32(y + (int64_t)row * n + col, v);
+            }
+        }
+    }
+}
+
+template <typename T>
+int launch_packed(const void *a, const uint8_t *packed, const void *bias, void *y, int64_t m, int64_t n, int64_t k,
+                  cudaStream_t stream) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap tm_act;
+    const cuuint64_t adim[2] = {(cuuint64_t)k, (cuuint64_t)m}, astride[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t abox[2] = {256, (cuuint32_t)m}, ones[2] = {1, 1};
+    CUresult r = encode(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(a), adim, astride, abox, ones,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: activation tensor map (%d)", (int)r);
+    const size_t slot = kPackChunkBytes + ((m * kPackBlocks * 64 + 127) / 128) * 128;
+    const size_t smem = (size_t)kPackSplit * 2 * slot + kPackSplit * 2 * 8 + (size_t)(kPackSplit - 1) * 32 * 8 * 4;
+    auto kern = mnb_packed_kernel<T>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return check_cuda(e, "MatMulNBits packed smem attribute");
+    }
+    kern<<<(unsigned)(n / kPackCols), 32 * kPackSplit, smem, stream>>>(packed, tm_act, static_cast<const T *>(bias),
+                                                                       static_cast<T *>(y), (int)m, (int)n, (int)k);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "MatMulNBits packed launch");
+}
+
 template <typename T>
 int launch_mma_rows(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
                     int64_t n, int64_t k, cudaStream_t stream) {
@@ -645,6 +830,36 @@ int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, con
             return launch_t<__nv_bfloat16>(a, b, scales, zp, bias, y, m, n, k, block_size, stream);
         default: return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits: dtype %d not supported", dtype);
     }
+}
+
+bool matmul_nbits_packable(int dtype, int64_t n, int64_t k, int block_size) {
+    return (dtype == SA_DTYPE_FLOAT16 || dtype == SA_DTYPE_BFLOAT16) && block_size == 32 && n > 0 &&
+           n % kPackCols == 0 && k > 0 && k % (32 * kPackBlocks * kPackSplit) == 0 && n <= (1 << 30) &&
+           k <= (1 << 24);
+}
+
+size_t matmul_nbits_packed_bytes(int64_t n, int64_t k) {
+    return (size_t)(n / kPackCols) * (size_t)(k / (32 * kPackBlocks)) * kPackChunkBytes;
+}
+
+int launch_matmul_nbits_prepack(const uint8_t *b, const void *scales, void *packed, int dtype, int64_t n, int64_t k,
+                                cudaStream_t stream) {
+    const dim3 grid((unsigned)(k / (32 * kPackBlocks)), (unsigned)(n / kPackCols));
+    if (dtype == SA_DTYPE_FLOAT16)
+        mnb_prepack_kernel<__half><<<grid, 256, 0, stream>>>(b, static_cast<const __half *>(scales),
+                                                            static_cast<uint8_t *>(packed), (int)n, (int)k);
+    else
+        mnb_prepack_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(b, static_cast<const __nv_bfloat16 *>(scales),
+                                                                   static_cast<uint8_t *>(packed), (int)n, (int)k);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "MatMulNBits prepack launch");
+}
+
+int launch_matmul_nbits_packed(const void *a, const void *packed, const void *bias, void *y, int dtype, int64_t m,
+                               int64_t n, int64_t k, cudaStream_t stream) {
+    const uint8_t *p = static_cast<const uint8_t *>(packed);
+    if (dtype == SA_DTYPE_FLOAT16) return launch_packed<__half>(a, p, bias, y, m, n, k, stream);
+    return launch_packed<__nv_bfloat16>(a, p, bias, y, m, n, k, stream);
 }
 
 }  // namespace sa

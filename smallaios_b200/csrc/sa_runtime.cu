@@ -526,6 +526,39 @@ int sa_group_query_attention(sa_kv_cache *cache, int32_t layer, const void *quer
                        value);
 }
 
+int64_t sa_matmul_nbits_packed_bytes(int64_t n, int64_t k, int32_t bits, int32_t block_size, int32_t dtype) {
+    if (bits != 4 || !matmul_nbits_packable(dtype, n, k, block_size)) return 0;
+    return (int64_t)matmul_nbits_packed_bytes(n, k);
+}
+
+int sa_matmul_nbits_prepack(const uint8_t *b, const void *scales, void *packed, int32_t dtype, int64_t n, int64_t k,
+                            int32_t bits, int32_t block_size, sa_stream_t stream) {
+    if (bits != 4) return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits prepack: bits=%d not supported (4 only)", bits);
+    if (!matmul_nbits_packable(dtype, n, k, block_size))
+        return set_error(SA_ERR_UNSUPPORTED,
+                         "MatMulNBits prepack: needs fp16/bf16, block 32, N %% 32 == 0, K %% 1024 == 0 "
+                         "(got dtype %d, block %d, N %lld, K %lld)",
+                         dtype, block_size, (long long)n, (long long)k);
+    if (!b || !scales || !packed) return set_error(SA_ERR_INVALID_ARGUMENT, "MatMulNBits prepack: NULL pointer");
+    if ((reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(packed)) & 15)
+        return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits prepack: B and packed must be 16-byte aligned");
+    return launch_matmul_nbits_prepack(b, scales, packed, dtype, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int sa_matmul_nbits_packed(const void *a, const void *packed, const void *bias, void *y, int32_t dtype, int64_t m,
+                           int64_t n, int64_t k, int32_t bits, int32_t block_size, sa_stream_t stream) {
+    if (bits != 4) return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits packed: bits=%d not supported (4 only)", bits);
+    if (!matmul_nbits_packable(dtype, n, k, block_size))
+        return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits packed: no packed path for this dtype/shape/block");
+    if (m < 0 || m > 8)
+        return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits packed: m=%lld rows (1..8 supported)", (long long)m);
+    if (m == 0) return SA_OK;
+    if (!a || !packed || !y) return set_error(SA_ERR_INVALID_ARGUMENT, "MatMulNBits packed: NULL input/output");
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(packed)) & 15)
+        return set_error(SA_ERR_UNSUPPORTED, "MatMulNBits packed: A and packed must be 16-byte aligned");
+    return launch_matmul_nbits_packed(a, packed, bias, y, dtype, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
 int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zero_points,
                     const void *bias, void *y, int32_t dtype, int64_t m, int64_t n, int64_t k, int32_t bits,
                     int32_t block_size, sa_stream_t stream) {

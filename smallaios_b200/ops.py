@@ -207,6 +207,48 @@ def matmul_nbits(a: torch.Tensor, b: torch.Tensor, scales: torch.Tensor, zero_po
     return out
 
 
+class PackedNBitsWeight:
+    """A MatMulNBits weight repacked once for the decode GEMV (``sa_matmul_nbits_prepack``).
+
+    Holds the packed device buffer; ``matmul_nbits_packed`` consumes it.  The
+    packed path needs fp16/bf16 scales, block 32, the default zero point, N a
+    multiple of 32 and K a multiple of 1024.
+    """
+
+    def __init__(self, b: torch.Tensor, scales: torch.Tensor, *, K: int, N: int, bits: int = 4,
+                 block_size: int = 32, stream=None):
+        _cuda(b, "B")
+        _cuda(scales, "scales")
+        nbytes = lib.sa_matmul_nbits_packed_bytes(N, K, bits, block_size, _dtype_code(scales))
+        if nbytes <= 0:
+            raise UnsupportedOp("MatMulNBits prepack: no packed path for this dtype/shape/block size")
+        self.K, self.N, self.bits, self.block_size, self.dtype = K, N, bits, block_size, scales.dtype
+        self.packed = torch.empty(nbytes, dtype=torch.uint8, device=b.device)
+        rc = lib.sa_matmul_nbits_prepack(b.data_ptr(), scales.data_ptr(), self.packed.data_ptr(),
+                                         _dtype_code(scales), N, K, bits, block_size,
+                                         _stream_handle(stream, b.device))
+        _raise_op(rc, "MatMulNBits prepack")
+
+
+def matmul_nbits_packed(a: torch.Tensor, w: PackedNBitsWeight, bias: torch.Tensor | None = None, *,
+                        out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """MatMulNBits (m <= 8 rows) against a ``PackedNBitsWeight``: same result as ``matmul_nbits``."""
+    _cuda(a, "A")
+    _cuda(bias, "bias")
+    if a.shape[-1] != w.K:
+        raise ShapeMismatch(f"MatMulNBits: A inner dim {a.shape[-1]} != K={w.K}")
+    if a.dtype != w.dtype:
+        raise UnsupportedOp("MatMulNBits: A must have the packed scales' dtype")
+    m = a.numel() // w.K
+    if out is None:
+        out = torch.empty(*a.shape[:-1], w.N, dtype=a.dtype, device=a.device)
+    rc = lib.sa_matmul_nbits_packed(a.data_ptr(), w.packed.data_ptr(), None if bias is None else bias.data_ptr(),
+                                    out.data_ptr(), _dtype_code(a), m, w.N, w.K, w.bits, w.block_size,
+                                    _stream_handle(stream, a.device))
+    _raise_op(rc, "MatMulNBits")
+    return out
+
+
 # ---- executor glue ------------------------------------------------------------
 SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits")
 

@@ -83,6 +83,33 @@ def test_tensor_core_path_narrow_n(cuda_device, m):
     _run(cuda_device, m, 272, 1024, adtype=torch.float16, bias=True, seed=200 + m)
 
 
+@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
+def test_packed_weights(cuda_device, m, adtype):
+    """Prepacked weights (decode GEMV path): same results as the oracle."""
+    import smallaios_b200 as sa
+
+    n, k = 1024, 2048
+    a, codes, scales, zps, bvec, want = _case(m, n, k, adtype=adtype, bias=True, seed=300 + m)
+    t = lambda x, dt: torch.from_numpy(x).to(dt).to(cuda_device)
+    w = sa.PackedNBitsWeight(t(codes, torch.uint8), t(scales, adtype), K=k, N=n)
+    y = sa.matmul_nbits_packed(t(a, adtype), w, t(bvec, adtype))
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    ulp = 2.0 ** -8 if adtype == torch.bfloat16 else 2.0 ** -11
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-3 + np.abs(want) * ulp), f"max err {err.max():.3e}"
+
+
+def test_packed_weights_rejects_unsupported(cuda_device):
+    import smallaios_b200 as sa
+
+    b = torch.zeros(48, 1024 // 2, dtype=torch.uint8, device=cuda_device)  # N = 48: not a multiple of 32
+    s = torch.zeros(48, 32, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(sa.UnsupportedOp):
+        sa.PackedNBitsWeight(b, s, K=1024, N=48)
+
+
 def test_bf16(cuda_device):
     _run(cuda_device, 4, 256, 2048, adtype=torch.bfloat16, seed=5)
 
