@@ -175,6 +175,46 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t w, int i) {
     }
 }
 
+// The four pairs of word w: p[0] = (n0, n4), p[1] = (n1, n5), p[2] = (n2, n6),
+// p[3] = (n3, n7) as (q - 8).  fp16 takes nibbles 1, 5, 3, 7 in place (bits
+// 4-7 of the mantissa, one shift less per word) as 16 (q - 8); the matching
+// activations are divided by 16 (mnb_act_scale_odd), which is exact.
+template <typename T>
+__device__ __forceinline__ void dq_word(uint32_t w, uint32_t (&p)[4]) {
+    if constexpr (std::is_same<T, __half>::value) {
+        const uint32_t w8 = w >> 8;
+        const __half2 o1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+        const __half2 o1152 = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+        uint32_t x[4];
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x[0]) : "r"(w), "r"(0x000F000Fu), "r"(0x64006400u));
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x[1]) : "r"(w), "r"(0x00F000F0u), "r"(0x64006400u));
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x[2]) : "r"(w8), "r"(0x000F000Fu), "r"(0x64006400u));
+        asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x[3]) : "r"(w8), "r"(0x00F000F0u), "r"(0x64006400u));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            __half2 h = *reinterpret_cast<__half2 *>(&x[i]);
+            h = __hsub2(h, (i & 1) ? o1152 : o1032);
+            p[i] = *reinterpret_cast<uint32_t *>(&h);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) p[i] = dq_pair<T>(w, i);
+    }
+}
+
+// Activation pair registers that meet the in-place high nibbles (b1, b3 of
+// a block) are scaled by 1/16 for fp16 (exact: a power of two).
+template <typename T>
+__device__ __forceinline__ uint32_t mnb_act_scale_odd(uint32_t v) {
+    if constexpr (std::is_same<T, __half>::value) {
+        __half2 h = *reinterpret_cast<__half2 *>(&v);
+        h = __hmul2(h, __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00)));  // 1/16
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        return v;
+    }
+}
+
 // 2-D tiled TMA load global -> shared (no multicast); x = inner coordinate.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -279,9 +319,9 @@ __global__ void __launch_bounds__(32 * SPLIT)
                 uint4 x = make_uint4(0u, 0u, 0u, 0u);
                 if (row < m) x = *reinterpret_cast<const uint4 *>(at + row * kMnbActRow + bi * 64 + 16 * t);
                 bf[mt][0] = __byte_perm(x.x, x.z, 0x5410);
-                bf[mt][1] = __byte_perm(x.x, x.z, 0x7632);
+                bf[mt][1] = mnb_act_scale_odd<T>(__byte_perm(x.x, x.z, 0x7632));
                 bf[mt][2] = __byte_perm(x.y, x.w, 0x5410);
-                bf[mt][3] = __byte_perm(x.y, x.w, 0x7632);
+                bf[mt][3] = mnb_act_scale_odd<T>(__byte_perm(x.y, x.w, 0x7632));
             }
             // rows g and g+8 of each 128-byte-swizzled 16-row tile: 16-byte unit bi sits at unit bi ^ (row & 7)
             const int u = ((bi ^ g) & 7) * 16 + 4 * t;
@@ -289,10 +329,11 @@ __global__ void __launch_bounds__(32 * SPLIT)
             for (int nt = 0; nt < NT; nt++) {
                 const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g) * 128 + u);
                 const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g + 8) * 128 + u);
-                const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
-                               p11 = dq_pair<T>(w1, 1);
-                const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
-                               p13 = dq_pair<T>(w1, 3);
+                uint32_t q0[4], q1[4];
+                dq_word<T>(w0, q0);
+                dq_word<T>(w1, q1);
+                const uint32_t p00 = q0[0], p10 = q1[0], p01 = q0[1], p11 = q1[1];
+                const uint32_t p02 = q0[2], p12 = q1[2], p03 = q0[3], p13 = q1[3];
                 const uint32_t sw0 = (&srow[nt][0].x)[bi >> 1], sw1 = (&srow[nt][1].x)[bi >> 1];
                 const T s0 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw0) + (bi & 1));
                 const T s1 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw1) + (bi & 1));
@@ -475,10 +516,11 @@ __global__ void __launch_bounds__(32 * kMnbWideWarps)
             const int u = ((bi ^ g) & 7) * 16 + 4 * t;
             const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + r0 * 128 + u);
             const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (r0 + 8) * 128 + u);
-            const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
-                           p11 = dq_pair<T>(w1, 1);
-            const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
-                           p13 = dq_pair<T>(w1, 3);
+            uint32_t q0[4], q1[4];
+            dq_word<T>(w0, q0);
+            dq_word<T>(w1, q1);
+            const uint32_t p00 = q0[0], p10 = q1[0], p01 = q0[1], p11 = q1[1];
+            const uint32_t p02 = q0[2], p12 = q1[2], p03 = q0[3], p13 = q1[3];
             const float sg = DT<T>::to_f32(st[r0 * kMnbChunk + bi]);
             const float sg8 = DT<T>::to_f32(st[(r0 + 8) * kMnbChunk + bi]);
             // activation row r of block bi: sub-tile bi/2, 16-byte unit (bi&1)*4 + t, swizzled with r & 7
@@ -489,10 +531,10 @@ __global__ void __launch_bounds__(32 * kMnbWideWarps)
                 uint4 x = make_uint4(0u, 0u, 0u, 0u);
                 if (row < m) x = *reinterpret_cast<const uint4 *>(ab + row * 128);
                 float acc[4];
-                mma_16816<T>(acc, p00, p10, p01, p11, __byte_perm(x.x, x.z, 0x5410), __byte_perm(x.x, x.z, 0x7632),
-                             true);
-                mma_16816<T>(acc, p02, p12, p03, p13, __byte_perm(x.y, x.w, 0x5410), __byte_perm(x.y, x.w, 0x7632),
-                             false);
+                mma_16816<T>(acc, p00, p10, p01, p11, __byte_perm(x.x, x.z, 0x5410),
+                             mnb_act_scale_odd<T>(__byte_perm(x.x, x.z, 0x7632)), true);
+                mma_16816<T>(acc, p02, p12, p03, p13, __byte_perm(x.y, x.w, 0x5410),
+                             mnb_act_scale_odd<T>(__byte_perm(x.y, x.w, 0x7632)), false);
                 tot[mt][0] = fmaf(sg, acc[0], tot[mt][0]);
                 tot[mt][1] = fmaf(sg, acc[1], tot[mt][1]);
                 tot[mt][2] = fmaf(sg8, acc[2], tot[mt][2]);
@@ -676,17 +718,20 @@ __global__ void __launch_bounds__(32 * kPackSplit)
                 const int bi = sb * 8 + bj;
                 uint4 x = make_uint4(0u, 0u, 0u, 0u);
                 if (g < m) x = *reinterpret_cast<const uint4 *>(at + g * 512 + bj * 64 + 16 * t);
-                const uint32_t bf0 = __byte_perm(x.x, x.z, 0x5410), bf1 = __byte_perm(x.x, x.z, 0x7632);
-                const uint32_t bf2 = __byte_perm(x.y, x.w, 0x5410), bf3 = __byte_perm(x.y, x.w, 0x7632);
+                const uint32_t bf0 = __byte_perm(x.x, x.z, 0x5410),
+                               bf1 = mnb_act_scale_odd<T>(__byte_perm(x.x, x.z, 0x7632));
+                const uint32_t bf2 = __byte_perm(x.y, x.w, 0x5410),
+                               bf3 = mnb_act_scale_odd<T>(__byte_perm(x.y, x.w, 0x7632));
                 const int u = ((bi & 8) | ((bi ^ g) & 7)) * 16 + 4 * t;  // same unit for rows g and g + 8
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
                     const uint32_t w0 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g) * 256 + u);
                     const uint32_t w1 = *reinterpret_cast<const uint32_t *>(ct + (16 * nt + g + 8) * 256 + u);
-                    const uint32_t p00 = dq_pair<T>(w0, 0), p10 = dq_pair<T>(w1, 0), p01 = dq_pair<T>(w0, 1),
-                                   p11 = dq_pair<T>(w1, 1);
-                    const uint32_t p02 = dq_pair<T>(w0, 2), p12 = dq_pair<T>(w1, 2), p03 = dq_pair<T>(w0, 3),
-                                   p13 = dq_pair<T>(w1, 3);
+                    uint32_t q0[4], q1[4];
+                    dq_word<T>(w0, q0);
+                    dq_word<T>(w1, q1);
+                    const uint32_t p00 = q0[0], p10 = q1[0], p01 = q0[1], p11 = q1[1];
+                    const uint32_t p02 = q0[2], p12 = q1[2], p03 = q0[3], p13 = q1[3];
                     const uint32_t sw0 = (&srow[nt][0].x)[bj >> 1], sw1 = (&srow[nt][1].x)[bj >> 1];
                     const T s0 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw0) + (bj & 1));
                     const T s1 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw1) + (bj & 1));
