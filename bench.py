@@ -43,15 +43,41 @@ NCU_TRAFFIC_DECODE_STREAM = 612_429_312
 CB = D * BITS // 8
 METRIC = "GQA decode tokens/s over int4-compressed KV (Llama-3-8B layer, B=64, T=8192)"
 UNIT = "tokens/s"
+WORKLOAD = "llama3-8b-layer-decode (BASELINE config 3)"
+
+# --config c5: the Llama-3-70B-shaped layer: 64 query / 8 KV
+# heads (8 per KV head), batch 128, context 32768; 4.8 GB of int4 cache.
+CONFIGS = {
+    "c3": dict(B=64, HQ=32, HKV=8, D=128, T=8192, BITS=4, THETA=500000.0, METRIC=METRIC, WORKLOAD=WORKLOAD,
+               NCU_TRAFFIC_PER_CALL=NCU_TRAFFIC_PER_CALL, NCU_TRAFFIC_DECODE_STREAM=NCU_TRAFFIC_DECODE_STREAM,
+               KERNEL_NOTE="gqa attend call: decode_prep + decode_stream + decode_merge (decode_stream is 88% of "
+                           "the call's device time)"),
+    "c5": dict(B=128, HQ=64, HKV=8, D=128, T=32768, BITS=4, THETA=500000.0,
+               METRIC="GQA decode tokens/s over int4-compressed KV (Llama-3-70B layer, B=128, T=32768)",
+               WORKLOAD="llama3-70b-layer-decode (BASELINE config 5)", NCU_TRAFFIC_PER_CALL=None,
+               NCU_TRAFFIC_DECODE_STREAM=None,
+               KERNEL_NOTE="gqa attend call: decode_prep8 + decode8_stream + decode_merge<8>"),
+}
 
 
-def algorithmic_bytes(b=B, hkv=HKV, t=T, hq=HQ, d=D, cb=CB, act=2):
+def select_config(name):
+    """Point the module's workload constants at BASELINE config `name`."""
+    g = globals()
+    g.update(CONFIGS[name])
+    g["CB"] = g["D"] * g["BITS"] // 8
+
+
+def algorithmic_bytes(b=None, hkv=None, t=None, hq=None, d=None, cb=None, act=2):
     """Per step: K+V codes and {scale, zp} of every cached token, q in, out, appended vectors."""
+    b, hkv, t, hq, d, cb = (x if x is not None else y for x, y in zip((b, hkv, t, hq, d, cb),
+                                                                     (B, HKV, T, HQ, D, CB)))
     cache = 2 * b * hkv * t * (cb + 8)
     return cache + b * hq * d * act * 2 + 2 * b * hkv * (cb + 8)
 
 
-def attend_bytes(b=B, hkv=HKV, t=T, hq=HQ, d=D, cb=CB, act=2):
+def attend_bytes(b=None, hkv=None, t=None, hq=None, d=None, cb=None, act=2):
+    b, hkv, t, hq, d, cb = (x if x is not None else y for x, y in zip((b, hkv, t, hq, d, cb),
+                                                                     (B, HKV, T, HQ, D, CB)))
     return 2 * b * hkv * t * (cb + 8) + b * hq * d * act * 2
 
 
@@ -116,7 +142,7 @@ def gpu_uuid(torch, dev):
         return str(dev.index)
 
 
-def build_workload(torch, sa, dev, seed, kv_begin=0, kv_count=HKV):
+def build_workload(torch, sa, dev, seed, kv_begin=0, kv_count=None):
     """Cache filled with T-1 tokens (seeded), plus the step's q/k/v.
 
     ``kv_begin``/``kv_count`` select a shard of the KV heads (and their query
@@ -125,6 +151,7 @@ def build_workload(torch, sa, dev, seed, kv_begin=0, kv_count=HKV):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     std = 1.28  # N(0,1) activations through N(0, 0.02) projections of width 4096
+    kv_count = HKV if kv_count is None else kv_count
     hkv, hq = kv_count, kv_count * (HQ // HKV)
     cache = sa.GpuKvCache(1, HKV, D, T, batch=B, num_heads=HQ, bits=BITS, kv_head_begin=kv_begin,
                           kv_head_count=kv_count, device=dev)
@@ -229,7 +256,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b-layer-decode", "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+        "config": {"workload": WORKLOAD, "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
                    "context": T, "kv_bits": BITS},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
                          "sample": f"{units} of {B * HKV} (batch row, kv head) units per step, scaled; the C "
@@ -335,6 +362,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS),
+                    help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
     ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits"],
                     help="gqa_decode = the headline (config 3); matmul_nbits = config 2, one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
@@ -351,6 +380,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    select_config(args.config)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "matmul_nbits":
@@ -497,7 +527,7 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True,
         "scaling": "strong" if heads else "weak", "vs_baseline": None,
         "dtype": "int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
-        "config": {"workload": "llama3-8b-layer-decode (BASELINE config 3)",
+        "config": {"workload": WORKLOAD,
                    "batch_per_gpu": B if not heads else f"{B} (kv heads {kv_count} of {HKV})",
                    "global_batch": B * rows_mult, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
                    "kv_bits": BITS, "rope_theta": THETA,
@@ -506,7 +536,7 @@ def main():
                                                                       if args.gather == "peer" else
                                                                       "NCCL all-gather of attn_out"))
                                    if heads else f"batch-sharded x{world} (no collective)"),
-                   "l2": "cache 604 MB > 126 MB L2 per step; no flush",
+                   "l2": f"cache {2 * B * HKV * T * (CB + 8) / 1e6:.0f} MB > 126 MB L2 per step; no flush",
                    "launch": "host launches" if args.no_graph else "CUDA graph of one step, replayed"},
         "gpu_launches": int(launches),
         "e2e": {"value": B * rows_mult / (e2e_ms * 1e-3), "unit": UNIT,
@@ -514,8 +544,7 @@ def main():
                 "d2h_bytes_per_step": int(hout.numel() * 2)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": NCU_TRAFFIC_PER_CALL, "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM,
-                     "kernel": "gqa attend call: decode_prep + decode_stream + decode_merge (decode_stream is 88% "
-                               "of the call's device time)", "launches_per_call": attend_launches,
+                     "kernel": KERNEL_NOTE, "launches_per_call": attend_launches,
                      "algorithmic_bytes": abytes, "ms_per_call": attend_ms,
                      "peak_source": f"{peak_kind} hbm_gbs"},
         "step_bytes": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)),  # per rank

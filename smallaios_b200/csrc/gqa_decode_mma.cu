@@ -1,5 +1,6 @@
 // Tensor-core decode attention over the PolarQuant cache: one query token per
-// sequence, 4/8-bit codes, head_dim 64/128, up to 4 query heads per KV head.
+// sequence, 4/8-bit codes, head_dim 64/128, up to 4 query heads per KV head
+// (5..8 heads: gqa_decode_g8.cu).
 //
 // Three launches per step:
 //
@@ -178,15 +179,9 @@ struct WGeo {
     static constexpr int VV = ((BITS == 4) ? NTV / 2 : NTV) / 4;  // 16-byte V loads per 16-token block
     static constexpr int QW = NCH * 4;                   // q-digit words per lane
     static constexpr int SCW = 4 * SCS;                  // floats of a warp's score buffer
-    static constexpr int REC = 4 * D + 16;               // floats per partial record: [4][D] values, R/L/Z x 4
+    static constexpr int REC = RecGeo<D, 4>::REC;        // floats per partial record: [4][D] values, R/L/Z x 4
     static constexpr int SMEM = kNW * 2 * SLOT + kNW * SCW * 4 + kNW * 12 * kTileW * 4 + 256;
 };
-
-// Warp owning flat chunk f when F chunks are cut into W ranges
-// [w*F/W, (w+1)*F/W): the largest w with w*F/W <= f.
-__host__ __device__ __forceinline__ int warp_of_chunk(int f, int F, int W) {
-    return (int)((((int64_t)f + 1) * W - 1) / F);
-}
 
 template <typename T, int BITS, int D>
 __global__ void __launch_bounds__(kNW * 32, 2)
@@ -564,79 +559,6 @@ __global__ void __launch_bounds__(kNW * 32, 2)
     }
 }
 
-// Merge of each unit's partial records (one warp per query head), then
-// normalisation, inverse rotation and the store.
-template <typename T, int BITS, int D>
-__global__ void __launch_bounds__(128) decode_merge_kernel(AttendArgs a, int ncu, int F, int W) {
-    using GG = WGeo<BITS, D>;
-    constexpr int EPL = D / 32;
-    const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
-    griddep_wait();  // the decode grid's records
-    if (g >= a.group) return;
-    const int u = blockIdx.x;
-    const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
-    const float *base = a.workspace + ((int64_t)u + w_lo) * GG::REC;  // record w_lo + u, then one per warp
-    const int nrec = w_hi - w_lo + 1;
-    // lane i handles the meta of records i, i + 32, ...
-    float M = -INFINITY;
-    for (int i = lane; i < nrec; i += 32) M = fmaxf(M, base[(int64_t)i * GG::REC + 4 * D + g]);
-    M = warp_max(M);
-    float x[EPL], L = 0.0f, Z = 0.0f;
-#pragma unroll
-    for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
-    for (int i0 = 0; i0 < nrec; i0 += 32) {
-        float wt = 0.0f;
-        if (i0 + lane < nrec) {
-            const float *m = base + (int64_t)(i0 + lane) * GG::REC + 4 * D;
-            const float Rw = m[g];
-            wt = Rw == -INFINITY ? 0.0f : exp2f(Rw - M);
-            L = fmaf(wt, m[4 + g], L);
-            Z = fmaf(wt, m[8 + g], Z);
-        }
-        const int n = min(32, nrec - i0);
-#pragma unroll 4
-        for (int j = 0; j < n; j++) {
-            const float wj = __shfl_sync(0xffffffffu, wt, j);
-            const float *v = base + (int64_t)(i0 + j) * GG::REC + g * D + lane * EPL;
-            if constexpr (EPL == 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(v);
-                x[0] = fmaf(wj, t.x, x[0]);
-                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
-                x[2 % EPL] = fmaf(wj, t.z, x[2 % EPL]);
-                x[3 % EPL] = fmaf(wj, t.w, x[3 % EPL]);
-            } else {
-                const float2 t = *reinterpret_cast<const float2 *>(v);
-                x[0] = fmaf(wj, t.x, x[0]);
-                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
-            }
-        }
-    }
-    L = warp_sum(L);
-    Z = warp_sum(Z);
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-#pragma unroll
-    for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
-    warp_wht_butterfly<EPL>(x, lane, D);
-    const int h = u % a.heads;
-    const float *sg = a.signs + (int64_t)h * D;
-#pragma unroll
-    for (int rr = 0; rr < EPL; rr++) x[rr] *= a.wht_scale * sg[lane * EPL + rr];
-    if (a.gather.n == 0) {
-        T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
-#pragma unroll
-        for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + lane * EPL + rr, x[rr]);
-    } else {
-        // head-sharded: row b, global query head col0 + h*G + g of every rank's buffer
-        const int64_t b = u / a.heads;
-        const int64_t off = (b * a.gather.cols + a.gather.col0 + (int64_t)h * a.group + g) * D + lane * EPL;
-        for (int r = 0; r < a.gather.n; r++) {
-            T *dst = static_cast<T *>(a.gather.p[r]) + off;
-#pragma unroll
-            for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + rr, x[rr]);
-        }
-    }
-}
-
 // Grid of the decode kernel: two CTAs per SM, no more warps than chunks.
 struct DecodeGrid {
     int ncu, F, W, ctas;
@@ -699,7 +621,7 @@ int launch_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream)
     cfg.gridDim = dim3((unsigned)(a.batch * a.heads));
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = 0;
-    rc = check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, BITS, D>, a, dg.ncu, dg.F, dg.W),
+    rc = check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, D, 4>, a, dg.ncu, dg.F, dg.W),
                     "gqa decode merge launch");
     count_launch();
     return rc;
@@ -717,22 +639,28 @@ int launch_dtype(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream)
 
 // Floats of partial records the decode needs: one per warp of the grid plus
 // one per unit (a warp's range touches one unit more than it crosses).
-size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim) {
+size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim, int group) {
+    if (group > 4) return decode8_workspace_floats(sm_count, units, head_dim);
     return (size_t)((int64_t)2 * sm_count * kNW + units) * (size_t)(4 * head_dim + 16);
 }
 
+// 32-bit words of the prep area per (row, KV head): the q-digit fragments of
+// 32 lanes, then the score constants.
+size_t decode_qprep_words(int group) { return group > 4 ? decode8_qprep_words() : 32 * 16 + 8; }
+
 // Whether the tensor-core decode handles this call.
 bool decode_fast_eligible(const AttendArgs &a) {
-    if (a.seq_len != 1 || a.group < 1 || a.group > 4) return false;
+    if (a.seq_len != 1 || a.group < 1 || a.group > 8) return false;
     if ((a.bits != 4 && a.bits != 8) || (a.head_dim != 64 && a.head_dim != 128)) return false;
     if (a.capacity % 64 != 0 || a.qprep == nullptr || a.dev_status == nullptr) return false;
     const int64_t units = (int64_t)a.batch * a.heads;
     if (units * ((a.pos0 + 32) / 32) >= ((int64_t)1 << 31)) return false;  // flat chunk indices are int
-    return decode_workspace_floats(a.sm_count, units, a.head_dim) <= a.workspace_floats;
+    return decode_workspace_floats(a.sm_count, units, a.head_dim, a.group) <= a.workspace_floats;
 }
 
 // Prep (+ append when `ap` is given), decode and merge of one query token per row.
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream) {
+    if (a.group > 4) return launch_gqa_decode8(a, ap, stream);
     switch (a.dtype) {
         case SA_DTYPE_FLOAT: return launch_dtype<float>(a, ap, stream);
         case SA_DTYPE_FLOAT16: return launch_dtype<__half>(a, ap, stream);

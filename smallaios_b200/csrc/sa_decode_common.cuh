@@ -6,6 +6,8 @@
 
 #include <stdint.h>
 
+#include "sa_append.cuh"
+
 namespace sa {
 namespace dec {
 
@@ -91,6 +93,95 @@ __device__ __forceinline__ void v_inv(int dim, int &nt, int &col) {
     } else {
         col = (dim >> 2) & 7;
         nt = 4 * (dim >> 5) + (dim & 3);
+    }
+}
+
+// ---- stream-K records and their merge -------------------------------------------
+// Warp owning flat chunk f when F chunks are cut into W ranges
+// [w*F/W, (w+1)*F/W): the largest w with w*F/W <= f.
+__host__ __device__ __forceinline__ int warp_of_chunk(int f, int F, int W) {
+    return (int)((((int64_t)f + 1) * W - 1) / F);
+}
+
+// Floats of one partial record holding HPR query heads: value sums
+// [HPR][D], then R, L, Z of each head (and HPR floats of padding).
+template <int D, int HPR>
+struct RecGeo {
+    static constexpr int REC = HPR * D + 4 * HPR;
+    static constexpr int R = HPR * D, L = HPR * D + HPR, Z = HPR * D + 2 * HPR;
+};
+
+// Merge of each unit's partial records (one warp per query head), then
+// normalisation, inverse rotation and the store.  The records of unit u are
+// w_lo + u .. w_hi + u, one per decode warp whose range touched the unit.
+template <typename T, int D, int HPR>
+__global__ void __launch_bounds__(32 * HPR) decode_merge_kernel(AttendArgs a, int ncu, int F, int W) {
+    using RG = RecGeo<D, HPR>;
+    constexpr int EPL = D / 32;
+    const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+    griddep_wait();  // the decode grid's records
+    if (g >= a.group) return;
+    const int u = blockIdx.x;
+    const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
+    const float *base = a.workspace + ((int64_t)u + w_lo) * RG::REC;  // record w_lo + u, then one per warp
+    const int nrec = w_hi - w_lo + 1;
+    // lane i handles the meta of records i, i + 32, ...
+    float M = -INFINITY;
+    for (int i = lane; i < nrec; i += 32) M = fmaxf(M, base[(int64_t)i * RG::REC + RG::R + g]);
+    M = warp_max(M);
+    float x[EPL], L = 0.0f, Z = 0.0f;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
+    for (int i0 = 0; i0 < nrec; i0 += 32) {
+        float wt = 0.0f;
+        if (i0 + lane < nrec) {
+            const float *m = base + (int64_t)(i0 + lane) * RG::REC;
+            const float Rw = m[RG::R + g];
+            wt = Rw == -INFINITY ? 0.0f : exp2f(Rw - M);
+            L = fmaf(wt, m[RG::L + g], L);
+            Z = fmaf(wt, m[RG::Z + g], Z);
+        }
+        const int n = min(32, nrec - i0);
+#pragma unroll 4
+        for (int j = 0; j < n; j++) {
+            const float wj = __shfl_sync(0xffffffffu, wt, j);
+            const float *v = base + (int64_t)(i0 + j) * RG::REC + g * D + lane * EPL;
+            if constexpr (EPL == 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(v);
+                x[0] = fmaf(wj, t.x, x[0]);
+                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
+                x[2 % EPL] = fmaf(wj, t.z, x[2 % EPL]);
+                x[3 % EPL] = fmaf(wj, t.w, x[3 % EPL]);
+            } else {
+                const float2 t = *reinterpret_cast<const float2 *>(v);
+                x[0] = fmaf(wj, t.x, x[0]);
+                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
+            }
+        }
+    }
+    L = warp_sum(L);
+    Z = warp_sum(Z);
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
+    warp_wht_butterfly<EPL>(x, lane, D);
+    const int h = u % a.heads;
+    const float *sg = a.signs + (int64_t)h * D;
+#pragma unroll
+    for (int rr = 0; rr < EPL; rr++) x[rr] *= a.wht_scale * sg[lane * EPL + rr];
+    if (a.gather.n == 0) {
+        T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
+#pragma unroll
+        for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + lane * EPL + rr, x[rr]);
+    } else {
+        // head-sharded: row b, global query head col0 + h*G + g of every rank's buffer
+        const int64_t b = u / a.heads;
+        const int64_t off = (b * a.gather.cols + a.gather.col0 + (int64_t)h * a.group + g) * D + lane * EPL;
+        for (int r = 0; r < a.gather.n; r++) {
+            T *dst = static_cast<T *>(a.gather.p[r]) + off;
+#pragma unroll
+            for (int rr = 0; rr < EPL; rr++) st_from_f32(dst + rr, x[rr]);
+        }
     }
 }
 

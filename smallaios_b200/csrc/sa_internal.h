@@ -52,7 +52,7 @@ struct kv_cache_impl {
     float *signs;      // [L][H][D]  +-1.0f
     float *workspace;  // split-K partials
     size_t workspace_floats;
-    uint32_t *qprep;   // [B*H*32*16] q-digit words + [B*H*8] score constants
+    uint32_t *qprep;   // [B*H] x decode_qprep_words(group): q-digit words, then score constants
     int *dev_status;   // one int: device-side status bits
     GatherOut gather;  // head-sharded output buffers (n = 0: off)
     size_t layer_codes_bytes;  // B*H*T*CB
@@ -100,7 +100,11 @@ int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
 int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream);
 bool decode_fast_eligible(const AttendArgs &a);
-size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim);
+size_t decode_workspace_floats(int sm_count, int64_t units, int head_dim, int group);
+size_t decode_qprep_words(int group);
+size_t decode8_workspace_floats(int sm_count, int64_t units, int head_dim);
+size_t decode8_qprep_words();
+int launch_gqa_decode8(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,

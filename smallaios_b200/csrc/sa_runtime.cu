@@ -147,14 +147,14 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->layer_codes_bytes = B * H * T * k->code_bytes;
     k->layer_meta_floats = B * H * T * 2;
     k->workspace_floats = B * H * (size_t)kMaxSplits * k->group * (D + 4);
-    const size_t dec_ws = decode_workspace_floats(k->sm_count, (int64_t)(B * H), (int)D);
+    const size_t dec_ws = decode_workspace_floats(k->sm_count, (int64_t)(B * H), (int)D, k->group);
     if (dec_ws > k->workspace_floats) k->workspace_floats = dec_ws;
     auto up = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t codes = up(L * k->layer_codes_bytes);
     const size_t meta = up(L * k->layer_meta_floats * sizeof(float));
     const size_t signs = up(L * H * D * sizeof(float));
     const size_t ws = up(k->workspace_floats * sizeof(float));
-    const size_t qp = up(B * H * (32 * 16 + 8) * sizeof(uint32_t));
+    const size_t qp = up(B * H * decode_qprep_words(k->group) * sizeof(uint32_t));
     const size_t st = 256;
     k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st;
     const size_t k_bytes = k->base_bytes;

@@ -114,6 +114,38 @@ def test_head_dims_and_groups(cuda_device, d, hq, hkv):
     _check(got, want, torch.float32)
 
 
+def test_c5_shape_group8_int4(cuda_device):
+    """Llama-3-70B layer shape (64/8 heads: 8 query heads per KV head, D=128, int4, theta 5e5) at B=2."""
+    got, want = _decode_case(cuda_device, b=2, hq=64, hkv=8, d=128, bits=4, t=1500, theta=500000.0, seed=21,
+                             chunks=(256, 100, 7))
+    _check(got, want, torch.float32)
+
+
+@pytest.mark.parametrize("d,hq,hkv,bits", [(128, 16, 2, 8), (64, 10, 2, 4), (64, 14, 2, 8), (128, 12, 2, 4),
+                                           (64, 8, 1, 4)])
+def test_groups_five_to_eight(cuda_device, d, hq, hkv, bits):
+    """5..8 query heads per KV head (the eight-head decode kernel, unused heads zero)."""
+    got, want = _decode_case(cuda_device, b=3, hq=hq, hkv=hkv, d=d, bits=bits, t=421, seed=d + hq + bits)
+    _check(got, want, torch.float32)
+
+
+def test_group8_first_tokens_and_long_context(cuda_device):
+    """Group 8: contexts of 1-3 and 65 tokens, then one row of 6000 tokens cut into many warp ranges."""
+    for t in (1, 2, 3, 65):
+        got, want = _decode_case(cuda_device, b=1, hq=8, hkv=1, d=128, bits=4, t=t, seed=40 + t)
+        _check(got, want, torch.float32)
+    got, want = _decode_case(cuda_device, b=1, hq=16, hkv=2, d=128, bits=4, t=6000, seed=47, chunks=(1000,),
+                             theta=500000.0)
+    _check(got, want, torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_group8_half_dtypes(cuda_device, dtype):
+    got, want = _decode_case(cuda_device, b=3, hq=64, hkv=8, d=128, bits=4, t=300, dtype=dtype, seed=48,
+                             theta=500000.0)
+    _check(got, want, dtype)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_half_dtypes(cuda_device, dtype):
     got, want = _decode_case(cuda_device, b=3, hq=32, hkv=8, d=128, bits=4, t=700, dtype=dtype, seed=4,
