@@ -479,11 +479,9 @@ __global__ void __launch_bounds__(kNW8 * 32, 1)
                     }
 #pragma unroll
                     for (int cc = 0; cc < 2; cc++) {
-                        float fe = (float)pacc[2 * np][cc] * w_a, fo = (float)pacc[2 * np + 1][cc] * w_a;
-                        if (lo) {
-                            fe += (float)pacc[2 * np][2 + cc];
-                            fo += (float)pacc[2 * np + 1][2 + cc];
-                        }
+                        // rows 12-15 of the P tile are zero, so c2/c3 of lanes >= 16 add nothing
+                        const float fe = fmaf((float)pacc[2 * np][cc], w_a, (float)pacc[2 * np][2 + cc]);
+                        const float fo = fmaf((float)pacc[2 * np + 1][cc], w_a, (float)pacc[2 * np + 1][2 + cc]);
                         const float recv = __shfl_xor_sync(0xffffffffu, lo ? fo : fe, 16);
                         facc[hh][2 * np + cc] = fmaf((lo ? fe : fo) + recv, ntw, facc[hh][2 * np + cc]);
                     }

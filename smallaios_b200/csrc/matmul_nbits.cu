@@ -1,8 +1,10 @@
 // MatMulNBits (ORT com.microsoft.MatMulNBits contract), int4 weights with
 // per-(column, k-block) scales and optional packed zero points.
 //
-// Tensor-core path (m <= 16, fp16/bf16 activations, block 32, default zero
-// point): see mnb_mma_kernel below.  Other shapes take the CUDA-core path:
+// tcgen05 path (matmul_nbits_umma.cu): fp16/bf16, block 32, default zero
+// point, 17 <= m <= 128, N % 128 == 0, K % 256 == 0.  mma.sync path (m <= 64,
+// the same types, N % 16 == 0): mnb_mma_kernel below.  Other shapes take the
+// CUDA-core path:
 //
 // GEMV path (m <= 8 rows per pass): one warp per output column streams that
 // column's packed codes with 128-bit loads (16 bytes = 32 codes per lane per
@@ -18,6 +20,7 @@
 #include "sa_async.cuh"
 #include "sa_common.cuh"
 #include "sa_internal.h"
+#include "sa_tma.cuh"
 
 namespace sa {
 
@@ -215,15 +218,6 @@ __device__ __forceinline__ uint32_t mnb_act_scale_odd(uint32_t v) {
     }
 }
 
-// 2-D tiled TMA load global -> shared (no multicast); x = inner coordinate.
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
 // (fma.rn.f32x2) d = s * a + d on two lanes of packed f32.
 __device__ __forceinline__ void ffma2(float &d0, float &d1, float s, float a0, float a1) {
     asm("{\n.reg .b64 dd, aa, ss;\nmov.b64 aa, {%2, %3};\nmov.b64 ss, {%4, %4};\nmov.b64 dd, {%0, %1};\n"
@@ -397,19 +391,6 @@ constexpr size_t mnb_mma_smem(int mt, int ns, int split, int nt, int sub, int mr
            (size_t)split * ns *
                (nt * sub * (kMnbCodeTile + kMnbScaleTile) + ((mrows * sub * kMnbActRow + 127) / 128) * 128) +
            split * ns * 8 + (size_t)(split - 1) * 32 * mt * nt * 4 * 4;
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }();
-    return fn;
 }
 
 template <typename T, int MT, int NT, int SUB = 1, int SPLIT = mnb_split(MT)>
@@ -864,6 +845,8 @@ int launch_t(const void *a, const uint8_t *b, const void *scales, const uint8_t 
 
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, const void *bias,
                         void *y, int dtype, int64_t m, int64_t n, int64_t k, int block_size, cudaStream_t stream) {
+    if (matmul_nbits_umma_eligible(a, b, scales, zp, dtype, m, n, k, block_size))
+        return launch_matmul_nbits_umma(a, b, scales, bias, y, dtype, m, n, k, stream);
     if (mnb_mma_eligible(a, b, scales, zp, dtype, m, n, k, block_size)) {
         if (dtype == SA_DTYPE_FLOAT16) return launch_mma_rows<__half>(a, b, scales, bias, y, m, n, k, stream);
         return launch_mma_rows<__nv_bfloat16>(a, b, scales, bias, y, m, n, k, stream);

@@ -1,0 +1,514 @@
+// MatMulNBits on the 5th-generation tensor cores (tcgen05, sm_100a): int4
+// weights, block 32, fp16/bf16 activations with scales of the same type,
+// default zero point 8, 17..128 activation rows.
+//
+// The product is computed transposed (weights as the MMA's M side):
+//   D[n, m] = sum_k W[n, k] * A[m, k],  W[n, k] = (q[n, k] - 8) * s[n, k / 32]
+// One CTA owns 128 weight rows (UMMA M = 128) and all BN (32..128) activation
+// rows (UMMA N), over the whole K:
+//
+//  warp 0     TMA producer: per stage of 256 k, the [128 rows x 128 B] code
+//             tile (128-byte swizzle), the [128 x 8] scale tile and four
+//             [BN x 64] activation tiles in the canonical K-major SW128
+//             layout the MMA reads directly.
+//  warp 1     allocates 512 TMEM columns; lane 0 issues the MMAs
+//             (tcgen05.mma kind::f16, A from TMEM, B from shared memory,
+//             D = f32 in TMEM: 256 / BN accumulators of BN columns taken in
+//             turn, so that back-to-back MMAs are independent) and commits
+//             their completion to the mbarriers that recycle the buffers.
+//  warps 2-9  dequantize: each thread owns one weight row (its TMEM lane)
+//             and writes 64 k of it per buffer into TMEM (tcgen05.st), four
+//             buffers in flight.  Warps 2-5 take the even 64-k sub-chunks,
+//             warps 6-9 the odd ones; warps 2-5 also run the epilogue
+//             (tcgen05.ld of the accumulators, their sum, bias, conversion,
+//             store).
+//
+// Exact weights: a scale s (fp16: 11 significant bits, bf16: 8) is split as
+// s = s1 + s2 with s1 = s with its low three mantissa bits cleared.  q - 8
+// has at most three significant bits, so (q-8)*s1 and (q-8)*s2 are exact in
+// the 16-bit type, and the MMA's products are exact in fp32: two MMAs per
+// k step (A1 = (q-8)*s1, A2 = (q-8)*s2) give the f32 dequantized product
+// with f32 accumulation.
+//
+// Every mbarrier wait is bounded; a wait that gives up sets a shared abort
+// flag (all roles leave their loops), the kernel lets its copies and MMAs
+// land, frees TMEM and returns without writing y.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "sa_async.cuh"
+#include "sa_common.cuh"
+#include "sa_internal.h"
+#include "sa_tma.cuh"
+
+namespace sa {
+
+namespace {
+
+constexpr int kUmBM = 128;                  // weight rows per CTA (UMMA M)
+constexpr int kUmKC = 256;                  // k per TMA stage
+constexpr int kUmSub = 64;                  // k per TMEM A buffer
+constexpr int kUmNA = 4;                    // A buffers in TMEM (an even number: buffer q % NA belongs to group q % 2)
+constexpr int kUmCodeTile = kUmBM * 128;    // [128 rows][128 B]
+constexpr int kUmScaleTile = kUmBM * 16;    // [128 rows][8 scales]
+constexpr int kUmDqWarps = 8;
+constexpr int kUmThreads = 32 * (2 + kUmDqWarps);
+constexpr uint32_t kUmTmemCols = 512;       // accumulators in [0, 256), A buffers in [256, 512)
+constexpr uint32_t kUmAcol = 256;
+
+__device__ int g_umma_status;  // bit 0: a bounded wait gave up
+
+template <int BN>
+struct UmGeo {
+    static constexpr int NS = BN <= 32 ? 4 : (BN <= 64 ? 3 : 2);   // TMA stages
+    // independent f32 accumulators in TMEM columns [0, 256): consecutive MMAs go to
+    // different ones, so they do not wait for each other's accumulation
+    static constexpr int NACC = 256 / BN;
+    static constexpr int ACT_SUB = BN * 128;                       // one [BN][64] activation tile
+    static constexpr int STAGE = kUmCodeTile + kUmScaleTile + 4 * ACT_SUB;
+    // at least 116 KB, so that one CTA (holding 512 TMEM columns) runs per SM
+    static constexpr int SMEM = (1024 + NS * STAGE + 256) > 116 * 1024 ? (1024 + NS * STAGE + 256) : 116 * 1024;
+    static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+};
+
+// ---- tcgen05 wrappers ----------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (f32, TMEM) (+)= A (16-bit, TMEM) * B^T (16-bit, shared memory descriptor)
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d),
+        "r"(a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15}, [%16];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte-swizzle
+// canonical layout: rows of 128 B, 8-row groups 1024 B apart (SBO), version 1,
+// layout type 2 (SWIZZLE_128B).  The tile base is 1024-byte aligned; a k step
+// of 16 elements inside the swizzle atom advances the start address by 32 B.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B of type T (K-major), N = BN, M = 128.
+template <typename T, int BN>
+__host__ __device__ constexpr uint32_t umma_idesc() {
+    return (1u << 4) | ((std::is_same<T, __half>::value ? 0u : 1u) << 7) |
+           ((std::is_same<T, __half>::value ? 0u : 1u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+           ((uint32_t)(kUmBM >> 4) << 24);
+}
+
+// One lane of the (converged) warp: the lowest active lane.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n.reg .b32 rx;\n.reg .pred px;\nelect.sync rx|px, 0xffffffff;\nselp.b32 %0, 1, 0, px;\n}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// Bounded wait that also gives up when another role has aborted.  The
+// hand-offs between the roles are short, so the wait polls (try_wait without
+// a suspend hint) instead of sleeping; the bound is 2 s of %globaltimer.
+__device__ __forceinline__ bool um_try(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t um_clock_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kUmWaitNs = 2000000000ull;
+
+__device__ __forceinline__ bool um_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (um_try(bar, parity)) return true;
+    const uint64_t t0 = um_clock_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (um_try(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*abort_flag) return false;
+            if (um_clock_ns() - t0 > kUmWaitNs) break;
+        }
+    }
+    *abort_flag = 1;
+    atomicOr(&g_umma_status, 1);
+    return false;
+}
+
+// ---- dequantization: two k of one byte -> a packed pair, split by the scale halves ----
+template <typename T>
+struct UmDq {
+    static constexpr uint32_t kMagic = std::is_same<T, __half>::value ? 0x64006400u : 0x43004300u;  // 1024 | 128 + q
+    static constexpr uint16_t kBias = std::is_same<T, __half>::value ? 0x6408 : 0x4308;            // 1032 | 136
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t um_sub8(uint32_t x) {
+    if constexpr (std::is_same<T, __half>::value) {
+        __half2 h = *reinterpret_cast<__half2 *>(&x);
+        h = __hsub2(h, __halves2half2(__ushort_as_half(UmDq<T>::kBias), __ushort_as_half(UmDq<T>::kBias)));
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&x);
+        h = __hsub2(h, __halves2bfloat162(__ushort_as_bfloat16(UmDq<T>::kBias), __ushort_as_bfloat16(UmDq<T>::kBias)));
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t um_mul(uint32_t x, uint32_t s) {
+    if constexpr (std::is_same<T, __half>::value) {
+        __half2 h = __hmul2(*reinterpret_cast<__half2 *>(&x), *reinterpret_cast<__half2 *>(&s));
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = __hmul2(*reinterpret_cast<__nv_bfloat162 *>(&x), *reinterpret_cast<__nv_bfloat162 *>(&s));
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+// Scale halves of one 16-bit scale as packed pairs (s1, s1) and (s2, s2).
+template <typename T>
+__device__ __forceinline__ void um_split_scale(uint16_t s, uint32_t &p1, uint32_t &p2) {
+    const uint16_t s1 = s & 0xFFF8u;
+    uint16_t s2;
+    if constexpr (std::is_same<T, __half>::value) {
+        s2 = __half_as_ushort(__hsub(__ushort_as_half(s), __ushort_as_half(s1)));
+    } else {
+        s2 = __bfloat16_as_ushort(__hsub(__ushort_as_bfloat16(s), __ushort_as_bfloat16(s1)));
+    }
+    p1 = (uint32_t)s1 | ((uint32_t)s1 << 16);
+    p2 = (uint32_t)s2 | ((uint32_t)s2 << 16);
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kUmThreads, 1)
+    mnb_umma_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
+                    const __grid_constant__ CUtensorMap tm_act, const T *__restrict__ bias, T *__restrict__ y, int m,
+                    int n, int k) {
+    using GG = UmGeo<BN>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + GG::NS * GG::STAGE);  // [NS] TMA landed
+    uint64_t *empty = full + GG::NS;                                            // [NS] stage consumed
+    uint64_t *afull = empty + GG::NS;                                           // [NA] A buffer written
+    uint64_t *aempty = afull + kUmNA;                                           // [NA] A buffer read by its MMAs
+    uint64_t *dfull = aempty + kUmNA;                                           // all MMAs complete
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(dfull + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+    const int n0 = blockIdx.x * kUmBM;
+    const int nchunks = k / kUmKC, nsub = k / kUmSub;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < GG::NS; i++) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kUmDqWarps + 1);
+        }
+        for (int i = 0; i < kUmNA; i++) {
+            mbar_init(afull + i, 4);
+            mbar_init(aempty + i, 1);
+        }
+        mbar_init(dfull, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(tslot, kUmTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    int issued = 0;  // producer: stages issued
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int c = 0; c < nchunks; c++) {
+                const int s = c % GG::NS;
+                if (c >= GG::NS && !um_wait(empty + s, (uint32_t)(((c / GG::NS) - 1) & 1), abort_flag)) break;
+                unsigned char *st = smem + s * GG::STAGE;
+                mbar_expect_tx(full + s, (uint32_t)GG::STAGE);
+                tma_load_2d(st, &tm_codes, c * 128, n0, full + s);
+                tma_load_2d(st + kUmCodeTile, &tm_scales, c * 8, n0, full + s);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, c * kUmKC + 64 * j, 0,
+                                   full + s);
+                issued = c + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // the whole warp runs the loop (uniform descriptors); one elected lane issues
+        constexpr uint32_t idesc = umma_idesc<T, BN>();
+        for (int q = 0; q < nsub; q++) {
+            const int c = q >> 2, j = q & 3, s = c % GG::NS, ab = q % kUmNA;
+            bool ok = j != 0 || um_wait(full + s, (uint32_t)((c / GG::NS) & 1), abort_flag);
+            if (ok) ok = um_wait(afull + ab, (uint32_t)((q / kUmNA) & 1), abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const uint32_t act = smem_u32(smem + s * GG::STAGE + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB);
+            const uint32_t ta = tbase + kUmAcol + (uint32_t)ab * 64;
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t bdesc = sw128_kmajor_desc(act + 32 * kk);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {  // A1 = (q-8)*s1, A2 = (q-8)*s2
+                        const int idx = q * 8 + 2 * kk + h;
+                        umma_ts(tbase + (uint32_t)((idx % GG::NACC) * BN), ta + 32 * h + 8 * kk, bdesc, idesc,
+                                idx >= GG::NACC ? 1u : 0u);
+                    }
+                }
+                umma_commit(aempty + ab);
+                if (j == 3) umma_commit(empty + s);
+            }
+            __syncwarp();
+        }
+        if (elect_one()) umma_commit(dfull);
+        __syncwarp();
+        // the MMAs always complete: wait for them (bounded) before TMEM is freed
+        const uint64_t t0 = um_clock_ns();
+        while (!um_try(dfull, 0) && um_clock_ns() - t0 < kUmWaitNs) {
+        }
+    } else {
+        const int g = (warp - 2) >> 2, sp = warp & 3;
+        const int row = 32 * sp + lane;                              // weight row in the tile = TMEM lane
+        const uint32_t tl = tbase + ((uint32_t)(32 * sp) << 16);     // this warp's lane quarter
+        // Software pipeline: sub-chunk q's TMEM stores drain while sub-chunk q + 2 is
+        // dequantized into the other register set.
+        // dq: wait for the stage, dequantize 64 k of this row into r (A1 in
+        // r[0..31], A2 in r[32..63]).
+        auto dq = [&](int q, uint32_t (&r)[64]) -> bool {
+            const int c = q >> 2, j = q & 3, s = c % GG::NS;
+            const bool ok = um_wait(full + s, (uint32_t)((c / GG::NS) & 1), abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) return false;
+            const unsigned char *st = smem + s * GG::STAGE;
+            // 64 codes of this row: 16-byte units 2j and 2j+1 of its swizzled 128-byte line
+            const uint4 u0 = *reinterpret_cast<const uint4 *>(st + row * 128 + (((2 * j) ^ (row & 7)) << 4));
+            const uint4 u1 = *reinterpret_cast<const uint4 *>(st + row * 128 + (((2 * j + 1) ^ (row & 7)) << 4));
+            const uint32_t sc = *reinterpret_cast<const uint32_t *>(st + kUmCodeTile + row * 16 + j * 4);
+            uint32_t s1[2], s2[2];
+            um_split_scale<T>((uint16_t)(sc & 0xFFFFu), s1[0], s2[0]);
+            um_split_scale<T>((uint16_t)(sc >> 16), s1[1], s2[1]);
+            const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int wi = 0; wi < 8; wi++) {  // words 0-3: block 2j, words 4-7: block 2j + 1
+                const uint32_t w = wv[wi], wh = w >> 4;
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    // byte p of w: its low nibble (k = 8wi + 2p) in half 0, high nibble in half 1
+                    const uint32_t t = __byte_perm(w, wh, (uint32_t)(p | (p << 4) | ((4 + p) << 8) | ((4 + p) << 12)));
+                    uint32_t x;
+                    asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(x) : "r"(t), "r"(0x000F000Fu), "r"(UmDq<T>::kMagic));
+                    x = um_sub8<T>(x);
+                    r[4 * wi + p] = um_mul<T>(x, s1[wi >> 2]);
+                    r[32 + 4 * wi + p] = um_mul<T>(x, s2[wi >> 2]);
+                }
+            }
+            return true;
+        };
+        // put: wait until buffer q % NA is free, store r into it
+        auto put = [&](int q, const uint32_t (&r)[64]) -> bool {
+            const int ab = q % kUmNA;
+            const bool ok = q < kUmNA || um_wait(aempty + ab, (uint32_t)(((q / kUmNA) - 1) & 1), abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) return false;
+            tc_fence_after();
+            const uint32_t abuf = tl + kUmAcol + (uint32_t)ab * 64;
+            tmem_st16(abuf, r);
+            tmem_st16(abuf + 16, r + 16);
+            tmem_st16(abuf + 32, r + 32);
+            tmem_st16(abuf + 48, r + 48);
+            return true;
+        };
+        // fin: the stores of q have landed: hand the buffer to the MMA warp
+        auto fin = [&](int q) {
+            const int c = q >> 2, j = q & 3, s = c % GG::NS, ab = q % kUmNA;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(afull + ab);
+                if (j >= 2) mbar_arrive(empty + s);
+            }
+        };
+        uint32_t ra[64], rb[64];
+        int q = g;
+        if (q < nsub && dq(q, ra)) {
+            for (;;) {
+                if (!put(q, ra)) break;
+                const int q2 = q + 2;
+                const bool more2 = q2 < nsub && dq(q2, rb);
+                fin(q);
+                if (!more2 || !put(q2, rb)) break;
+                const int q3 = q2 + 2;
+                const bool more3 = q3 < nsub && dq(q3, ra);
+                fin(q2);
+                if (!more3) break;
+                q = q3;
+            }
+        }
+        if (g == 0) {
+            // epilogue: D row `row` (output column n0 + row) for the m activation rows
+            bool ok = um_wait(dfull, 0, abort_flag);
+            ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+            tc_fence_after();
+            if (ok) {
+                const float bv = bias ? DT<T>::to_f32(bias[n0 + row]) : 0.0f;
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float acc[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[i] = bv;
+                    for (int d = 0; d < GG::NACC; d++) {  // the accumulators' sum
+                        uint32_t v[16];
+                        tmem_ld16(tl + (uint32_t)(d * BN + c0), v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(v[i]);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int mi = c0 + i;
+                        if (mi < m) y[(int64_t)mi * n + n0 + row] = DT<T>::from_f32(acc[i]);
+                    }
+                }
+            }
+        }
+    }
+    // teardown: copies still in flight after an abort land before the CTA exits
+    if (warp == 0 && lane == 0 && *abort_flag) {
+        for (int c = (issued > GG::NS ? issued - GG::NS : 0); c < issued; c++)
+            mbar_wait_bounded(full + c % GG::NS, (uint32_t)((c / GG::NS) & 1));
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kUmTmemCols);
+    }
+}
+
+template <typename T, int BN>
+int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
+                   int64_t n, int64_t k, cudaStream_t stream) {
+    using GG = UmGeo<BN>;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap tm_codes, tm_scales, tm_act;
+    const cuuint32_t ones[2] = {1, 1};
+    const cuuint64_t cdim[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n}, cstride[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t cbox[2] = {128, (cuuint32_t)kUmBM};
+    CUresult r = encode(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(b), cdim, cstride, cbox,
+                        ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits umma: code tensor map (%d)", (int)r);
+    const cuuint64_t sdim[2] = {(cuuint64_t)(k / 32), (cuuint64_t)n}, sstride[1] = {(cuuint64_t)(k / 32) * 2};
+    const cuuint32_t sbox[2] = {8, (cuuint32_t)kUmBM};
+    r = encode(&tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(scales), sdim, sstride, sbox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits umma: scale tensor map (%d)", (int)r);
+    const cuuint64_t adim[2] = {(cuuint64_t)k, (cuuint64_t)m}, astride[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t abox[2] = {64, (cuuint32_t)BN};
+    r = encode(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(a), adim, astride, abox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits umma: activation tensor map (%d)", (int)r);
+    auto kern = mnb_umma_kernel<T, BN>;
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GG::SMEM);
+        if (e != cudaSuccess) return check_cuda(e, "MatMulNBits umma smem attribute");
+        if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
+    }
+    kern<<<(unsigned)(n / kUmBM), kUmThreads, GG::SMEM, stream>>>(tm_codes, tm_scales, tm_act,
+                                                                  static_cast<const T *>(bias), static_cast<T *>(y),
+                                                                  (int)m, (int)n, (int)k);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "MatMulNBits umma launch");
+}
+
+template <typename T>
+int launch_umma_t(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
+                  int64_t n, int64_t k, cudaStream_t stream) {
+    if (m <= 32) return launch_umma_bn<T, 32>(a, b, scales, bias, y, m, n, k, stream);
+    if (m <= 64) return launch_umma_bn<T, 64>(a, b, scales, bias, y, m, n, k, stream);
+    return launch_umma_bn<T, 128>(a, b, scales, bias, y, m, n, k, stream);
+}
+
+}  // namespace
+
+// fp16/bf16, block 32, default zero point, 17 <= m <= 128, N a multiple of
+// 128, K a multiple of 256, codes / scales / activations 16-byte aligned.
+// (Up to 16 rows the mma.sync kernels are faster: each tcgen05.mma here costs
+// about 65 cycles of issue whatever N is, and a tile needs K/8 of them.)
+bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
+                                int64_t m, int64_t n, int64_t k, int block_size) {
+    if (dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16) return false;
+    if (zp || block_size != 32 || m < 17 || m > 128) return false;
+    if (n % kUmBM != 0 || k % kUmKC != 0 || n > (1 << 30) || k > (1 << 24)) return false;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(scales);
+    return (al & 15) == 0;
+}
+
+int launch_matmul_nbits_umma(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y,
+                             int dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+    if (dtype == SA_DTYPE_FLOAT16) return launch_umma_t<__half>(a, b, scales, bias, y, m, n, k, stream);
+    return launch_umma_t<__nv_bfloat16>(a, b, scales, bias, y, m, n, k, stream);
+}
+
+}  // namespace sa

@@ -109,6 +109,10 @@ int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaSt
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
                         int block_size, cudaStream_t stream);
+bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
+                                int64_t m, int64_t n, int64_t k, int block_size);
+int launch_matmul_nbits_umma(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y,
+                             int dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 bool matmul_nbits_packable(int dtype, int64_t n, int64_t k, int block_size);
 size_t matmul_nbits_packed_bytes(int64_t n, int64_t k);
 int launch_matmul_nbits_prepack(const uint8_t *b, const void *scales, void *packed, int dtype, int64_t n, int64_t k,

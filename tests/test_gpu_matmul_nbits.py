@@ -73,8 +73,9 @@ def test_block_sizes_zero_points_bias(cuda_device, block):
 @pytest.mark.parametrize("m", [1, 5, 8, 9, 16, 23, 33, 64])
 @pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
 def test_tensor_core_path(cuda_device, m, adtype):
-    """The mma.sync path (fp16/bf16, block 32, default zero point, K % 1024 == 0, m <= 64)."""
-    _run(cuda_device, m, 512, 2048, adtype=adtype, bias=True, seed=100 + m)
+    """The mma.sync path (fp16/bf16, block 32, default zero point, K % 1024 == 0, m <= 64; N = 448 is not a
+    multiple of 128, so the tcgen05 path does not take it)."""
+    _run(cuda_device, m, 448, 2048, adtype=adtype, bias=True, seed=100 + m)
 
 
 @pytest.mark.parametrize("m", [24, 64])
@@ -125,3 +126,21 @@ def test_errors(cuda_device):
         sa.matmul_nbits(a, b, s, K=64, N=8, bits=3)
     with pytest.raises(sa.ShapeMismatch):
         sa.matmul_nbits(a, b, s, K=32, N=8)
+
+
+@pytest.mark.parametrize("m", [17, 31, 32, 40, 64, 100, 128])
+@pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
+def test_tcgen05_path(cuda_device, m, adtype):
+    """The tcgen05 path (N % 128 == 0, K % 256 == 0, 17 <= m <= 128): split-scale exact weights, f32 accumulation.
+    K = 1280 is 5 stages of 256 and 20 TMEM buffer uses: both rings wrap."""
+    _run(cuda_device, m, 384, 1280, adtype=adtype, bias=(m % 2 == 1), seed=300 + m)
+
+
+def test_tcgen05_path_c2_shape_bf16(cuda_device):
+    """BASELINE config 2 width (N=14336, K=4096) with bf16 activations and scales at m = 64."""
+    _run(cuda_device, 64, 14336, 4096, adtype=torch.bfloat16, seed=42)
+
+
+def test_c2_shape_m128_fp16(cuda_device):
+    """128 activation rows (a prefill chunk) on the tcgen05 path."""
+    _run(cuda_device, 128, 14336, 4096, adtype=torch.float16, seed=43)
