@@ -289,6 +289,35 @@ int sa_matmul_nbits_packed(const void *a, const void *packed, const void *bias, 
                            int64_t m, int64_t n, int64_t k, int32_t bits, int32_t block_size,
                            sa_stream_t stream);
 
+/* Fused QKV projection of a decode step: MatMulNBits + RotaryEmbedding +
+ * quantize-on-append in one operator.  It replaces the node sequence the
+ * reference's graph runs before the attention proper: the Q/K/V MatMulNBits
+ * projections, then the rotary and present-K/V concat of
+ * op_group_query_attention (onnx-rt/src/ops/microsoft.rs:1082-1196, rotary
+ * :1004-1050, kv_concat :762-794), with the rotary in the projection's
+ * epilogue.
+ *
+ *   x         (batch, hidden) activations, fp16 or bf16 (one token per row)
+ *   w_codes   packed QKV weights, uint8 (n, hidden/32, 16), n = (Hq + 2*Hkv)*D:
+ *             rows [0, Hq*D) are Wq, then Hkv*D rows of Wk, then Wv; Hq, Hkv
+ *             are this cache's heads (its KV-head shard and their query heads)
+ *   w_scales  (n, hidden/32) in dtype; block 32, default zero point 8
+ *   q_out     (batch, Hq*D): x.Wq^T rounded to dtype, then RoPE at the cache
+ *             position (when do_rotary), rounded to dtype
+ *   k_out, v_out  (batch, Hkv*D): x.Wk^T, x.Wv^T rounded to dtype (no RoPE)
+ * and appends RoPE(k_out) (when do_rotary) and v_out to `layer` at the cache
+ * position, bit-exact with sa_kv_append of (k_out, v_out).  The position is
+ * not advanced (sa_kv_cache_advance after the step).  Attention then runs
+ * with sa_gqa_attend(q_out, do_rotary = 0).  batch 17..128 with
+ * Hq*D and Hkv*D multiples of 128 and hidden a multiple of 256 is one
+ * tcgen05 launch whose epilogue does the rotary and the append; other shapes
+ * run the three projections, then one epilogue launch. */
+int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, const uint8_t *w_codes,
+                          const void *w_scales, int32_t dtype, int32_t batch, int64_t hidden,
+                          const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                          int32_t do_rotary, int32_t rotary_interleaved, void *q_out, void *k_out,
+                          void *v_out, sa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

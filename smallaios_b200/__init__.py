@@ -9,10 +9,11 @@ operator interface; all compute runs in the CUDA library.
 from .kv_cache import DEFAULT_SEED, GpuKvCache, LayerView
 from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatchCtx, OpError, PackedNBitsWeight,
                   ShapeMismatch, UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend,
-                  group_query_attention, matmul_nbits, matmul_nbits_packed, supports_op)
+                  group_query_attention, matmul_nbits, matmul_nbits_packed, qkv_project_append, supports_op)
 
 __all__ = [
     "DEFAULT_SEED", "GpuKvCache", "LayerView", "CapacityError", "InternalError", "InvalidAttribute",
     "KvCacheDispatchCtx", "OpError", "ShapeMismatch", "UnsupportedOp", "dispatch_gpu_node", "finalize_kv_cache",
-    "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight", "supports_op",
+    "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight",
+    "qkv_project_append", "supports_op",
 ]

@@ -41,6 +41,7 @@
 #include "sa_async.cuh"
 #include "sa_common.cuh"
 #include "sa_internal.h"
+#include "sa_qkv.cuh"
 #include "sa_tma.cuh"
 
 namespace sa {
@@ -233,11 +234,15 @@ __device__ __forceinline__ void um_split_scale(uint16_t s, uint32_t &p1, uint32_
     p2 = (uint32_t)s2 | ((uint32_t)s2 << 16);
 }
 
-template <typename T, int BN>
+// FUSED: the QKV projection of a decode step.  The CTA's 128 output columns
+// are 128 / head_dim whole heads; the epilogue stores them (rounded) into
+// q_out / k_out / v_out and then finishes each head vector (qkv_finish_vector:
+// RoPE of q, quantize-on-append of k and v).
+template <typename T, int BN, bool FUSED>
 __global__ void __launch_bounds__(kUmThreads, 1)
     mnb_umma_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
                     const __grid_constant__ CUtensorMap tm_act, const T *__restrict__ bias, T *__restrict__ y, int m,
-                    int n, int k) {
+                    int n, int k, const __grid_constant__ QkvArgs qa) {
     using GG = UmGeo<BN>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -403,6 +408,24 @@ __global__ void __launch_bounds__(kUmThreads, 1)
             bool ok = um_wait(dfull, 0, abort_flag);
             ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
             tc_fence_after();
+            // destination of output column n0 + row: y, or the q / k / v output of the fused projection
+            T *dst = y;
+            int64_t ld = n, col = n0 + row;
+            if constexpr (FUSED) {
+                const int64_t qc = (int64_t)qa.q_heads * qa.ap.head_dim, kc = (int64_t)qa.ap.heads * qa.ap.head_dim;
+                if (col < qc) {
+                    dst = static_cast<T *>(qa.q_out);
+                    ld = qc;
+                } else if (col < qc + kc) {
+                    dst = static_cast<T *>(const_cast<void *>(qa.ap.key));
+                    ld = kc;
+                    col -= qc;
+                } else {
+                    dst = static_cast<T *>(const_cast<void *>(qa.ap.value));
+                    ld = kc;
+                    col -= qc + kc;
+                }
+            }
             if (ok) {
                 const float bv = bias ? DT<T>::to_f32(bias[n0 + row]) : 0.0f;
 #pragma unroll
@@ -420,8 +443,22 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const int mi = c0 + i;
-                        if (mi < m) y[(int64_t)mi * n + n0 + row] = DT<T>::from_f32(acc[i]);
+                        if (mi < m) dst[(int64_t)mi * ld + col] = DT<T>::from_f32(acc[i]);
                     }
+                }
+            }
+            if constexpr (FUSED) {
+                // all 128 columns of every row are stored: each warp finishes rows e, e + 4, ...
+                __threadfence_block();
+                asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the four epilogue warps
+                if (ok && !*abort_flag) {
+                    const int e = warp - 2, d = qa.ap.head_dim;
+                    uint8_t *s_codes = smem + e * 256;  // the stages are idle now
+                    for (int mi = e; mi < m; mi += 4)
+                        for (int hh = n0 / d; hh < (n0 + kUmBM) / d; hh++) {
+                            if (d == 128) qkv_finish_vector<T, 4>(qa, mi, hh, lane, s_codes);
+                            else qkv_finish_vector<T, 2>(qa, mi, hh, lane, s_codes);
+                        }
                 }
             }
         }
@@ -439,9 +476,9 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     }
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool FUSED>
 int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
-                   int64_t n, int64_t k, cudaStream_t stream) {
+                   int64_t n, int64_t k, const QkvArgs &qa, cudaStream_t stream) {
     using GG = UmGeo<BN>;
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
@@ -465,7 +502,7 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits umma: activation tensor map (%d)", (int)r);
-    auto kern = mnb_umma_kernel<T, BN>;
+    auto kern = mnb_umma_kernel<T, BN, FUSED>;
     static int configured[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -476,17 +513,17 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
     }
     kern<<<(unsigned)(n / kUmBM), kUmThreads, GG::SMEM, stream>>>(tm_codes, tm_scales, tm_act,
                                                                   static_cast<const T *>(bias), static_cast<T *>(y),
-                                                                  (int)m, (int)n, (int)k);
+                                                                  (int)m, (int)n, (int)k, qa);
     count_launch();
     return check_cuda(cudaGetLastError(), "MatMulNBits umma launch");
 }
 
-template <typename T>
+template <typename T, bool FUSED>
 int launch_umma_t(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
-                  int64_t n, int64_t k, cudaStream_t stream) {
-    if (m <= 32) return launch_umma_bn<T, 32>(a, b, scales, bias, y, m, n, k, stream);
-    if (m <= 64) return launch_umma_bn<T, 64>(a, b, scales, bias, y, m, n, k, stream);
-    return launch_umma_bn<T, 128>(a, b, scales, bias, y, m, n, k, stream);
+                  int64_t n, int64_t k, const QkvArgs &qa, cudaStream_t stream) {
+    if (m <= 32) return launch_umma_bn<T, 32, FUSED>(a, b, scales, bias, y, m, n, k, qa, stream);
+    if (m <= 64) return launch_umma_bn<T, 64, FUSED>(a, b, scales, bias, y, m, n, k, qa, stream);
+    return launch_umma_bn<T, 128, FUSED>(a, b, scales, bias, y, m, n, k, qa, stream);
 }
 
 }  // namespace
@@ -507,8 +544,21 @@ bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *sca
 
 int launch_matmul_nbits_umma(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y,
                              int dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
-    if (dtype == SA_DTYPE_FLOAT16) return launch_umma_t<__half>(a, b, scales, bias, y, m, n, k, stream);
-    return launch_umma_t<__nv_bfloat16>(a, b, scales, bias, y, m, n, k, stream);
+    const QkvArgs none{};
+    if (dtype == SA_DTYPE_FLOAT16) return launch_umma_t<__half, false>(a, b, scales, bias, y, m, n, k, none, stream);
+    return launch_umma_t<__nv_bfloat16, false>(a, b, scales, bias, y, m, n, k, none, stream);
+}
+
+// The fused QKV projection: x [batch][k] times the packed [n][k] weights
+// (q rows, then k rows, then v rows), epilogue per qkv_finish_vector.  The
+// caller checked matmul_nbits_umma_eligible and that every 128-column tile
+// holds whole heads of one kind (q_heads*D and kv_heads*D multiples of 128).
+int launch_qkv_umma_fused(const void *x, const uint8_t *w_codes, const void *w_scales, const QkvArgs &a,
+                          int64_t n, int64_t k, cudaStream_t stream) {
+    const int64_t m = a.ap.batch;
+    if (a.ap.dtype == SA_DTYPE_FLOAT16)
+        return launch_umma_t<__half, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream);
+    return launch_umma_t<__nv_bfloat16, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream);
 }
 
 }  // namespace sa

@@ -74,6 +74,14 @@ struct AppendArgs {
     int cache_rows, do_rotary, interleaved;
 };
 
+// Parameters of the fused QKV projection's epilogue (one token per row):
+// `ap` appends k_out / v_out (key / value, seq_len 1) at the cache position.
+struct QkvArgs {
+    AppendArgs ap;
+    void *q_out;  // [batch][q_heads * head_dim], RoPE applied in place
+    int q_heads;
+};
+
 // Parameters of one attention launch.
 struct AttendArgs {
     const void *query;
@@ -109,6 +117,9 @@ int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaSt
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
                         int block_size, cudaStream_t stream);
+int launch_qkv_finish(const QkvArgs &a, cudaStream_t stream);
+int launch_qkv_umma_fused(const void *x, const uint8_t *w_codes, const void *w_scales, const QkvArgs &a,
+                          int64_t n, int64_t k, cudaStream_t stream);
 bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
                                 int64_t m, int64_t n, int64_t k, int block_size);
 int launch_matmul_nbits_umma(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y,

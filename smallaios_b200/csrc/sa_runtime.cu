@@ -575,4 +575,76 @@ int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const u
                                static_cast<cudaStream_t>(stream));
 }
 
+int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, const uint8_t *w_codes,
+                          const void *w_scales, int32_t dtype, int32_t batch, int64_t hidden,
+                          const float *cos_cache, const float *sin_cache, int32_t cache_rows,
+                          int32_t do_rotary, int32_t rotary_interleaved, void *q_out, void *k_out,
+                          void *v_out, sa_stream_t stream) {
+    if (!cache) return set_error(SA_ERR_INVALID_ARGUMENT, "qkv_project_append: NULL cache");
+    kv_cache_impl *k = reinterpret_cast<kv_cache_impl *>(cache);
+    if (layer < 0 || layer >= k->cfg.num_layers)
+        return set_error(SA_ERR_INVALID_ARGUMENT, "qkv_project_append: layer_idx %d", layer);
+    if (dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16)
+        return set_error(SA_ERR_UNSUPPORTED, "qkv_project_append: dtype %d (fp16/bf16 only)", dtype);
+    if (batch != k->cfg.batch)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "qkv_project_append: batch %d != cache batch %d", batch,
+                         k->cfg.batch);
+    if (hidden <= 0 || hidden % 32 != 0)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "qkv_project_append: hidden %lld not a multiple of 32",
+                         (long long)hidden);
+    if (!x || !w_codes || !w_scales || !q_out || !k_out || !v_out)
+        return set_error(SA_ERR_INVALID_ARGUMENT, "qkv_project_append: NULL input/output");
+    if (k->position + 1 > k->cfg.max_seq_len)
+        return set_error(SA_ERR_CAPACITY, "qkv_project_append: position_overflow (%lld + 1 > %d)",
+                         (long long)k->position, k->cfg.max_seq_len);
+    int rc = check_rope("qkv_project_append", do_rotary, cos_cache, sin_cache, cache_rows, k->position);
+    if (rc != SA_OK) return rc;
+    sa_kv_layer_view v;
+    sa_kv_cache_layer_view(cache, layer, &v);
+    QkvArgs a{};
+    AppendArgs &ap = a.ap;
+    ap.key = k_out;
+    ap.value = v_out;
+    ap.dtype = dtype;
+    ap.batch = batch;
+    ap.seq_len = 1;
+    ap.heads = v.kv_heads;
+    ap.head_dim = v.head_dim;
+    ap.bits = v.bits;
+    ap.code_bytes = v.code_bytes;
+    ap.capacity = v.capacity;
+    ap.pos0 = k->position;
+    ap.k_codes = v.k_codes;
+    ap.v_codes = v.v_codes;
+    ap.k_meta = v.k_meta;
+    ap.v_meta = v.v_meta;
+    ap.signs = v.signs;
+    ap.wht_scale = v.wht_scale;
+    ap.cos_cache = cos_cache;
+    ap.sin_cache = sin_cache;
+    ap.cache_rows = cache_rows;
+    ap.do_rotary = do_rotary ? 1 : 0;
+    ap.interleaved = rotary_interleaved ? 1 : 0;
+    a.q_out = q_out;
+    a.q_heads = v.kv_heads * k->group;
+    const int64_t D = v.head_dim, qc = (int64_t)a.q_heads * D, kc = (int64_t)v.kv_heads * D;
+    const int64_t n = qc + 2 * kc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((D == 64 || D == 128) && qc % 128 == 0 && kc % 128 == 0 &&
+        matmul_nbits_umma_eligible(x, w_codes, w_scales, nullptr, dtype, batch, n, hidden, 32))
+        return launch_qkv_umma_fused(x, w_codes, w_scales, a, n, hidden, st);
+    // the three projections (row ranges of the packed weights), then the epilogue launch
+    const int64_t row_codes = hidden / 2, row_scales = (hidden / 32) * 2;
+    const uint8_t *sc = static_cast<const uint8_t *>(w_scales);
+    rc = launch_matmul_nbits(x, w_codes, sc, nullptr, nullptr, q_out, dtype, batch, qc, hidden, 32, st);
+    if (rc == SA_OK)
+        rc = launch_matmul_nbits(x, w_codes + qc * row_codes, sc + qc * row_scales, nullptr, nullptr, k_out, dtype,
+                                 batch, kc, hidden, 32, st);
+    if (rc == SA_OK)
+        rc = launch_matmul_nbits(x, w_codes + (qc + kc) * row_codes, sc + (qc + kc) * row_scales, nullptr, nullptr,
+                                 v_out, dtype, batch, kc, hidden, 32, st);
+    if (rc != SA_OK) return rc;
+    return launch_qkv_finish(a, st);
+}
+
 }  // extern "C"

@@ -207,6 +207,51 @@ def matmul_nbits(a: torch.Tensor, b: torch.Tensor, scales: torch.Tensor, zero_po
     return out
 
 
+def qkv_project_append(x: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor, cache: GpuKvCache,
+                       layer: int, *, do_rotary: bool = True, rotary_interleaved: bool = False, cos_cache=None,
+                       sin_cache=None, q_out=None, k_out=None, v_out=None, stream=None):
+    """Fused QKV projection of a decode step (sa_qkv_project_append).
+
+    ``x`` (B, hidden) fp16/bf16; ``w_codes`` uint8 (n, hidden/32, 16) and
+    ``w_scales`` (n, hidden/32) in x's dtype are the packed Wq/Wk/Wv
+    MatMulNBits weights of this cache's heads (n = (Hq + 2*Hkv)*D, block 32,
+    zero point 8).  Returns ``(q, k, v)``: q (B, Hq*D) with RoPE applied at the
+    cache position, k and v (B, Hkv*D) as projected.  RoPE(k) and v are
+    appended to ``layer`` at the cache position (not advanced).  The attention
+    then runs with ``gqa_attend(q, ..., do_rotary=False)``.
+    """
+    for name, t in (("x", x), ("w_codes", w_codes), ("w_scales", w_scales)):
+        _cuda(t, name)
+    if x.dim() != 2:
+        raise ShapeMismatch("qkv_project_append: x must be (batch, hidden)")
+    if w_codes.dtype != torch.uint8:
+        raise UnsupportedOp("qkv_project_append: w_codes must be uint8")
+    if w_scales.dtype != x.dtype:
+        raise UnsupportedOp("qkv_project_append: w_scales must have x's dtype")
+    cfg = cache.config
+    b, hidden = x.shape
+    d = cfg.head_dim
+    hkv = cfg.kv_head_count
+    hq = hkv * (cfg.num_heads // cfg.num_kv_heads)
+    n = (hq + 2 * hkv) * d
+    if w_codes.numel() != n * hidden // 2 or w_scales.numel() != n * (hidden // 32):
+        raise ShapeMismatch("qkv_project_append: weights do not match ((Hq + 2*Hkv)*D, hidden)")
+    rows = _rope_tables(cos_cache, sin_cache)
+    if q_out is None:
+        q_out = torch.empty(b, hq * d, dtype=x.dtype, device=x.device)
+    if k_out is None:
+        k_out = torch.empty(b, hkv * d, dtype=x.dtype, device=x.device)
+    if v_out is None:
+        v_out = torch.empty(b, hkv * d, dtype=x.dtype, device=x.device)
+    rc = lib.sa_qkv_project_append(cache.handle, layer, x.data_ptr(), w_codes.data_ptr(), w_scales.data_ptr(),
+                                   _dtype_code(x), b, hidden, None if cos_cache is None else cos_cache.data_ptr(),
+                                   None if sin_cache is None else sin_cache.data_ptr(), rows, int(bool(do_rotary)),
+                                   int(bool(rotary_interleaved)), q_out.data_ptr(), k_out.data_ptr(),
+                                   v_out.data_ptr(), _stream_handle(stream, x.device))
+    _raise_op(rc, "qkv_project_append")
+    return q_out, k_out, v_out
+
+
 class PackedNBitsWeight:
     """A MatMulNBits weight repacked once for the decode GEMV (``sa_matmul_nbits_prepack``).
 
