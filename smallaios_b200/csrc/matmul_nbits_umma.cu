@@ -41,7 +41,6 @@
 #include "sa_async.cuh"
 #include "sa_common.cuh"
 #include "sa_internal.h"
-#include "sa_qkv.cuh"
 #include "sa_tma.cuh"
 
 namespace sa {
@@ -144,6 +143,20 @@ __host__ __device__ constexpr uint32_t umma_idesc() {
            ((uint32_t)(kUmBM >> 4) << 24);
 }
 
+// Barrier over every thread of every CTA of the cluster (release / acquire:
+// shared and global writes before it are visible after it).
+__device__ __forceinline__ void cluster_sync_all() {
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Generic address of the same shared-memory location in CTA 0 of the cluster.
+__device__ __forceinline__ float *map_to_rank0(float *p) {
+    uint64_t out;
+    asm volatile("mapa.u64 %0, %1, 0;\n" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)));
+    return reinterpret_cast<float *>(out);
+}
+
 // One lane of the (converged) warp: the lowest active lane.
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred = 0;
@@ -235,9 +248,13 @@ __device__ __forceinline__ void um_split_scale(uint16_t s, uint32_t &p1, uint32_
 }
 
 // FUSED: the QKV projection of a decode step.  The CTA's 128 output columns
-// are 128 / head_dim whole heads; the epilogue stores them (rounded) into
-// q_out / k_out / v_out and then finishes each head vector (qkv_finish_vector:
-// RoPE of q, quantize-on-append of k and v).
+// are 128 / head_dim whole heads of one kind; the epilogue stores them
+// (rounded) straight into q_out, k_out or v_out.  The rotary and the
+// quantize-on-append then run as a programmatic dependent launch, one warp
+// per head vector (qkv_finish_kernel): measured on B200 at the Llama-3-8B
+// layer shape (batch 64), finishing the vectors inside this kernel's
+// epilogue took 36.7 us for the projection against 22.6 us + a 3 us launch,
+// the vector encode being latency-bound with a few warps per tile.
 template <typename T, int BN, bool FUSED>
 __global__ void __launch_bounds__(kUmThreads, 1)
     mnb_umma_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
@@ -254,8 +271,14 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     uint64_t *dfull = aempty + kUmNA;                                           // all MMAs complete
     uint32_t *tslot = reinterpret_cast<uint32_t *>(dfull + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    const int n0 = blockIdx.x * kUmBM;
-    const int nchunks = k / kUmKC, nsub = k / kUmSub;
+    // split-K over a thread-block cluster: CTA `rank` of a cluster of `nsplit`
+    // (consecutive blockIdx.x) takes chunks [cb, ce) of the tile's K
+    uint32_t rank = 0, nsplit = 1;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(rank));
+    asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(nsplit));
+    const int n0 = (blockIdx.x / nsplit) * kUmBM;
+    const int cb = (int)(rank * (k / kUmKC) / nsplit), ce = (int)((rank + 1) * (k / kUmKC) / nsplit);
+    const int nchunks = ce - cb, nsub = 4 * nchunks;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < GG::NS; i++) {
@@ -273,6 +296,8 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     if (warp == 1) tmem_alloc(tslot, kUmTmemCols);
     tc_fence_before();
     __syncthreads();
+    // a dependent launch (the fused projection's finishing kernel) may start; it waits for this grid
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     tc_fence_after();
     const uint32_t tbase = *tslot;
 
@@ -284,11 +309,12 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 if (c >= GG::NS && !um_wait(empty + s, (uint32_t)(((c / GG::NS) - 1) & 1), abort_flag)) break;
                 unsigned char *st = smem + s * GG::STAGE;
                 mbar_expect_tx(full + s, (uint32_t)GG::STAGE);
-                tma_load_2d(st, &tm_codes, c * 128, n0, full + s);
-                tma_load_2d(st + kUmCodeTile, &tm_scales, c * 8, n0, full + s);
+                const int cg = cb + c;  // chunk of the tile's K
+                tma_load_2d(st, &tm_codes, cg * 128, n0, full + s);
+                tma_load_2d(st + kUmCodeTile, &tm_scales, cg * 8, n0, full + s);
 #pragma unroll
                 for (int j = 0; j < 4; j++)
-                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, c * kUmKC + 64 * j, 0,
+                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, cg * kUmKC + 64 * j, 0,
                                    full + s);
                 issued = c + 1;
             }
@@ -403,62 +429,78 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 q = q3;
             }
         }
-        if (g == 0) {
-            // epilogue: D row `row` (output column n0 + row) for the m activation rows
-            bool ok = um_wait(dfull, 0, abort_flag);
-            ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
-            tc_fence_after();
-            // destination of output column n0 + row: y, or the q / k / v output of the fused projection
-            T *dst = y;
-            int64_t ld = n, col = n0 + row;
-            if constexpr (FUSED) {
-                const int64_t qc = (int64_t)qa.q_heads * qa.ap.head_dim, kc = (int64_t)qa.ap.heads * qa.ap.head_dim;
-                if (col < qc) {
-                    dst = static_cast<T *>(qa.q_out);
-                    ld = qc;
-                } else if (col < qc + kc) {
-                    dst = static_cast<T *>(const_cast<void *>(qa.ap.key));
-                    ld = kc;
-                    col -= qc;
-                } else {
-                    dst = static_cast<T *>(const_cast<void *>(qa.ap.value));
-                    ld = kc;
-                    col -= qc + kc;
-                }
+    }
+
+    // ---- epilogue (every thread of the CTA comes here) ----
+    // warps 2-5 hold TMEM lane quarters (warp & 3) = weight rows of the tile
+    const bool epi = warp >= 2 && warp < 6;
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t tl = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+    bool ok = true;
+    if (epi) {
+        ok = um_wait(dfull, 0, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+    }
+    // this CTA's f32 sums of output column n0 + row, 16 activation rows at a time
+    auto load_sums = [&](int c0, float (&acc)[16]) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+        for (int d = 0; d < GG::NACC; d++) {  // the accumulators' sum
+            uint32_t v[16];
+            tmem_ld16(tl + (uint32_t)(d * BN + c0), v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(v[i]);
+        }
+    };
+    // split-K: ranks 1.. store their sums into rank 0's shared memory ([rank-1][column][row], the
+    // stages are idle after the first cluster barrier), rank 0 adds them
+    float *part = reinterpret_cast<float *>(smem);
+    if (nsplit > 1) {
+        cluster_sync_all();
+        if (epi && rank != 0 && ok && !*abort_flag) {
+            float *dst = map_to_rank0(part) + (size_t)(rank - 1) * BN * kUmBM;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float acc[16];
+                load_sums(c0, acc);
+#pragma unroll
+                for (int i = 0; i < 16; i++) dst[(c0 + i) * kUmBM + row] = acc[i];
             }
-            if (ok) {
-                const float bv = bias ? DT<T>::to_f32(bias[n0 + row]) : 0.0f;
-#pragma unroll
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float acc[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++) acc[i] = bv;
-                    for (int d = 0; d < GG::NACC; d++) {  // the accumulators' sum
-                        uint32_t v[16];
-                        tmem_ld16(tl + (uint32_t)(d * BN + c0), v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(v[i]);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const int mi = c0 + i;
-                        if (mi < m) dst[(int64_t)mi * ld + col] = DT<T>::from_f32(acc[i]);
-                    }
-                }
+        }
+        cluster_sync_all();
+    }
+    if (epi && rank == 0) {
+        // destination of output column n0 + row: y, or the q / k / v output of the fused projection
+        T *dst = y;
+        int64_t ld = n, col = n0 + row;
+        if constexpr (FUSED) {
+            const int64_t qc = (int64_t)qa.q_heads * qa.ap.head_dim, kc = (int64_t)qa.ap.heads * qa.ap.head_dim;
+            if (col < qc) {
+                dst = static_cast<T *>(qa.q_out);
+                ld = qc;
+            } else if (col < qc + kc) {
+                dst = static_cast<T *>(const_cast<void *>(qa.ap.key));
+                ld = kc;
+                col -= qc;
+            } else {
+                dst = static_cast<T *>(const_cast<void *>(qa.ap.value));
+                ld = kc;
+                col -= qc + kc;
             }
-            if constexpr (FUSED) {
-                // all 128 columns of every row are stored: each warp finishes rows e, e + 4, ...
-                __threadfence_block();
-                asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the four epilogue warps
-                if (ok && !*abort_flag) {
-                    const int e = warp - 2, d = qa.ap.head_dim;
-                    uint8_t *s_codes = smem + e * 256;  // the stages are idle now
-                    for (int mi = e; mi < m; mi += 4)
-                        for (int hh = n0 / d; hh < (n0 + kUmBM) / d; hh++) {
-                            if (d == 128) qkv_finish_vector<T, 4>(qa, mi, hh, lane, s_codes);
-                            else qkv_finish_vector<T, 2>(qa, mi, hh, lane, s_codes);
-                        }
+        }
+        if (ok && !*abort_flag) {
+            const float bv = bias ? DT<T>::to_f32(bias[n0 + row]) : 0.0f;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float acc[16];
+                load_sums(c0, acc);
+                for (uint32_t r = 1; r < nsplit; r++)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[i] += part[((size_t)(r - 1) * BN + c0 + i) * kUmBM + row];
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int mi = c0 + i;
+                    if (mi < m) dst[(int64_t)mi * ld + col] = DT<T>::from_f32(acc[i] + bv);
                 }
             }
         }
@@ -504,18 +546,53 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
     if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits umma: activation tensor map (%d)", (int)r);
     auto kern = mnb_umma_kernel<T, BN, FUSED>;
     static int configured[64];
+    static int max_clusters[64][5];  // co-resident clusters of 2..4 CTAs
     int dev = 0;
     cudaGetDevice(&dev);
+    const int tiles = (int)(n / kUmBM);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    cfg.blockDim = dim3(kUmThreads);
+    cfg.dynamicSmemBytes = GG::SMEM;
+    cfg.stream = stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
     if (dev < 0 || dev >= 64 || !__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GG::SMEM);
         if (e != cudaSuccess) return check_cuda(e, "MatMulNBits umma smem attribute");
-        if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
+        if (dev >= 0 && dev < 64) {
+            for (int sc = 2; sc <= 4; sc++) {
+                at[0].val.clusterDim.x = (unsigned)sc;
+                at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
+                cfg.gridDim = dim3((unsigned)(sc * 64));
+                int nc = 0;
+                if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    nc = 0;
+                }
+                max_clusters[dev][sc] = nc;
+            }
+            __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
+        }
     }
-    kern<<<(unsigned)(n / kUmBM), kUmThreads, GG::SMEM, stream>>>(tm_codes, tm_scales, tm_act,
-                                                                  static_cast<const T *>(bias), static_cast<T *>(y),
-                                                                  (int)m, (int)n, (int)k, qa);
+    // K split over a cluster: the largest of 2..4 CTAs per tile that keeps one
+    // wave (every cluster co-resident) and whose partial sums fit in the stages
+    int split = 1;
+    int sm_count = 148;
+    cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (dev >= 0 && dev < 64)
+        for (int sc = 2; sc <= 4; sc++)
+            if (sc <= k / kUmKC && tiles * sc <= sm_count && tiles <= max_clusters[dev][sc] &&
+                (sc - 1) * BN * kUmBM * 4 <= GG::NS * GG::STAGE)
+                split = sc;
+    at[0].val.clusterDim.x = (unsigned)split;
+    at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(tiles * split));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tm_codes, tm_scales, tm_act, static_cast<const T *>(bias),
+                                       static_cast<T *>(y), (int)m, (int)n, (int)k, qa);
     count_launch();
-    return check_cuda(cudaGetLastError(), "MatMulNBits umma launch");
+    return check_cuda(e, "MatMulNBits umma launch");
 }
 
 template <typename T, bool FUSED>
@@ -556,9 +633,11 @@ int launch_matmul_nbits_umma(const void *a, const uint8_t *b, const void *scales
 int launch_qkv_umma_fused(const void *x, const uint8_t *w_codes, const void *w_scales, const QkvArgs &a,
                           int64_t n, int64_t k, cudaStream_t stream) {
     const int64_t m = a.ap.batch;
-    if (a.ap.dtype == SA_DTYPE_FLOAT16)
-        return launch_umma_t<__half, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream);
-    return launch_umma_t<__nv_bfloat16, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream);
+    const int rc = a.ap.dtype == SA_DTYPE_FLOAT16
+                       ? launch_umma_t<__half, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream)
+                       : launch_umma_t<__nv_bfloat16, true>(x, w_codes, w_scales, nullptr, nullptr, m, n, k, a, stream);
+    if (rc != SA_OK) return rc;
+    return launch_qkv_finish(a, stream);
 }
 
 }  // namespace sa

@@ -1,8 +1,7 @@
-// Epilogue kernel of the fused QKV projection when the projection itself ran
-// as separate MatMulNBits launches (the mma.sync / GEMV shapes): one warp per
-// (head, row) finishes the head vector (RoPE of q in place, quantize-on-append
-// of k and v).  The tcgen05 projection runs the same routine in its own
-// epilogue instead (matmul_nbits_umma.cu).
+// Finishing kernel of the fused QKV projection: one warp per (head, row)
+// finishes the head vector (RoPE of q in place, quantize-on-append of k and
+// v) once the projection (the tcgen05 kernel writing q / k / v directly, or
+// three MatMulNBits launches) has stored it.
 #include "sa_qkv.cuh"
 
 namespace sa {
@@ -12,22 +11,35 @@ namespace {
 template <typename T, int EPL>
 __global__ void __launch_bounds__(32) qkv_finish_kernel(QkvArgs a) {
     __shared__ uint8_t s_codes[256];
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the projection's outputs (a no-op without PDL)
     qkv_finish_vector<T, EPL>(a, blockIdx.y, blockIdx.x, threadIdx.x, s_codes);
 }
 
+// Launched as a programmatic dependent of the projection kernel before it, so
+// its warps are resident (and waiting) when the projection completes.
 template <typename T>
 int launch_t(const QkvArgs &a, cudaStream_t stream) {
-    const dim3 grid((unsigned)(a.q_heads + 2 * a.ap.heads), (unsigned)a.ap.batch);
+    void (*kern)(QkvArgs);
     switch (a.ap.head_dim) {
-        case 16: qkv_finish_kernel<T, 1><<<grid, 32, 0, stream>>>(a); break;
-        case 32: qkv_finish_kernel<T, 1><<<grid, 32, 0, stream>>>(a); break;
-        case 64: qkv_finish_kernel<T, 2><<<grid, 32, 0, stream>>>(a); break;
-        case 128: qkv_finish_kernel<T, 4><<<grid, 32, 0, stream>>>(a); break;
-        case 256: qkv_finish_kernel<T, 8><<<grid, 32, 0, stream>>>(a); break;
+        case 16:
+        case 32: kern = qkv_finish_kernel<T, 1>; break;
+        case 64: kern = qkv_finish_kernel<T, 2>; break;
+        case 128: kern = qkv_finish_kernel<T, 4>; break;
+        case 256: kern = qkv_finish_kernel<T, 8>; break;
         default: return set_error(SA_ERR_UNSUPPORTED, "qkv_project_append: head_dim %d", a.ap.head_dim);
     }
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.q_heads + 2 * a.ap.heads), (unsigned)a.ap.batch);
+    cfg.blockDim = dim3(32);
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     count_launch();
-    return check_cuda(cudaGetLastError(), "qkv finish launch");
+    return check_cuda(e, "qkv finish launch");
 }
 
 }  // namespace
