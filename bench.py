@@ -355,6 +355,100 @@ def run_matmul_nbits(args):
     print(json.dumps(line), flush=True)
 
 
+def run_decode_block(args):
+    """``--workload decode_block``: the attention block of one decode layer (not the headline).
+
+    One step = the fused QKV projection (sa_qkv_project_append: int4
+    MatMulNBits of the packed Wq/Wk/Wv, RoPE, quantize-on-append) + the
+    attention over the cache (sa_gqa_attend on the rotated q).  The line also
+    times the unfused sequence on the same inputs: MatMulNBits of the packed
+    weights, then GroupQueryAttention (RoPE + append + attention).
+    Weights are random int4 codes with scales U[0.005, 0.02] (hidden 4096,
+    block 32), activations N(0, 1); the cache is the headline's.
+    """
+    import torch
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cache, cos, sin, _, _, _ = build_workload(torch, sa, dev, seed=1)
+    hidden = 4096 if args.config == "c3" else 8192
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    n = (HQ + 2 * HKV) * D
+    codes = torch.randint(0, 256, (n, hidden // 32, 16), dtype=torch.uint8, device=dev, generator=g)
+    scales = (torch.rand(n, hidden // 32, device=dev, generator=g) * 0.015 + 0.005).to(torch.bfloat16)
+    x = torch.randn(B, hidden, device=dev, generator=g).to(torch.bfloat16)
+    q = torch.empty(B, HQ * D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(B, HKV * D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    y = torch.empty(B, n, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B, 1, HQ * D, dtype=torch.bfloat16, device=dev)
+
+    def fused():
+        cache.set_position(T - 1)
+        sa.qkv_project_append(x, codes, scales, cache, 0, cos_cache=cos, sin_cache=sin, q_out=q, k_out=k, v_out=v)
+        sa.gqa_attend(q.view(B, 1, HQ * D), cache, 0, num_heads=HQ, do_rotary=False, out=out)
+
+    def unfused():
+        cache.set_position(T - 1)
+        sa.matmul_nbits(x, codes, scales, K=hidden, N=n, out=y)
+        q.copy_(y[:, :HQ * D])
+        k.copy_(y[:, HQ * D:(HQ + HKV) * D])
+        v.copy_(y[:, (HQ + HKV) * D:])
+        sa.group_query_attention(q.view(B, 1, -1), k.view(B, 1, -1), v.view(B, 1, -1), cache, 0, num_heads=HQ,
+                                 kv_num_heads=HKV, cos_cache=cos, sin_cache=sin, out=out)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        c0 = lib.sa_kernel_launches()
+        with torch.cuda.graph(graph):
+            fn()
+        launches = lib.sa_kernel_launches() - c0
+        for _ in range(args.warmup):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps, launches
+
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    sampler.start()
+    t_ms, launches = timed(fused)
+    clocks = sampler.stop()
+    u_ms, u_launches = timed(unfused)
+    peak, peak_kind = load_peaks()
+    wbytes = n * hidden // 2 + n * (hidden // 32) * 2
+    byts = wbytes + B * hidden * 2 + attend_bytes() + 2 * B * HKV * (CB + 8)
+    line = {
+        "metric": f"attention block tokens/s (fused QKV MatMulNBits + RoPE + append + attention), {WORKLOAD}",
+        "value": B / (t_ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4-w/int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded; random int4 weights)",
+        "config": {"workload": f"decode attention block, {WORKLOAD}", "batch": B, "hidden": hidden, "q_heads": HQ,
+                   "kv_heads": HKV, "head_dim": D, "context": T, "launch": "CUDA graph of one step, replayed"},
+        "gpu_launches": int(launches) * args.steps,
+        "unfused": {"ms_per_step": u_ms, "value": B / (u_ms * 1e-3), "launches_per_step": int(u_launches),
+                    "sequence": "sa_matmul_nbits (QKV) + sa_group_query_attention"},
+        "roofline": {"bound": "hbm", "achieved": byts / (t_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": byts / (t_ms * 1e-3) / 1e9 / peak, "algorithmic_bytes": byts, "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    cache.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,8 +458,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS),
                     help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
-    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits"],
-                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2, one line, 1 GPU")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="gqa_decode: override the config's batch (a smaller case for profiler captures)")
+    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block"],
+                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
     ap.add_argument("--packed", action="store_true", help="matmul_nbits: weights prepacked once (m <= 8)")
     ap.add_argument("--no-graph", action="store_true",
@@ -381,10 +477,14 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     select_config(args.config)
+    if args.batch is not None:
+        globals()["B"] = args.batch
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "matmul_nbits":
         return run_matmul_nbits(args)
+    if args.workload == "decode_block":
+        return run_decode_block(args)
 
     import torch
     import torch.distributed as dist
