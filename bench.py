@@ -12,6 +12,8 @@ no flush is needed between steps.
   value   tokens/s of the device-resident step (B / step time), max over ranks
   e2e     same metric through the same C-ABI call with q/k/v copied from
           pinned host memory and attn_out copied back inside the timed region
+          (copy-in of the next step and copy-out of the previous one overlap the
+          compute, as a serving loop runs them; the serial loop is reported beside it)
   roofline  the attention call alone (prep + decode + merge launches): algorithmic bytes / call time
   cpu_baseline  the CPU oracle (C restatement of the reference's Rust CPU
           path: encode + read_k/read_v + SDPA) on a bounded sample, rank 0
@@ -610,13 +612,60 @@ def main():
         e2e_step()
     x1.record(stream)
     barrier()
-    e2e_ms = x0.elapsed_time(x1) / args.steps
+    e2e_eager_ms = x0.elapsed_time(x1) / args.steps
+    # The same steps as a serving loop runs them: the copy-in of step i+1 (one stream)
+    # and the copy-out of step i-1 (another stream) overlap the compute of step i, with
+    # double-buffered device inputs/outputs.  Every step still copies its inputs in from
+    # pinned host memory and its attn_out back; the timed region covers all copies.
+    e2e_ms, e2e_mode = e2e_eager_ms, "host launches, copies serial with the compute"
+    if not heads:
+        cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        bufs = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(out))
+                for _ in range(2)]
+        houts = [torch.empty_like(out, device="cpu").pin_memory() for _ in range(2)]
+        ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("ready", "done", "copied")}
+
+        def pipelined(steps):
+            for i in range(steps):
+                sl = i % 2
+                dq_, dk_, dv_, do_ = bufs[sl]
+                with torch.cuda.stream(cs_in):
+                    if i >= 2:
+                        cs_in.wait_event(ev["done"][sl])  # step i-2 has read this slot's inputs
+                    dq_.copy_(hq_, non_blocking=True)
+                    dk_.copy_(hk_, non_blocking=True)
+                    dv_.copy_(hv_, non_blocking=True)
+                    ev["ready"][sl].record(cs_in)
+                stream.wait_event(ev["ready"][sl])
+                if i >= 2:
+                    stream.wait_event(ev["copied"][sl])  # step i-2's output has left this slot
+                cache.set_position(T - 1)
+                sa.group_query_attention(dq_, dk_, dv_, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
+                                         sin_cache=sin, do_rotary=True, out=do_)
+                ev["done"][sl].record(stream)
+                with torch.cuda.stream(cs_out):
+                    cs_out.wait_event(ev["done"][sl])
+                    houts[sl].copy_(do_, non_blocking=True)
+                    ev["copied"][sl].record(cs_out)
+            for sl in range(2):
+                stream.wait_event(ev["copied"][sl])
+
+        pipelined(4)
+        barrier()
+        x0.record(stream)
+        cs_in.wait_event(x0)
+        pipelined(args.steps)
+        x1.record(stream)
+        barrier()
+        e2e_ms = x0.elapsed_time(x1) / args.steps
+        e2e_mode = ("host launches; step i+1's copy-in and step i-1's copy-out overlap step i "
+                    "(two copy streams, double buffers)")
 
     # max over ranks
-    times = torch.tensor([t_ms, e2e_ms, attend_ms], device=dev, dtype=torch.float64)
+    times = torch.tensor([t_ms, e2e_ms, attend_ms, e2e_eager_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, attend_ms = times.tolist()
+    t_ms, e2e_ms, attend_ms, e2e_eager_ms = times.tolist()
     rows_mult = 1 if heads else world  # sequences decoded per step = B * rows_mult
 
     peak, peak_kind = load_peaks()
@@ -641,7 +690,8 @@ def main():
         "gpu_launches": int(launches),
         "e2e": {"value": B * rows_mult / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
-                "d2h_bytes_per_step": int(hout.numel() * 2)},
+                "d2h_bytes_per_step": int(hout.numel() * 2), "ms_per_step": e2e_ms, "mode": e2e_mode,
+                "serial_value": B * rows_mult / (e2e_eager_ms * 1e-3), "serial_ms_per_step": e2e_eager_ms},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": NCU_TRAFFIC_PER_CALL, "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM,
                      "kernel": KERNEL_NOTE, "launches_per_call": attend_launches,
@@ -665,6 +715,7 @@ def main():
         torch.cuda.synchronize(dev)
         graph.reset()
         del graph
+
     if world > 1:
         dist.destroy_process_group()
     return 0
