@@ -1,11 +1,11 @@
 // MatMulNBits on the 5th-generation tensor cores (tcgen05, sm_100a): int4
 // weights, block 32, fp16/bf16 activations with scales of the same type,
-// default zero point 8, 17..128 activation rows.
+// default zero point 8, 17 or more activation rows (blocks of up to 128).
 //
 // The product is computed transposed (weights as the MMA's M side):
 //   D[n, m] = sum_k W[n, k] * A[m, k],  W[n, k] = (q[n, k] - 8) * s[n, k / 32]
-// One CTA owns 128 weight rows (UMMA M = 128) and all BN (32..128) activation
-// rows (UMMA N), over the whole K:
+// One CTA owns 128 weight rows (UMMA M = 128) and a block of BN (32..128)
+// activation rows (UMMA N; grid.y walks the blocks), over the whole K:
 //
 //  warp 0     TMA producer: per stage of 256 k, the [128 rows x 128 B] code
 //             tile (128-byte swizzle), the [128 x 8] scale tile and four
@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(rank));
     asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(nsplit));
     const int n0 = (blockIdx.x / nsplit) * kUmBM;
+    const int m0 = blockIdx.y * BN;  // first activation row of this CTA
     const int cb = (int)(rank * (k / kUmKC) / nsplit), ce = (int)((rank + 1) * (k / kUmKC) / nsplit);
     const int nchunks = ce - cb, nsub = 4 * nchunks;
 
@@ -314,7 +315,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 tma_load_2d(st + kUmCodeTile, &tm_scales, cg * 8, n0, full + s);
 #pragma unroll
                 for (int j = 0; j < 4; j++)
-                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, cg * kUmKC + 64 * j, 0,
+                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, cg * kUmKC + 64 * j, m0,
                                    full + s);
                 issued = c + 1;
             }
@@ -499,7 +500,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                     for (int i = 0; i < 16; i++) acc[i] += part[((size_t)(r - 1) * BN + c0 + i) * kUmBM + row];
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
-                    const int mi = c0 + i;
+                    const int mi = m0 + c0 + i;
                     if (mi < m) dst[(int64_t)mi * ld + col] = DT<T>::from_f32(acc[i] + bv);
                 }
             }
@@ -583,12 +584,12 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
     cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64)
         for (int sc = 2; sc <= 4; sc++)
-            if (sc <= k / kUmKC && tiles * sc <= sm_count && tiles <= max_clusters[dev][sc] &&
+            if (m <= BN && sc <= k / kUmKC && tiles * sc <= sm_count && tiles <= max_clusters[dev][sc] &&
                 (sc - 1) * BN * kUmBM * 4 <= GG::NS * GG::STAGE)
                 split = sc;
     at[0].val.clusterDim.x = (unsigned)split;
     at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3((unsigned)(tiles * split));
+    cfg.gridDim = dim3((unsigned)(tiles * split), (unsigned)((m + BN - 1) / BN));
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tm_codes, tm_scales, tm_act, static_cast<const T *>(bias),
                                        static_cast<T *>(y), (int)m, (int)n, (int)k, qa);
     count_launch();
@@ -605,14 +606,15 @@ int launch_umma_t(const void *a, const uint8_t *b, const void *scales, const voi
 
 }  // namespace
 
-// fp16/bf16, block 32, default zero point, 17 <= m <= 128, N a multiple of
-// 128, K a multiple of 256, codes / scales / activations 16-byte aligned.
+// fp16/bf16, block 32, default zero point, m >= 17 (blocks of 128 rows above
+// 128), N a multiple of 128, K a multiple of 256, codes / scales /
+// activations 16-byte aligned.
 // (Up to 16 rows the mma.sync kernels are faster: each tcgen05.mma here costs
 // about 65 cycles of issue whatever N is, and a tile needs K/8 of them.)
 bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
                                 int64_t m, int64_t n, int64_t k, int block_size) {
     if (dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16) return false;
-    if (zp || block_size != 32 || m < 17 || m > 128) return false;
+    if (zp || block_size != 32 || m < 17 || m > (1 << 22)) return false;  // grid.y = m / 128 blocks
     if (n % kUmBM != 0 || k % kUmKC != 0 || n > (1 << 30) || k > (1 << 24)) return false;
     const uintptr_t al = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
                          reinterpret_cast<uintptr_t>(scales);

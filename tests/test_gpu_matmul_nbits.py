@@ -144,3 +144,9 @@ def test_tcgen05_path_c2_shape_bf16(cuda_device):
 def test_c2_shape_m128_fp16(cuda_device):
     """128 activation rows (a prefill chunk) on the tcgen05 path."""
     _run(cuda_device, 128, 14336, 4096, adtype=torch.float16, seed=43)
+
+
+@pytest.mark.parametrize("m", [129, 200, 520])
+def test_tcgen05_row_blocks(cuda_device, m):
+    """More than 128 rows (prefill): blocks of 128 activation rows, the last one ragged."""
+    _run(cuda_device, m, 1024, 2048, adtype=torch.bfloat16, bias=True, seed=500 + m)
