@@ -124,10 +124,7 @@ constexpr int kMnbActRow = kMnbChunk * 32 * 2;     // 512 B: one activation row 
 __host__ __device__ constexpr int mnb_slots(int mrows) { return 2 + 0 * mrows; }
 // K splits (warps) per CTA: more warps for one m-tile, fewer when the
 // activation tiles are large.
-__host__ __device__ constexpr int mnb_split(int mt) { return mt == 1 ? 4 : 2; }
-__host__ __device__ constexpr int mnb_slot_bytes(int mrows) {
-    return kMnbCodeTile + kMnbScaleTile + ((mrows * kMnbActRow + 127) / 128) * 128;
-}
+[[maybe_unused]] constexpr int mnb_split(int mt) { return mt == 1 ? 4 : 2; }
 
 template <typename T>
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,

@@ -49,7 +49,6 @@ namespace {
 
 constexpr int kUmBM = 128;                  // weight rows per CTA (UMMA M)
 constexpr int kUmKC = 256;                  // k per TMA stage
-constexpr int kUmSub = 64;                  // k per TMEM A buffer
 constexpr int kUmNA = 4;                    // A buffers in TMEM (an even number: buffer q % NA belongs to group q % 2)
 constexpr int kUmCodeTile = kUmBM * 128;    // [128 rows][128 B]
 constexpr int kUmScaleTile = kUmBM * 16;    // [128 rows][8 scales]
