@@ -451,6 +451,89 @@ def run_decode_block(args):
     return 0
 
 
+def run_decode_layer(args):
+    """``--workload decode_layer``: one whole decoder layer per step (not the headline).
+
+    smallaios_b200.decoder_layer_step: SkipSimplifiedLayerNormalization, the
+    fused QKV projection (RoPE + append), attention over the cache, o_proj,
+    SkipSimplifiedLayerNormalization, the packed gate|up projection, SwiGLU,
+    down_proj; all projections int4 MatMulNBits (random codes, scales
+    U[0.005, 0.02], block 32), the cache is the headline's.
+    """
+    import torch
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cache, cos, sin, _, _, _ = build_workload(torch, sa, dev, seed=1)
+    hidden, inter = (4096, 14336) if args.config == "c3" else (8192, 28672)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+
+    def weight(n, k):
+        codes = torch.randint(0, 256, (n, k // 32, 16), dtype=torch.uint8, device=dev, generator=g)
+        scales = (torch.rand(n, k // 32, device=dev, generator=g) * 0.015 + 0.005).to(torch.bfloat16)
+        return codes, scales
+
+    qkv = weight((HQ + 2 * HKV) * D, hidden)
+    wo = weight(hidden, HQ * D)
+    wgu = weight(2 * inter, hidden)
+    wdn = weight(hidden, inter)
+    ones = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+    w = sa.LayerWeights(*qkv, *wo, *wgu, *wdn, ones, ones, 1e-5)
+    x = torch.randn(B, hidden, device=dev, generator=g).to(torch.bfloat16)
+    resid = torch.randn(B, hidden, device=dev, generator=g).to(torch.bfloat16)
+
+    def step():
+        cache.set_position(T - 1)
+        sa.decoder_layer_step(x, resid, w, cache, 0, cos_cache=cos, sin_cache=sin)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    c0 = lib.sa_kernel_launches()
+    with torch.cuda.graph(graph):
+        step()
+    launches = lib.sa_kernel_launches() - c0
+    for _ in range(args.warmup):
+        graph.replay()
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    t_ms = e0.elapsed_time(e1) / args.steps
+    peak, peak_kind = load_peaks()
+    wbytes = sum(c.numel() + s.numel() * 2 for c, s in (qkv, wo, wgu, wdn))
+    byts = wbytes + attend_bytes() + 2 * B * HKV * (CB + 8) + 12 * B * hidden * 2
+    line = {
+        "metric": f"decoder layer tokens/s (one full decode-step layer), {WORKLOAD}",
+        "value": B / (t_ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4-w/int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded; random int4 weights)",
+        "config": {"workload": f"decoder layer, {WORKLOAD}", "batch": B, "hidden": hidden, "intermediate": inter,
+                   "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
+                   "launch": "CUDA graph of one step, replayed"},
+        "gpu_launches": int(launches) * args.steps, "launches_per_step": int(launches),
+        "roofline": {"bound": "hbm", "achieved": byts / (t_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": byts / (t_ms * 1e-3) / 1e9 / peak, "algorithmic_bytes": byts, "weight_bytes": wbytes,
+                     "traffic": None, "peak_source": f"{peak_kind} hbm_gbs"},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    graph.reset()
+    cache.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -462,8 +545,8 @@ def main():
                     help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
     ap.add_argument("--batch", type=int, default=None,
                     help="gqa_decode: override the config's batch (a smaller case for profiler captures)")
-    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block"],
-                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); one line, 1 GPU")
+    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block", "decode_layer"],
+                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); decode_layer = a whole decoder layer; one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
     ap.add_argument("--packed", action="store_true", help="matmul_nbits: weights prepacked once (m <= 8)")
     ap.add_argument("--no-graph", action="store_true",
@@ -487,6 +570,8 @@ def main():
         return run_matmul_nbits(args)
     if args.workload == "decode_block":
         return run_decode_block(args)
+    if args.workload == "decode_layer":
+        return run_decode_layer(args)
 
     import torch
     import torch.distributed as dist

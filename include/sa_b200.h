@@ -318,6 +318,28 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
                           int32_t do_rotary, int32_t rotary_interleaved, void *q_out, void *k_out,
                           void *v_out, sa_stream_t stream);
 
+/* ======================================================================
+ * Decoder-layer glue (the ops around GQA and MatMulNBits in a decoder
+ * layer, onnx-rt/src/model_loader/gemma.rs:13-36).
+ *
+ * sa_rms_norm: com.microsoft.SkipSimplifiedLayerNormalization
+ * (onnx-rt/src/ops/microsoft.rs:491-540) over rows of `cols`:
+ *   pre = x + skip (+ bias);  y = pre / sqrt(mean(pre^2) + epsilon) * weight
+ * with f32 arithmetic.  skip == NULL gives SimplifiedLayerNormalization /
+ * RMSNormalization (microsoft.rs:447-480, generative.rs:517-580); `pre`
+ * may be NULL (not stored).  x, skip, y, pre: (rows, cols); weight, bias:
+ * (cols), all of dtype.
+ *
+ * sa_silu_mul: SwiGLU, Silu(gate) * up (GraphBuilder::swiglu,
+ * graph_builder.rs:366-369): y[r][j] = gate[r][j] / (1 + exp(-gate[r][j])) *
+ * up[r][j], gate and up rows `ld_in` elements apart (ld_in = cols for
+ * separate tensors, 2*cols for one packed gate|up projection), y (rows, cols).
+ * ====================================================================== */
+int sa_rms_norm(const void *x, const void *skip, const void *bias, const void *weight, void *y, void *pre,
+                int32_t dtype, int64_t rows, int64_t cols, float epsilon, sa_stream_t stream);
+int sa_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int32_t dtype, int64_t rows,
+                int64_t cols, sa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

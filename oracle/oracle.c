@@ -588,3 +588,42 @@ int orc_matmul_nbits(const float *a, const uint8_t *b_codes, const float *scales
     free(wt);
     return ORC_OK;
 }
+
+/* ---- decoder-layer glue ----------------------------------------------------
+ * sqrt of op_rms_normalization: libm_sqrt (ops/generative.rs:96-106), 16
+ * Newton steps from x, 0 for x <= 0. */
+static float libm_sqrt_newton(float x) {
+    if (x <= 0.0f) return 0.0f;
+    float guess = x;
+    for (int i = 0; i < 16; i++) guess = 0.5f * (guess + x / guess);
+    return guess;
+}
+
+/* SkipSimplifiedLayerNormalization (ops/microsoft.rs:491-540) over rows of
+ * `cols`: pre = x + skip (+ bias), y = rms_norm(pre) * w with
+ * op_rms_normalization (ops/generative.rs:517-580): ss accumulated in index
+ * order, rms_inv = 1 / libm_sqrt(ss / n + eps), y = v * rms_inv * w.  With
+ * skip == NULL it is SimplifiedLayerNormalization without its bias. */
+void orc_rms_norm(const float *x, const float *skip, const float *bias, const float *w, float *y, float *pre,
+                  int rows, int cols, float eps) {
+    for (int r = 0; r < rows; r++) {
+        const float *xr = x + (size_t)r * cols;
+        float *pr = pre + (size_t)r * cols;
+        float ss = 0.0f;
+        for (int i = 0; i < cols; i++) {
+            float v = xr[i];
+            if (skip) v = v + skip[(size_t)r * cols + i];
+            if (bias) v = v + bias[i];
+            pr[i] = v;
+            ss += v * v;
+        }
+        float rms_inv = 1.0f / libm_sqrt_newton(ss / (float)cols + eps);
+        for (int i = 0; i < cols; i++) y[(size_t)r * cols + i] = pr[i] * rms_inv * w[i];
+    }
+}
+
+/* SwiGLU: Swish (ops/activations.rs:37-39, x / (1 + expf_approx(-x))) of the
+ * gate times up (the Mul of GraphBuilder::swiglu, graph_builder.rs:366-369). */
+void orc_silu_mul(const float *gate, const float *up, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = gate[i] / (1.0f + orc_expf_approx(-gate[i])) * up[i];
+}

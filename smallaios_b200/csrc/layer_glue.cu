@@ -1,0 +1,112 @@
+// The decoder-layer glue around the attention and MatMulNBits: RMSNorm with an
+// optional fused residual add (com.microsoft.SimplifiedLayerNormalization /
+// SkipSimplifiedLayerNormalization, onnx-rt/src/ops/microsoft.rs:441-540, on
+// op_rms_normalization, onnx-rt/src/ops/generative.rs:517-580), and SwiGLU
+// (Silu(gate) * up, the Silu + Mul pair GraphBuilder::swiglu emits,
+// onnx-rt/src/model_loader/graph_builder.rs:366-369; Silu as in
+// onnx-rt/src/ops/activations.rs:37-39).  Both are HBM-bound row kernels
+// with coalesced loads and f32 arithmetic, rounding once to the activation
+// type at the store (RMSNorm: one CTA per row; SwiGLU: a row per grid.y).
+#include "sa_common.cuh"
+#include "sa_internal.h"
+
+namespace sa {
+
+namespace {
+
+constexpr int kGlueThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ float glue_ld(const T *p, int64_t i) {
+    return ld_f32(p + i);
+}
+
+// pre = x (+ skip) (+ bias); y = pre / sqrt(mean(pre^2) + eps) * w.
+// `pre` (optional) receives the rounded pre-sum: the residual of the next add.
+template <typename T>
+__global__ void __launch_bounds__(kGlueThreads)
+    rms_norm_kernel(const T *__restrict__ x, const T *__restrict__ skip, const T *__restrict__ bias,
+                    const T *__restrict__ w, T *__restrict__ y, T *__restrict__ pre, int cols, float eps) {
+    __shared__ float s_red[kGlueThreads / 32];
+    const int64_t base = (int64_t)blockIdx.x * cols;
+    const int tid = threadIdx.x;
+    float ss = 0.0f;
+    for (int i = tid; i < cols; i += kGlueThreads) {
+        float v = glue_ld(x, base + i);
+        if (skip) v += glue_ld(skip, base + i);
+        if (bias) v += glue_ld(bias, i);
+        if (pre) st_from_f32(pre + base + i, v);
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+        float t = tid < kGlueThreads / 32 ? s_red[tid] : 0.0f;
+        t = warp_sum(t);
+        if (tid == 0) s_red[0] = t;
+    }
+    __syncthreads();
+    const float rinv = 1.0f / sqrtf(s_red[0] / (float)cols + eps);
+    for (int i = tid; i < cols; i += kGlueThreads) {
+        float v = glue_ld(x, base + i);
+        if (skip) v += glue_ld(skip, base + i);
+        if (bias) v += glue_ld(bias, i);
+        st_from_f32(y + base + i, v * rinv * glue_ld(w, i));
+    }
+}
+
+// y[r][j] = silu(gate[r][j]) * up[r][j], silu(g) = g / (1 + exp(-g)).
+template <typename T>
+__global__ void __launch_bounds__(kGlueThreads)
+    silu_mul_kernel(const T *__restrict__ gate, const T *__restrict__ up, int64_t ld_in, T *__restrict__ y,
+                    int cols) {
+    const int64_t r = blockIdx.y;
+    for (int j = blockIdx.x * kGlueThreads + threadIdx.x; j < cols; j += gridDim.x * kGlueThreads) {
+        const float g = glue_ld(gate, r * ld_in + j), u = glue_ld(up, r * ld_in + j);
+        st_from_f32(y + r * cols + j, g / (1.0f + expf(-g)) * u);
+    }
+}
+
+template <typename T>
+int launch_rms_t(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int64_t rows,
+                 int64_t cols, float eps, cudaStream_t stream) {
+    rms_norm_kernel<T><<<(unsigned)rows, kGlueThreads, 0, stream>>>(
+        static_cast<const T *>(x), static_cast<const T *>(skip), static_cast<const T *>(bias),
+        static_cast<const T *>(w), static_cast<T *>(y), static_cast<T *>(pre), (int)cols, eps);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "rms_norm launch");
+}
+
+template <typename T>
+int launch_silu_t(const void *gate, const void *up, int64_t ld_in, void *y, int64_t rows, int64_t cols,
+                  cudaStream_t stream) {
+    const int64_t blocks = (cols + kGlueThreads - 1) / kGlueThreads;
+    const unsigned bx = (unsigned)(blocks < 64 ? blocks : 64);
+    silu_mul_kernel<T><<<dim3(bx, (unsigned)rows), kGlueThreads, 0, stream>>>(
+        static_cast<const T *>(gate), static_cast<const T *>(up), ld_in, static_cast<T *>(y), (int)cols);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "silu_mul launch");
+}
+
+}  // namespace
+
+int launch_rms_norm(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int dtype,
+                    int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+    switch (dtype) {
+        case SA_DTYPE_FLOAT: return launch_rms_t<float>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        case SA_DTYPE_FLOAT16: return launch_rms_t<__half>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        default: return launch_rms_t<__nv_bfloat16>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+    }
+}
+
+int launch_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int dtype, int64_t rows, int64_t cols,
+                    cudaStream_t stream) {
+    switch (dtype) {
+        case SA_DTYPE_FLOAT: return launch_silu_t<float>(gate, up, ld_in, y, rows, cols, stream);
+        case SA_DTYPE_FLOAT16: return launch_silu_t<__half>(gate, up, ld_in, y, rows, cols, stream);
+        default: return launch_silu_t<__nv_bfloat16>(gate, up, ld_in, y, rows, cols, stream);
+    }
+}
+
+}  // namespace sa

@@ -118,6 +118,10 @@ int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, con
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
                         int block_size, cudaStream_t stream);
 int launch_qkv_finish(const QkvArgs &a, cudaStream_t stream);
+int launch_rms_norm(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int dtype,
+                    int64_t rows, int64_t cols, float eps, cudaStream_t stream);
+int launch_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int dtype, int64_t rows, int64_t cols,
+                    cudaStream_t stream);
 int launch_qkv_umma_fused(const void *x, const uint8_t *w_codes, const void *w_scales, const QkvArgs &a,
                           int64_t n, int64_t k, cudaStream_t stream);
 bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,

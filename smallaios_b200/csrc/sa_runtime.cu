@@ -647,4 +647,27 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
     return launch_qkv_finish(a, st);
 }
 
+int sa_rms_norm(const void *x, const void *skip, const void *bias, const void *weight, void *y, void *pre,
+                int32_t dtype, int64_t rows, int64_t cols, float epsilon, sa_stream_t stream) {
+    if (!dtype_ok(dtype)) return set_error(SA_ERR_UNSUPPORTED, "rms_norm: dtype %d not supported", dtype);
+    if (rows < 0 || cols <= 0 || cols > (1 << 30) || rows > 0x7fffffff)
+        return set_error(SA_ERR_SHAPE_MISMATCH, "RMSNormalization: normalized region is empty or too large");
+    if (rows == 0) return SA_OK;
+    if (!x || !weight || !y) return set_error(SA_ERR_INVALID_ARGUMENT, "rms_norm: NULL input/output");
+    if (!(epsilon >= 0.0f)) return set_error(SA_ERR_INVALID_ATTRIBUTE, "rms_norm: epsilon must be >= 0");
+    return launch_rms_norm(x, skip, bias, weight, y, pre, dtype, rows, cols, epsilon,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int sa_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int32_t dtype, int64_t rows,
+                int64_t cols, sa_stream_t stream) {
+    if (!dtype_ok(dtype)) return set_error(SA_ERR_UNSUPPORTED, "silu_mul: dtype %d not supported", dtype);
+    if (rows < 0 || cols <= 0 || ld_in < cols || rows > 65535 || cols > (1 << 30))
+        return set_error(SA_ERR_SHAPE_MISMATCH, "silu_mul: bad shape (rows %lld, cols %lld, ld_in %lld)",
+                         (long long)rows, (long long)cols, (long long)ld_in);
+    if (rows == 0) return SA_OK;
+    if (!gate || !up || !y) return set_error(SA_ERR_INVALID_ARGUMENT, "silu_mul: NULL input/output");
+    return launch_silu_mul(gate, up, ld_in, y, dtype, rows, cols, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

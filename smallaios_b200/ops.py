@@ -252,6 +252,61 @@ def qkv_project_append(x: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.T
     return q_out, k_out, v_out
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, *, skip: torch.Tensor | None = None,
+             bias: torch.Tensor | None = None, epsilon: float = 1e-5, out: torch.Tensor | None = None,
+             pre_out: torch.Tensor | None = None, stream=None):
+    """SkipSimplifiedLayerNormalization / SimplifiedLayerNormalization over the last axis.
+
+    Returns ``(y, pre)``: ``pre = x + skip (+ bias)`` (``x`` itself when there
+    is no skip or bias), ``y = pre / sqrt(mean(pre^2) + epsilon) * weight``.
+    """
+    for name, t in (("x", x), ("weight", weight), ("skip", skip), ("bias", bias)):
+        _cuda(t, name)
+    cols = x.shape[-1]
+    if weight.numel() != cols or (bias is not None and bias.numel() != cols):
+        raise ShapeMismatch("RMSNormalization: scale must match normalized region")
+    if skip is not None and skip.shape != x.shape:
+        raise ShapeMismatch("SkipSimplifiedLayerNormalization: x and skip must have matching shapes")
+    for name, t in (("weight", weight), ("skip", skip), ("bias", bias)):
+        if t is not None and t.dtype != x.dtype:
+            raise UnsupportedOp(f"rms_norm: {name} must have x's dtype")
+    if out is None:
+        out = torch.empty_like(x)
+    need_pre = skip is not None or bias is not None
+    if need_pre and pre_out is None:
+        pre_out = torch.empty_like(x)
+    rc = lib.sa_rms_norm(x.data_ptr(), None if skip is None else skip.data_ptr(),
+                         None if bias is None else bias.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                         pre_out.data_ptr() if need_pre else None, _dtype_code(x), x.numel() // cols, cols,
+                         float(epsilon), _stream_handle(stream, x.device))
+    _raise_op(rc, "RMSNormalization")
+    return out, (pre_out if need_pre else x)
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor | None = None, *, out: torch.Tensor | None = None, stream=None):
+    """SwiGLU: Silu(gate) * up.  With ``up`` None, ``gate`` is one packed (rows, 2F)
+    gate|up projection (gate in the first F columns)."""
+    _cuda(gate, "gate")
+    if up is None:
+        rows, two_f = gate.shape[0], gate.shape[-1]
+        if two_f % 2:
+            raise ShapeMismatch("silu_mul: a packed gate|up projection has an even width")
+        f, ld = two_f // 2, two_f
+        g_ptr, u_ptr = gate.data_ptr(), gate.data_ptr() + f * gate.element_size()
+    else:
+        _cuda(up, "up")
+        if up.shape != gate.shape or up.dtype != gate.dtype:
+            raise ShapeMismatch("silu_mul: gate and up must have the same shape and dtype")
+        rows, f = gate.shape[0], gate.shape[-1]
+        ld, g_ptr, u_ptr = f, gate.data_ptr(), up.data_ptr()
+    if out is None:
+        out = torch.empty(rows, f, dtype=gate.dtype, device=gate.device)
+    rc = lib.sa_silu_mul(g_ptr, u_ptr, ld, out.data_ptr(), _dtype_code(gate), rows, f,
+                         _stream_handle(stream, gate.device))
+    _raise_op(rc, "silu_mul")
+    return out
+
+
 class PackedNBitsWeight:
     """A MatMulNBits weight repacked once for the decode GEMV (``sa_matmul_nbits_prepack``).
 
