@@ -375,3 +375,24 @@ def test_matmul_nbits_matches_float_dequant():
     q = np.stack([lo, hi], -1).reshape(n, k).astype(np.float64)
     w = (q - 8.0) * np.repeat(scales, 32, axis=1)
     assert np.allclose(y, a.astype(np.float64) @ w.T, atol=1e-4)
+
+
+def test_rms_norm_known_answers():
+    """generative.rs rms_norm_constant_input / rms_norm_preserves_zero_mean_direction."""
+    y, _ = oracle.rms_norm(np.ones((1, 4)), np.full(4, 0.5), 1e-6)
+    assert np.all(np.abs(y - 0.5) < 1e-4)
+    y, _ = oracle.rms_norm(np.array([[1.0, -1.0, 1.0, -1.0]]), np.ones(4), 1e-6)
+    assert np.all(np.abs(y - np.array([1.0, -1.0, 1.0, -1.0])) < 1e-3)
+    # SkipSimplifiedLayerNormalization: pre = x + skip + bias is returned
+    x, s, b = np.array([[1.0, 2.0]]), np.array([[3.0, -1.0]]), np.array([0.5, 0.5])
+    y, pre = oracle.rms_norm(x, np.ones(2), 0.0, skip=s, bias=b)
+    assert np.allclose(pre, [[4.5, 1.5]])
+    assert np.allclose(y, pre / np.sqrt((pre ** 2).mean()), atol=1e-6)
+
+
+def test_silu_known_answers():
+    """activations.rs test_swish_at_zero / test_swish_known_values / test_swish_negative."""
+    y = oracle.silu_mul(np.array([0.0, 1.0, 2.0, -1.0]), np.ones(4))
+    assert abs(y[0]) < 1e-5
+    assert abs(y[1] - 0.7310) < 1e-2 and abs(y[2] - 1.7616) < 1e-2 and abs(y[3] + 0.2689) < 1e-2
+    assert np.allclose(oracle.silu_mul(np.array([1.0]), np.array([3.0])), 3 * 0.7310586, atol=1e-4)
