@@ -350,7 +350,8 @@ def matmul_nbits_packed(a: torch.Tensor, w: PackedNBitsWeight, bias: torch.Tenso
 
 
 # ---- executor glue ------------------------------------------------------------
-SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits")
+SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits", "RMSNormalization", "SimplifiedLayerNormalization",
+                 "SkipSimplifiedLayerNormalization")
 
 
 def supports_op(op_type: str) -> bool:
@@ -392,6 +393,18 @@ def dispatch_gpu_node(op_type: str, inputs: list, attrs: dict, kv_cache_ctx: KvC
             cos_cache=inp[7] if inp[7] is not None else kv_cache_ctx.rope.get("cos_cache"),
             sin_cache=inp[8] if inp[8] is not None else kv_cache_ctx.rope.get("sin_cache"))
         return [out]
+    if op_type in ("RMSNormalization", "SimplifiedLayerNormalization"):
+        # inputs (X, scale[, bias]); attributes epsilon (1e-5), axis (-1: the last axis only)
+        if int(attrs.get("axis", -1)) not in (-1, inputs[0].dim() - 1):
+            raise InvalidAttribute(f"{op_type}: only the last axis is normalized on this path")
+        inp = list(inputs) + [None] * (3 - len(inputs))
+        y, _ = rms_norm(inp[0], inp[1], bias=inp[2], epsilon=float(attrs.get("epsilon", 1e-5)))
+        return [y]
+    if op_type == "SkipSimplifiedLayerNormalization":
+        # inputs (input, skip, gamma[, bias]) -> [output, input_skip_bias_sum]
+        inp = list(inputs) + [None] * (4 - len(inputs))
+        y, pre = rms_norm(inp[0], inp[2], skip=inp[1], bias=inp[3], epsilon=float(attrs.get("epsilon", 1e-5)))
+        return [y, pre]
     if op_type == "MatMulNBits":
         inp = list(inputs) + [None] * (6 - len(inputs))
         return [matmul_nbits(inp[0], inp[1], inp[2], inp[3], inp[5], K=int(attrs["K"]), N=int(attrs["N"]),

@@ -133,3 +133,25 @@ def test_decoder_layer_step(cuda_device, b):
                                                                      want_pre2)):
         rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
         assert rel <= 1e-2, f"{name}: relative error {rel:.3e}"
+
+
+def test_dispatch_norm_nodes(cuda_device):
+    """dispatch_gpu_node arms for the normalization ops (ORT input orders)."""
+    import smallaios_b200 as sa
+
+    for op in ("RMSNormalization", "SimplifiedLayerNormalization", "SkipSimplifiedLayerNormalization"):
+        assert sa.supports_op(op)
+    r = rng(13)
+    x = r.standard_normal((2, 3, 64)).astype(np.float32)
+    s = r.standard_normal((2, 3, 64)).astype(np.float32)
+    w = r.uniform(0.5, 1.5, 64).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda_device)
+    (y,) = sa.dispatch_gpu_node("SimplifiedLayerNormalization", [t(x), t(w)], {"epsilon": 1e-6})
+    want, _ = oracle.rms_norm(x, w, 1e-6)
+    assert np.allclose(y.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    y, pre = sa.dispatch_gpu_node("SkipSimplifiedLayerNormalization", [t(x), t(s), t(w)], {"epsilon": 1e-6})
+    want, want_pre = oracle.rms_norm(x, w, 1e-6, skip=s)
+    assert np.allclose(y.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
+    assert np.allclose(pre.cpu().numpy(), want_pre, rtol=1e-6, atol=1e-6)
+    with pytest.raises(sa.InvalidAttribute):
+        sa.dispatch_gpu_node("RMSNormalization", [t(x), t(w)], {"axis": 1})
