@@ -11,7 +11,8 @@
 //             tile (128-byte swizzle), the [128 x 8] scale tile and four
 //             [BN x 64] activation tiles in the canonical K-major SW128
 //             layout the MMA reads directly.
-//  warp 1     allocates 512 TMEM columns; lane 0 issues the MMAs
+//  warps 1,10 warp 1 allocates 512 TMEM columns; one elected lane of each
+//             issues the MMAs of the even / odd sub-chunks
 //             (tcgen05.mma kind::f16, A from TMEM, B from shared memory,
 //             D = f32 in TMEM: 256 / BN accumulators of BN columns taken in
 //             turn, so that back-to-back MMAs are independent) and commits
@@ -53,7 +54,7 @@ constexpr int kUmNA = 4;                    // A buffers in TMEM (an even number
 constexpr int kUmCodeTile = kUmBM * 128;    // [128 rows][128 B]
 constexpr int kUmScaleTile = kUmBM * 16;    // [128 rows][8 scales]
 constexpr int kUmDqWarps = 8;
-constexpr int kUmThreads = 32 * (2 + kUmDqWarps);
+constexpr int kUmThreads = 32 * (3 + kUmDqWarps);  // + the TMA warp and two MMA warps
 constexpr uint32_t kUmTmemCols = 512;       // accumulators in [0, 256), A buffers in [256, 512)
 constexpr uint32_t kUmAcol = 256;
 
@@ -283,13 +284,13 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < GG::NS; i++) {
             mbar_init(full + i, 1);
-            mbar_init(empty + i, kUmDqWarps + 1);
+            mbar_init(empty + i, kUmDqWarps + 2);
         }
         for (int i = 0; i < kUmNA; i++) {
             mbar_init(afull + i, 4);
             mbar_init(aempty + i, 1);
         }
-        mbar_init(dfull, 1);
+        mbar_init(dfull, 2);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -319,12 +320,15 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 issued = c + 1;
             }
         }
-    } else if (warp == 1) {
-        // the whole warp runs the loop (uniform descriptors); one elected lane issues
+    } else if (warp == 1 || warp == 10) {
+        // two MMA warps take the even and the odd sub-chunks, each into its own half of the
+        // accumulators (issuing from two warps is 6-9% faster than from one); the whole warp
+        // runs the loop (uniform descriptors) and one elected lane issues
+        const int par = warp == 1 ? 0 : 1;
         constexpr uint32_t idesc = umma_idesc<T, BN>();
-        for (int q = 0; q < nsub; q++) {
+        for (int q = par; q < nsub; q += 2) {
             const int c = q >> 2, j = q & 3, s = c % GG::NS, ab = q % kUmNA;
-            bool ok = j != 0 || um_wait(full + s, (uint32_t)((c / GG::NS) & 1), abort_flag);
+            bool ok = j != par || um_wait(full + s, (uint32_t)((c / GG::NS) & 1), abort_flag);
             if (ok) ok = um_wait(afull + ab, (uint32_t)((q / kUmNA) & 1), abort_flag);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
@@ -336,13 +340,14 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                     const uint64_t bdesc = sw128_kmajor_desc(act + 32 * kk);
 #pragma unroll
                     for (int h = 0; h < 2; h++) {  // A1 = (q-8)*s1, A2 = (q-8)*s2
-                        const int idx = q * 8 + 2 * kk + h;
-                        umma_ts(tbase + (uint32_t)((idx % GG::NACC) * BN), ta + 32 * h + 8 * kk, bdesc, idesc,
-                                idx >= GG::NACC ? 1u : 0u);
+                        const int idx = (q >> 1) * 8 + 2 * kk + h;  // this warp's MMA count
+                        constexpr int HA = GG::NACC / 2;
+                        umma_ts(tbase + (uint32_t)((par * HA + idx % HA) * BN), ta + 32 * h + 8 * kk, bdesc, idesc,
+                                idx >= HA ? 1u : 0u);
                     }
                 }
                 umma_commit(aempty + ab);
-                if (j == 3) umma_commit(empty + s);
+                if (j >= 2) umma_commit(empty + s);  // each MMA warp's last sub-chunk of the chunk
             }
             __syncwarp();
         }

@@ -1,8 +1,9 @@
 """Decoder-layer glue and one whole decoder layer (decode step) against the oracle.
 
 - sa_rms_norm (SkipSimplifiedLayerNormalization / SimplifiedLayerNormalization)
-  and sa_silu_mul (SwiGLU) element for element: f32 within 1e-5 relative,
-  fp16/bf16 within 1e-3 plus half an ulp of the output type.
+  element for element: f32 within 1e-5 relative, fp16/bf16 within 1e-3 plus
+  half an ulp of the output type; sa_silu_mul (SwiGLU) within 1e-3 (the
+  oracle's Swish uses the reference's expf_approx, the kernel CUDA's expf).
 - decoder_layer_step: the layer of the reference's model loader composed
   from the oracle's own ops (RMSNorm, MatMulNBits, RoPE, PolarQuant append,
   compressed attention, SwiGLU), rounding to the activation type where the
@@ -68,7 +69,8 @@ def test_silu_mul_packed_and_separate(cuda_device, dt):
     for got in (sa.silu_mul(t), sa.silu_mul(t[:, :f].contiguous(), t[:, f:].contiguous())):
         torch.cuda.synchronize()
         g = got.float().cpu().numpy()
-        bound = _bound(want, dtype) + (1e-5 if dtype == torch.float32 else 0.0)
+        # the oracle's Swish uses the reference's expf_approx, the kernel CUDA's expf: f32 within the 1e-3 bar
+        bound = 1e-3 + np.abs(want) * 1e-5 if dtype == torch.float32 else _bound(want, dtype)
         assert np.all(np.abs(g - want) <= bound), f"max err {np.abs(g - want).max():.3e}"
 
 
