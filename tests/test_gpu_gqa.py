@@ -159,6 +159,29 @@ def test_prefill_chunk_causal(cuda_device):
     _check(got, want, torch.float32)
 
 
+@pytest.mark.parametrize("d,hq,hkv,bits", [(128, 32, 8, 4), (128, 16, 2, 8), (64, 8, 8, 4), (64, 8, 4, 8),
+                                           (128, 8, 1, 4)])
+def test_prefill_tensor_core(cuda_device, d, hq, hkv, bits):
+    """Prefill chunks of 16+ query tokens run on the tensor-core kernel (groups 1, 2, 4, 8):
+    a 200-token chunk after 60 cached tokens (past > 0, rows across CTAs, a ragged last tile)."""
+    got, want = _decode_case(cuda_device, b=2, hq=hq, hkv=hkv, d=d, bits=bits, t=260, s=200, seed=d + hq + bits,
+                             chunks=(60,), theta=500000.0)
+    _check(got, want, torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_whole_prompt_half(cuda_device, dtype):
+    """A whole 300-token prompt in one call (empty cache), fp16/bf16 activations."""
+    got, want = _decode_case(cuda_device, b=2, hq=32, hkv=8, d=128, bits=8, t=300, s=300, dtype=dtype, seed=31)
+    _check(got, want, dtype)
+
+
+def test_prefill_interleaved_rope_scale_16_tokens(cuda_device):
+    got, want = _decode_case(cuda_device, b=3, hq=8, hkv=2, d=64, bits=4, t=40, s=16, seed=32, interleaved=True,
+                             scale=0.2)
+    _check(got, want, torch.float32)
+
+
 def test_first_token_and_tiny_context(cuda_device):
     for t in (1, 2, 3, 5):
         got, want = _decode_case(cuda_device, b=1, hq=4, hkv=2, d=64, bits=4, t=t, seed=t)
