@@ -534,6 +534,82 @@ def run_decode_layer(args):
     return 0
 
 
+def run_prefill_attention(args):
+    """``--workload prefill``: the attention of the C4 prefill (not the headline).
+
+    One step = one GroupQueryAttention call on a whole prompt per sequence
+    (B = 8, S = 2048, 32 query / 8 KV heads, D = 128, int8 KV, theta 5e5):
+    quantize-on-append of the 2048 tokens, then causal attention of the 2048
+    queries on the tensor-core prefill kernel.  Roofline: tensor (causal
+    attention FLOPs 4*B*Hq*S*S/2*D against the measured bf16 peak; the kernel
+    computes in fp16 on mma.sync).
+    """
+    import torch
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    b, s, hq, hkv, d, bits = 8, 2048, 32, 8, 128, 8
+    cos_np, sin_np = rope_np(s + 8, d, THETA)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    cache = sa.GpuKvCache(1, hkv, d, s + 8, batch=b, num_heads=hq, bits=bits, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    q = (torch.randn(b, s, hq * d, device=dev, generator=g) * 1.28).to(torch.bfloat16)
+    k = (torch.randn(b, s, hkv * d, device=dev, generator=g) * 1.28).to(torch.bfloat16)
+    v = (torch.randn(b, s, hkv * d, device=dev, generator=g) * 1.28).to(torch.bfloat16)
+    out = torch.empty_like(q)
+
+    def step():
+        cache.set_position(0)
+        sa.group_query_attention(q, k, v, cache, 0, num_heads=hq, kv_num_heads=hkv, cos_cache=cos, sin_cache=sin,
+                                 out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    sampler.start()
+    l0 = lib.sa_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    launches = lib.sa_kernel_launches() - l0
+    t_ms = e0.elapsed_time(e1) / args.steps
+    flops = 4.0 * b * hq * s * s / 2 * d
+    peak_tf = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak_tf = float(json.load(f).get("bf16_tflops", 0)) or None
+    peak_kind = "measured bf16_tflops" if peak_tf else "fallback 1590 TFLOP/s"
+    peak_tf = peak_tf or 1590.0
+    achieved = flops / (t_ms * 1e-3) / 1e12
+    line = {
+        "metric": "prefill attention tokens/s (quantize-on-append + causal GQA of whole prompts), BASELINE config 4 shape",
+        "value": b * s / (t_ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8-kv/bf16-act/fp16-mma/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
+        "config": {"workload": "llama3-8b prefill attention, one layer (BASELINE config 4 shape)", "batch": b,
+                   "prompt": s, "q_heads": hq, "kv_heads": hkv, "head_dim": d, "kv_bits": bits,
+                   "launch": "host launches"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "algorithmic_flops": flops, "traffic": None,
+                     "peak_source": peak_kind},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    cache.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -545,8 +621,8 @@ def main():
                     help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
     ap.add_argument("--batch", type=int, default=None,
                     help="gqa_decode: override the config's batch (a smaller case for profiler captures)")
-    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block", "decode_layer"],
-                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); decode_layer = a whole decoder layer; one line, 1 GPU")
+    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block", "decode_layer", "prefill"],
+                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); decode_layer = a whole decoder layer; prefill = the C4 prefill attention; one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
     ap.add_argument("--packed", action="store_true", help="matmul_nbits: weights prepacked once (m <= 8)")
     ap.add_argument("--no-graph", action="store_true",
@@ -572,6 +648,8 @@ def main():
         return run_decode_block(args)
     if args.workload == "decode_layer":
         return run_decode_layer(args)
+    if args.workload == "prefill":
+        return run_prefill_attention(args)
 
     import torch
     import torch.distributed as dist
