@@ -138,7 +138,7 @@ def _declare(l: ctypes.CDLL) -> None:
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"smallaios_b200: {LIB_PATH} is missing; build it with `python -m smallaios_b200.build` "
+            f"smallaios_b200: {LIB_PATH} is missing; build it with `python smallaios_b200/build.py` "
             "(there is no CPU fallback)")
     l = ctypes.CDLL(str(LIB_PATH))
     _declare(l)
