@@ -176,6 +176,20 @@ def test_prefill_whole_prompt_half(cuda_device, dtype):
     _check(got, want, dtype)
 
 
+def test_prefill_long_sharp_softmax(cuda_device):
+    """A 1100-token prompt (18 KV tiles, the running max and V reference moving across tiles)
+    with wide activations (std 3), so the softmax is peaked and scores span a large range."""
+    got, want = _decode_case(cuda_device, b=1, hq=8, hkv=2, d=128, bits=4, t=1100, s=1100, seed=41, std=3.0)
+    _check(got, want, torch.float32)
+
+
+def test_prefill_int8_tiny_values(cuda_device):
+    """8-bit codes on small activations (std 0.05: V scales near 4e-4), where the products
+    p * scale sit far below fp16's normal range unless they are normalised."""
+    got, want = _decode_case(cuda_device, b=2, hq=8, hkv=4, d=64, bits=8, t=333, s=300, seed=42, std=0.05)
+    _check(got, want, torch.float32)
+
+
 def test_prefill_interleaved_rope_scale_16_tokens(cuda_device):
     got, want = _decode_case(cuda_device, b=3, hq=8, hkv=2, d=64, bits=4, t=40, s=16, seed=32, interleaved=True,
                              scale=0.2)

@@ -70,8 +70,17 @@ def _case(dev, *, b, hq, hkv, d, hidden, dtype, past, seed, interleaved=False, b
         assert np.all(err <= 1e-3 + np.abs(w) * ulp), f"{name}: max err {err.max():.3e}"
     q_pre = torch.from_numpy(want[:, :qc]).to(dtype).float().numpy().reshape(b, hq, 1, d)
     q_want = oracle.apply_rope(q_pre, cos, sin, np.array([past]), interleaved=interleaved).reshape(b, qc)
+    # the op rounds its f32 projection to the activation type before the rotation, like the
+    # oracle's q_pre; near a rounding boundary the two sums may round one ulp (2 * ulp * |x|)
+    # apart, and the rotation carries that into the element AND its rotary partner
+    mag = np.abs(q_pre).reshape(b, hq, d)
+    if interleaved:
+        partner = mag.reshape(b, hq, d // 2, 2)[..., ::-1].reshape(b, hq, d)
+    else:
+        partner = np.concatenate([mag[..., d // 2:], mag[..., :d // 2]], axis=-1)
+    tol = 2e-3 + 2 * ulp * (mag + partner).reshape(b, qc) + np.abs(q_want) * ulp
     err = np.abs(q - q_want)
-    assert np.all(err <= 2e-3 + np.abs(q_want) * 3 * ulp), f"q: max err {err.max():.3e}"
+    assert np.all(err <= tol), f"q: max err {err.max():.3e}, worst excess {(err - tol).max():.3e}"
 
     # cache codes: bit-exact with the encoder on the op's own k / v (past tokens: the library's append)
     kall = np.concatenate([kp.float().numpy(), k.reshape(b, 1, hkv, d)], axis=1)
