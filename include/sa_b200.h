@@ -89,6 +89,17 @@ uint64_t sa_kernel_launches(void);
  *                                       (CB must be a multiple of 4)
  *   k_meta   float [B][H][T][2]         {scale, zero_point} per K vector
  *   v_meta   float [B][H][T][2]         {scale, zero_point} per V vector
+ * With qjl_residual set, every append also stores the QJL residual of each
+ * vector (QJLResidualEncoder::encode, kv_compression.rs:365-395, of the
+ * input against PolarQuantizer::decode of its own codes, as write_kv does at
+ * :826-840), bit-exact:
+ *   k_qjl_bits / v_qjl_bits  uint8 [B][H][T][D/8]  sign bits, bit i of the
+ *                                       vector = bit i%8 of byte i/8 (1 when
+ *                                       residual i >= 0): the bytes of the
+ *                                       reference's little-endian u64 words
+ *   k_qjl_mag  / v_qjl_mag   float [B][H][T]       c_magnitude = sum|r| / D
+ * The reference never reads them back (read_k / read_v, :862-899), and
+ * neither does attention here.
  * ====================================================================== */
 typedef struct sa_kv_cache sa_kv_cache;
 
@@ -103,6 +114,7 @@ typedef struct sa_kv_cache_config {
     int32_t max_seq_len;   /* GpuKvCache::max_seq_len */
     int32_t bits;          /* KVCacheConfig::kv_quant_bits: 3, 4 or 8 */
     uint64_t seed;         /* KVCacheConfig::seed (default 0xDEADBEEFCAFE1234) */
+    int32_t qjl_residual;  /* KVCacheConfig::kv_qjl_residual: nonzero stores QJL residuals */
 } sa_kv_cache_config;
 
 /* Raw device pointers of one layer (GpuKvCache::view_at, kv_cache.rs:336-378). */
@@ -119,6 +131,10 @@ typedef struct sa_kv_layer_view {
     int32_t code_bytes;        /* CB */
     int32_t capacity;          /* T (padded capacity, tokens) */
     float wht_scale;           /* 1 / sqrt_approx(head_dim), kv_compression.rs:100 */
+    uint8_t *k_qjl_bits;       /* QJL residual sign bits, NULL unless qjl_residual */
+    uint8_t *v_qjl_bits;
+    float *k_qjl_mag;          /* QJL residual c_magnitude, NULL unless qjl_residual */
+    float *v_qjl_mag;
 } sa_kv_layer_view;
 
 /* GpuKvCache::allocate (kv_cache.rs:129-193) + CompressedKVCache::new

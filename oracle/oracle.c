@@ -231,6 +231,15 @@ void orc_qjl_encode(const float *original, const float *approx, int dim,
     *c_magnitude = dim > 0 ? msum / (float)dim : 0.0f;
 }
 
+/* QJLResidualEncoder::correction (kv_compression.rs:401-417) */
+float orc_qjl_correction(const uint64_t *a_bits, float a_c, const uint64_t *b_bits, float b_c, int dim) {
+    if (dim == 0) return 0.0f;
+    uint32_t xor_popcount = 0;
+    for (int w = 0; w < (dim + 63) / 64; w++) xor_popcount += (uint32_t)__builtin_popcountll(a_bits[w] ^ b_bits[w]);
+    float sign_inner = (float)dim - 2.0f * (float)xor_popcount;
+    return a_c * b_c * sign_inner / (float)dim;
+}
+
 /* ---- RoPE: validate_rope_caches (:71-110) + apply_rope_in_place (:177-231)
  * + rotate_rope_block (:137-160) ---------------------------------------- */
 int orc_apply_rope(float *x, int b, int h, int sq, int d,

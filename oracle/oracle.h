@@ -53,6 +53,7 @@ int orc_polar_decode(const uint8_t *codes, float scale, float zero_point,
 /* QJLResidualEncoder::encode (:365-395).  sign_bits gets ceil(dim/64) words. */
 void orc_qjl_encode(const float *original, const float *approx, int dim,
                     uint64_t *sign_bits, float *c_magnitude);
+float orc_qjl_correction(const uint64_t *a_bits, float a_c, const uint64_t *b_bits, float b_c, int dim);
 
 /* ---- attention (ops/microsoft.rs) -------------------------------------- */
 /* apply_rope_in_place (:177-231) over a (B, H, Sq, D) f32 tensor.

@@ -6,7 +6,7 @@ MatMulNBits GEMV/GEMM, behind the C ABI in include/sa_b200.h
 (libsa_b200.so).  This package is the host-side mirror of the reference's
 operator interface; all compute runs in the CUDA library.
 """
-from .kv_cache import DEFAULT_SEED, GpuKvCache, LayerView
+from .kv_cache import DEFAULT_SEED, GpuKvCache, LayerView, qjl_correction
 from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatchCtx, OpError, PackedNBitsWeight,
                   ShapeMismatch, UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend,
                   group_query_attention, matmul_nbits, matmul_nbits_packed, qkv_project_append, rms_norm, silu_mul,
@@ -18,4 +18,5 @@ __all__ = [
     "KvCacheDispatchCtx", "OpError", "ShapeMismatch", "UnsupportedOp", "dispatch_gpu_node", "finalize_kv_cache",
     "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight",
     "qkv_project_append", "rms_norm", "silu_mul", "supports_op", "LayerWeights", "decoder_layer_step",
+    "qjl_correction",
 ]

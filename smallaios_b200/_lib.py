@@ -53,6 +53,7 @@ class KvCacheConfig(ctypes.Structure):
         ("max_seq_len", ctypes.c_int32),
         ("bits", ctypes.c_int32),
         ("seed", ctypes.c_uint64),
+        ("qjl_residual", ctypes.c_int32),
     ]
 
 
@@ -70,6 +71,10 @@ class KvLayerView(ctypes.Structure):
         ("code_bytes", ctypes.c_int32),
         ("capacity", ctypes.c_int32),
         ("wht_scale", ctypes.c_float),
+        ("k_qjl_bits", ctypes.c_void_p),
+        ("v_qjl_bits", ctypes.c_void_p),
+        ("k_qjl_mag", ctypes.c_void_p),
+        ("v_qjl_mag", ctypes.c_void_p),
     ]
 
 

@@ -52,6 +52,10 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
             x[r] = rope_element(src, x[r], lane * EPL + r, d, pos, a.cos_cache, a.sin_cache, a.interleaved);
     }
 
+    float x0[EPL];  // the vector as written (after RoPE): the QJL residual is taken against it
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x0[r] = x[r];
+
     // apply_signs + butterfly + 1/sqrt_approx(n) (kv_compression.rs:81-123).
     const float *sg = a.signs + (int64_t)h * d;
 #pragma unroll
@@ -129,6 +133,44 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
         float *meta = (which == 0 ? a.k_meta : a.v_meta) + (row * a.capacity + pos) * 2;
         meta[0] = scale;
         meta[1] = zp;
+    }
+
+    // QJL residual (CompressedKVCache::write_kv, kv_compression.rs:826-840): the input minus
+    // PolarQuantizer::decode of its own codes (:270-286: q * scale + zp, butterfly, * 1/sqrt_approx(n),
+    // * sign), then QJLResidualEncoder::encode (:365-395): sign bits and sum|r| / n, the sum taken
+    // sequentially in element order.
+    uint8_t *qbits = which == 0 ? a.k_qjl_bits : a.v_qjl_bits;
+    if (qbits != nullptr) {
+        float y[EPL];
+#pragma unroll
+        for (int r = 0; r < EPL; r++)
+            y[r] = active ? __fadd_rn(__fmul_rn((float)s_codes[lane * EPL + r], scale), zp) : 0.0f;
+        warp_wht_butterfly<EPL>(y, lane, d);
+        uint32_t pos_bits[EPL];  // bit l: element l * EPL + r of the residual is >= 0
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            const float sgn = active ? sg[lane * EPL + r] : 1.0f;
+            y[r] = __fsub_rn(x0[r], __fmul_rn(__fmul_rn(y[r], a.wht_scale), sgn));
+            pos_bits[r] = __ballot_sync(0xffffffffu, active && y[r] >= 0.0f);
+        }
+        const int64_t vec = row * a.capacity + pos;
+        if (lane < d / 8) {
+            // byte `lane` holds elements 8 * lane + i, i = 0..7; EPL divides 8
+            uint32_t byte = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                byte |= ((pos_bits[i % EPL] >> (8 * lane / EPL + i / EPL)) & 1u) << i;
+            qbits[vec * (d / 8) + lane] = (uint8_t)byte;
+        }
+        float msum = 0.0f;
+        for (int l = 0; l < d / EPL; l++) {
+            if (lane == l) {
+#pragma unroll
+                for (int r = 0; r < EPL; r++) msum = __fadd_rn(msum, fabsf(y[r]));
+            }
+            msum = __shfl_sync(0xffffffffu, msum, l);
+        }
+        if (lane == 0) (which == 0 ? a.k_qjl_mag : a.v_qjl_mag)[vec] = __fdiv_rn(msum, (float)d);
     }
     __syncwarp();
 }

@@ -57,6 +57,12 @@ struct kv_cache_impl {
     GatherOut gather;  // head-sharded output buffers (n = 0: off)
     size_t layer_codes_bytes;  // B*H*T*CB
     size_t layer_meta_floats;  // B*H*T*2
+    uint8_t *k_qjl_bits;       // [L][B][H][T][D/8], nullptr unless cfg.qjl_residual
+    uint8_t *v_qjl_bits;
+    float *k_qjl_mag;          // [L][B][H][T]
+    float *v_qjl_mag;
+    size_t layer_qjl_bytes;    // B*H*T*D/8
+    size_t layer_qjl_floats;   // B*H*T
 };
 
 // Parameters of one append launch (K and V of `batch * seq_len` tokens).
@@ -72,6 +78,9 @@ struct AppendArgs {
     float wht_scale;
     const float *cos_cache, *sin_cache;
     int cache_rows, do_rotary, interleaved;
+    // QJL residuals of the appended vectors (all nullptr: not stored)
+    uint8_t *k_qjl_bits, *v_qjl_bits;
+    float *k_qjl_mag, *v_qjl_mag;
 };
 
 // Parameters of the fused QKV projection's epilogue (one token per row):

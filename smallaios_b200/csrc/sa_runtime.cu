@@ -156,7 +156,12 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     const size_t ws = up(k->workspace_floats * sizeof(float));
     const size_t qp = up(B * H * decode_qprep_words(k->group) * sizeof(uint32_t));
     const size_t st = 256;
-    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st;
+    // QJL residuals (KVCacheConfig::kv_qjl_residual): D/8 sign bytes and one magnitude per vector
+    k->layer_qjl_bytes = c.qjl_residual ? B * H * T * (D / 8) : 0;
+    k->layer_qjl_floats = c.qjl_residual ? B * H * T : 0;
+    const size_t qjl_bits = up(L * k->layer_qjl_bytes);
+    const size_t qjl_mag = up(L * k->layer_qjl_floats * sizeof(float));
+    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st + 2 * qjl_bits + 2 * qjl_mag;
     const size_t k_bytes = k->base_bytes;
     cudaError_t e = cudaMalloc(&k->base, k->base_bytes);
     if (e != cudaSuccess) {
@@ -181,6 +186,16 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->qprep = reinterpret_cast<uint32_t *>(p);
     p += qp;
     k->dev_status = reinterpret_cast<int *>(p);
+    p += st;
+    if (c.qjl_residual) {
+        k->k_qjl_bits = p;
+        p += qjl_bits;
+        k->v_qjl_bits = p;
+        p += qjl_bits;
+        k->k_qjl_mag = reinterpret_cast<float *>(p);
+        p += qjl_mag;
+        k->v_qjl_mag = reinterpret_cast<float *>(p);
+    }
     // Zero-initialise like GpuKvCache::allocate (kv_cache.rs:171-175).
     e = cudaMemset(k->base, 0, k->base_bytes);
     if (e == cudaSuccess) {
@@ -311,6 +326,11 @@ int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_
     v->code_bytes = k->code_bytes;
     v->capacity = k->capacity;
     v->wht_scale = k->wht_scale;
+    const bool qjl = k->k_qjl_bits != nullptr;
+    v->k_qjl_bits = qjl ? k->k_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
+    v->v_qjl_bits = qjl ? k->v_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
+    v->k_qjl_mag = qjl ? k->k_qjl_mag + (size_t)layer * k->layer_qjl_floats : nullptr;
+    v->v_qjl_mag = qjl ? k->v_qjl_mag + (size_t)layer * k->layer_qjl_floats : nullptr;
     return SA_OK;
 }
 
@@ -368,6 +388,10 @@ int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void 
     a.v_codes = v.v_codes;
     a.k_meta = v.k_meta;
     a.v_meta = v.v_meta;
+    a.k_qjl_bits = v.k_qjl_bits;
+    a.v_qjl_bits = v.v_qjl_bits;
+    a.k_qjl_mag = v.k_qjl_mag;
+    a.v_qjl_mag = v.v_qjl_mag;
     a.signs = v.signs;
     a.wht_scale = v.wht_scale;
     a.cos_cache = cos_cache;
@@ -452,6 +476,10 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         ap.v_codes = v.v_codes;
         ap.k_meta = v.k_meta;
         ap.v_meta = v.v_meta;
+        ap.k_qjl_bits = v.k_qjl_bits;
+        ap.v_qjl_bits = v.v_qjl_bits;
+        ap.k_qjl_mag = v.k_qjl_mag;
+        ap.v_qjl_mag = v.v_qjl_mag;
         ap.signs = v.signs;
         ap.wht_scale = v.wht_scale;
         ap.cos_cache = cos_cache;
@@ -619,6 +647,10 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
     ap.v_codes = v.v_codes;
     ap.k_meta = v.k_meta;
     ap.v_meta = v.v_meta;
+    ap.k_qjl_bits = v.k_qjl_bits;
+    ap.v_qjl_bits = v.v_qjl_bits;
+    ap.k_qjl_mag = v.k_qjl_mag;
+    ap.v_qjl_mag = v.v_qjl_mag;
     ap.signs = v.signs;
     ap.wht_scale = v.wht_scale;
     ap.cos_cache = cos_cache;

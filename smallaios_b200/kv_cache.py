@@ -45,6 +45,11 @@ class LayerView:
     bits: int
     code_bytes: int
     capacity: int
+    # QJL residuals (KVCacheConfig::kv_qjl_residual), None unless the cache stores them
+    k_qjl_bits: torch.Tensor | None = None  # uint8 (B, H, T, D/8): bit i of a vector = bit i%8 of byte i/8
+    v_qjl_bits: torch.Tensor | None = None
+    k_qjl_mag: torch.Tensor | None = None   # f32 (B, H, T): c_magnitude
+    v_qjl_mag: torch.Tensor | None = None
 
     def v_codes_tokens(self) -> torch.Tensor:
         """V codes in per-token pack_bits order (B, H, T, CB).
@@ -58,6 +63,26 @@ class LayerView:
         return self.v_codes.permute(0, 1, 2, 4, 6, 3, 5).reshape(b, h, nblk * g * tt, c4 * jj)
 
 
+def qjl_correction(bits_a, mag_a, bits_b, mag_b, dim: int):
+    """QJLResidualEncoder::correction (kv_compression.rs:401-417) of stored residual pairs, on the host.
+
+    ``bits_*``: uint8 sign bytes (..., dim/8) as the cache stores them (LayerView.k_qjl_bits);
+    ``mag_*``: their c_magnitude (...).  Returns C_a * C_b * (dim - 2 popcount(a ^ b)) / dim in
+    f32, in the reference's operation order.  The reference computes the term but never applies
+    it on read; this is the same helper for callers that want it.
+    """
+    import numpy as np
+
+    to_np = (lambda t: t.cpu().numpy() if isinstance(t, torch.Tensor) else np.asarray(t))
+    a, b = to_np(bits_a).astype(np.uint8), to_np(bits_b).astype(np.uint8)
+    ma, mb = to_np(mag_a).astype(np.float32), to_np(mag_b).astype(np.float32)
+    if dim == 0:
+        return np.zeros(np.broadcast_shapes(ma.shape, mb.shape), np.float32)
+    pop = np.unpackbits(np.bitwise_xor(a, b), axis=-1).sum(axis=-1, dtype=np.int64)
+    sign_inner = np.float32(dim) - np.float32(2.0) * pop.astype(np.float32)
+    return (ma * mb * sign_inner / np.float32(dim)).astype(np.float32)
+
+
 class GpuKvCache:
     """Per-layer compressed K/V cache for a batch of sequences on one GPU.
 
@@ -65,12 +90,15 @@ class GpuKvCache:
     reset`` (kv_cache.rs).  ``kv_head_begin/kv_head_count`` select a shard of
     the KV heads (KV-head sharding across GPUs); the PolarQuant seed of each
     head still uses its global index, so a sharded cache holds exactly the
-    codes the unsharded one would.
+    codes the unsharded one would.  ``qjl_residual`` (KVCacheConfig::
+    kv_qjl_residual) makes every append also store the QJL residual of each
+    vector; nothing reads it back, as in the reference, so it is off by default.
     """
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_seq_len: int, *,
                  batch: int = 1, num_heads: int | None = None, bits: int = 4, seed: int = DEFAULT_SEED,
-                 kv_head_begin: int = 0, kv_head_count: int | None = None, device=None):
+                 kv_head_begin: int = 0, kv_head_count: int | None = None, qjl_residual: bool = False,
+                 device=None):
         self.device = torch.device(device if device is not None else "cuda", )
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
@@ -85,6 +113,7 @@ class GpuKvCache:
         cfg.max_seq_len = max_seq_len
         cfg.bits = bits
         cfg.seed = seed & (2**64 - 1)
+        cfg.qjl_residual = 1 if qjl_residual else 0
         self._handle = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             check(lib.sa_kv_cache_create(ctypes.byref(cfg), ctypes.byref(self._handle)))
@@ -147,7 +176,12 @@ class GpuKvCache:
             k_meta=_view(v.k_meta, (B, H, T, 2), "<f4", dev),
             v_meta=_view(v.v_meta, (B, H, T, 2), "<f4", dev),
             signs=_view(v.signs, (H, D), "<f4", dev),
-            wht_scale=v.wht_scale, bits=v.bits, code_bytes=CB, capacity=T)
+            wht_scale=v.wht_scale, bits=v.bits, code_bytes=CB, capacity=T,
+            **({} if not v.k_qjl_bits else dict(
+                k_qjl_bits=_view(v.k_qjl_bits, (B, H, T, D // 8), "|u1", dev),
+                v_qjl_bits=_view(v.v_qjl_bits, (B, H, T, D // 8), "|u1", dev),
+                k_qjl_mag=_view(v.k_qjl_mag, (B, H, T), "<f4", dev),
+                v_qjl_mag=_view(v.v_qjl_mag, (B, H, T), "<f4", dev))))
 
     def close(self) -> None:
         if self._handle:

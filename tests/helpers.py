@@ -42,6 +42,36 @@ def oracle_append(k_bshd: np.ndarray, v_bshd: np.ndarray, signs_hd: np.ndarray, 
     return kc, km, vc, vm
 
 
+def oracle_qjl(k_bshd: np.ndarray, v_bshd: np.ndarray, signs_hd: np.ndarray, bits: int, pos0: int,
+               cos=None, sin=None, do_rotary=False, interleaved=False):
+    """Reference QJL residuals of an append (CompressedKVCache::write_kv, kv_compression.rs:826-840):
+    QJLResidualEncoder::encode(x, PolarQuantizer::decode(encode(x))) per vector, x = RoPE(k) or v.
+
+    Returns k_bits, k_mag, v_bits, v_mag shaped (B, H, S, D/8) and (B, H, S); the bit bytes are
+    the little-endian bytes of the reference's u64 sign words.
+    """
+    b, s, h, d = k_bshd.shape
+    kc, km, vc, vm = oracle_append(k_bshd, v_bshd, signs_hd, bits, pos0, cos, sin, do_rotary, interleaved)
+    k = np.ascontiguousarray(np.transpose(k_bshd, (0, 2, 1, 3)), np.float32)
+    v = np.ascontiguousarray(np.transpose(v_bshd, (0, 2, 1, 3)), np.float32)
+    if do_rotary:
+        k = oracle.apply_rope(k, cos, sin, np.arange(pos0, pos0 + s), interleaved=interleaved)
+    out = []
+    for x, codes, meta in ((k, kc, km), (v, vc, vm)):
+        qbits = np.zeros((b, h, s, d // 8), np.uint8)
+        qmag = np.zeros((b, h, s), np.float32)
+        for bi in range(b):
+            for hi in range(h):
+                for si in range(s):
+                    approx = oracle.polar_decode(codes[bi, hi, si], meta[bi, hi, si, 0], meta[bi, hi, si, 1], d,
+                                                 bits, signs_hd[hi])
+                    words, c = oracle.qjl_encode(x[bi, hi, si], approx)
+                    qbits[bi, hi, si] = words.view(np.uint8)[:d // 8]
+                    qmag[bi, hi, si] = c
+        out += [qbits, qmag]
+    return tuple(out)
+
+
 def oracle_attend(q_bshd: np.ndarray, kc, km, vc, vm, signs_hd, bits, pos0, scale=None, cos=None, sin=None,
                   do_rotary=False, interleaved=False):
     """Composite oracle: RoPE q at positions pos0.., read_k/read_v, causal SDPA.

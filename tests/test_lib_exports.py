@@ -92,3 +92,31 @@ def test_product_package_does_not_import_oracle():
     for p in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):
         text = p.read_text(errors="ignore")
         assert "import oracle" not in text and "from oracle" not in text and "liboracle" not in text, p
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """The ctypes mirrors of sa_kv_cache_config / sa_kv_layer_view have the C layout
+    (sizes and field offsets from a C compiler on include/sa_b200.h)."""
+    import subprocess
+
+    from smallaios_b200 import _lib
+
+    structs = {"sa_kv_cache_config": _lib.KvCacheConfig, "sa_kv_layer_view": _lib.KvLayerView}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "sa_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'    printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'    printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["    return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.check_call(["gcc", "-std=c11", "-I", str(ROOT / "include"), str(src), "-o", str(exe)])
+    got = {}
+    for line in subprocess.check_output([str(exe)], text=True).splitlines():
+        s, f, v = line.split()
+        got[(s, f)] = int(v)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, f"{cname}.{f}"
