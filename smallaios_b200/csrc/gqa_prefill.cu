@@ -34,6 +34,7 @@ namespace {
 constexpr int kPfWarps = 8;
 constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
 constexpr int kPfTok = 64;              // tokens per KV tile
+constexpr int kPfSub = 32;              // tokens per softmax step within a tile
 
 template <int D>
 struct PfGeo {
@@ -48,7 +49,8 @@ struct PfGeo {
     static constexpr int V_OFF = K_OFF + K_BYTES;
     static constexpr int META_OFF = V_OFF + V_BYTES;
     static constexpr int QSUM_OFF = META_OFF + META_BYTES;
-    static constexpr int O_BYTES = kPfRows * D * 4;  // f32 staging of O' (reuses the q' planes)
+    static constexpr int OS = D + 8;                  // f32 per staged O' row (rows g, g+8 on distinct banks)
+    static constexpr int O_BYTES = kPfRows * OS * 4;  // f32 staging of O' (reuses the q' planes)
     static constexpr int SMEM = QSUM_OFF + QSUM_BYTES;
     static_assert(O_BYTES <= K_OFF, "O' staging overlaps the code tiles");
     static constexpr int NKS = D / 16;  // k-steps of Q'.C^T
@@ -80,7 +82,7 @@ __device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
-// grid = (ceil(seq_len * G / 128), kv heads, batch), 256 threads.
+// grid = ceil(seq_len * G / 128) * kv heads * batch blocks (1-D), 256 threads.
 template <typename T, int BITS, int D>
 __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(AttendArgs a) {
     using GG = PfGeo<D>;
@@ -96,8 +98,13 @@ __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(Attend
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int G = a.group, h = blockIdx.y, b = blockIdx.z;
-    const int r0 = blockIdx.x * kPfRows;  // first query row (row = position * G + head)
+    // one block per (row block, KV head, batch row), row blocks slowest and in reverse: the last
+    // row blocks walk the most tiles, so they take the lowest block indices and start first
+    const int units = a.heads * a.batch;
+    const int rblocks = (int)(gridDim.x / (unsigned)units);
+    const int h = (int)(blockIdx.x % (unsigned)a.heads), b = (int)(blockIdx.x / (unsigned)a.heads) % a.batch;
+    const int G = a.group;
+    const int r0 = (rblocks - 1 - (int)(blockIdx.x / (unsigned)units)) * kPfRows;  // row = position * G + head
     const int nrows = a.seq_len * G;
     const int64_t unit = (int64_t)b * a.heads + h;
     const float *sg = a.signs + (int64_t)h * D;
@@ -170,6 +177,7 @@ __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(Attend
     const int last_row = min(r0 + kPfRows, nrows) - 1;
     const int pos_last = (int)a.pos0 + last_row / G;  // the CTA's largest position
     const int ntiles = pos_last / kPfTok + 1;
+    const int pos_wmax = (int)a.pos0 + (min(r0 + warp * 16 + 15, nrows - 1)) / G;  // this warp's largest position
 
     float oacc[GG::NTO][4];
 #pragma unroll
@@ -256,96 +264,115 @@ __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(Attend
         }
         __syncthreads();
 
-        // ---- S = (Q'hi + Q'lo).C^T: rows warp*16 + (g, g+8), tokens 8j + (2t, 2t+1) ----
-        float sacc[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; j++) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
-        const __half *qh = qhs + (warp * 16 + g) * GG::QS;
-        const __half *ql = qls + (warp * 16 + g) * GG::QS;
-#pragma unroll
-        for (int kk = 0; kk < GG::NKS; kk++) {
-            const int c0 = 16 * kk + 2 * t;
-            const uint32_t a0 = *reinterpret_cast<const uint32_t *>(qh + c0);
-            const uint32_t a1 = *reinterpret_cast<const uint32_t *>(qh + 8 * GG::QS + c0);
-            const uint32_t a2 = *reinterpret_cast<const uint32_t *>(qh + c0 + 8);
-            const uint32_t a3 = *reinterpret_cast<const uint32_t *>(qh + 8 * GG::QS + c0 + 8);
-            const uint32_t e0 = *reinterpret_cast<const uint32_t *>(ql + c0);
-            const uint32_t e1 = *reinterpret_cast<const uint32_t *>(ql + 8 * GG::QS + c0);
-            const uint32_t e2 = *reinterpret_cast<const uint32_t *>(ql + c0 + 8);
-            const uint32_t e3 = *reinterpret_cast<const uint32_t *>(ql + 8 * GG::QS + c0 + 8);
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const __half *krow = ks + (8 * j + g) * GG::QS + c0;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(krow);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(krow + 8);
-                mma_f16(sacc[j], a0, a1, a2, a3, b0, b1);
-                mma_f16(sacc[j], e0, e1, e2, e3, b0, b1);
-            }
-        }
-        // ---- scale / zero point per token, causal mask, running max ----
-        float mx[2] = {m_r[0], m_r[1]};
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-#pragma unroll
-            for (int ee = 0; ee < 2; ee++) {
-                const int tok = 8 * j + 2 * t + ee;
-                const float2 km = *reinterpret_cast<const float2 *>(&meta[tok]);
-#pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    float s = fmaf(sacc[j][2 * hf + ee], km.x, km.y * qs_r[hf]);
-                    if (t0 + tok > pos_r[hf]) s = -INFINITY;
-                    sacc[j][2 * hf + ee] = s;
-                    mx[hf] = fmaxf(mx[hf], s);
-                }
-            }
         // the tile's largest V scale (metadata of masked tokens is zero)
         float vmax = fmaxf(meta[lane].z, meta[lane + 32].z);
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, m));
         const float lvmax = __log2f(fmaxf(vmax, 1.17549435e-38f));
-        float kr[2];
+
+        // two halves of 32 tokens (fewer live score registers); a half past every row of this
+        // warp is skipped
+#pragma unroll 1
+        for (int th = 0; th < kPfTok; th += kPfSub) {
+            if (t0 + th > pos_wmax) break;
+            // ---- S = (Q'hi + Q'lo).C^T: rows warp*16 + (g, g+8), tokens th + 8j + (2t, 2t+1) ----
+            float sacc[kPfSub / 8][4];
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 1));
-            mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 2));
-            const float fac = exp2f(m_r[hf] - mx[hf]);  // 0 on the first tile (m = -inf)
-            l_r[hf] *= fac;
-            z_r[hf] *= fac;
-            m_r[hf] = mx[hf];
-            const float rn = fmaxf(R_r[hf], mx[hf] + lvmax);
-            const float ofac = exp2f(R_r[hf] - rn);
-            R_r[hf] = rn;
-            kr[hf] = exp2f(mx[hf] - rn);  // p * vscale * kr <= 1
+            for (int j = 0; j < kPfSub / 8; j++) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
+            const __half *qh = qhs + (warp * 16 + g) * GG::QS;
+            const __half *ql = qls + (warp * 16 + g) * GG::QS;
 #pragma unroll
-            for (int n = 0; n < GG::NTO; n++) {
-                oacc[n][2 * hf] *= ofac;
-                oacc[n][2 * hf + 1] *= ofac;
+            for (int kk = 0; kk < GG::NKS; kk++) {
+                const int c0 = 16 * kk + 2 * t;
+                const uint32_t a0 = *reinterpret_cast<const uint32_t *>(qh + c0);
+                const uint32_t a1 = *reinterpret_cast<const uint32_t *>(qh + 8 * GG::QS + c0);
+                const uint32_t a2 = *reinterpret_cast<const uint32_t *>(qh + c0 + 8);
+                const uint32_t a3 = *reinterpret_cast<const uint32_t *>(qh + 8 * GG::QS + c0 + 8);
+                const uint32_t e0 = *reinterpret_cast<const uint32_t *>(ql + c0);
+                const uint32_t e1 = *reinterpret_cast<const uint32_t *>(ql + 8 * GG::QS + c0);
+                const uint32_t e2 = *reinterpret_cast<const uint32_t *>(ql + c0 + 8);
+                const uint32_t e3 = *reinterpret_cast<const uint32_t *>(ql + 8 * GG::QS + c0 + 8);
+                uint32_t bk[kPfSub / 8][2];
+#pragma unroll
+                for (int j = 0; j < kPfSub / 8; j++) {
+                    const __half *krow = ks + (th + 8 * j + g) * GG::QS + c0;
+                    bk[j][0] = *reinterpret_cast<const uint32_t *>(krow);
+                    bk[j][1] = *reinterpret_cast<const uint32_t *>(krow + 8);
+                }
+                // all hi products, then all lo products: no MMA waits on the one before it
+#pragma unroll
+                for (int j = 0; j < kPfSub / 8; j++) mma_f16(sacc[j], a0, a1, a2, a3, bk[j][0], bk[j][1]);
+#pragma unroll
+                for (int j = 0; j < kPfSub / 8; j++) mma_f16(sacc[j], e0, e1, e2, e3, bk[j][0], bk[j][1]);
             }
-        }
-        // ---- P, U = P * vscale * kr as hi + lo fp16, O'_u += U.C ----
+            // ---- scale / zero point per token, causal mask, running max ----
+            float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-        for (int kk = 0; kk < kPfTok / 16; kk++) {
-            uint32_t ah[4], al[4];  // A fragments: (row g, j = 2kk), (row g+8, 2kk), (g, 2kk+1), (g+8, 2kk+1)
+            for (int j = 0; j < kPfSub / 8; j++)
 #pragma unroll
-            for (int jj = 0; jj < 2; jj++) {
-                const int j = 2 * kk + jj;
-                const float4 m0 = meta[8 * j + 2 * t], m1 = meta[8 * j + 2 * t + 1];
+                for (int ee = 0; ee < 2; ee++) {
+                    const int tok = th + 8 * j + 2 * t + ee;
+                    const float2 km = *reinterpret_cast<const float2 *>(&meta[tok]);
 #pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    const float p0 = exp2f(sacc[j][2 * hf] - m_r[hf]);
-                    const float p1 = exp2f(sacc[j][2 * hf + 1] - m_r[hf]);
-                    l_r[hf] += p0 + p1;
-                    z_r[hf] = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r[hf]));
-                    split_h2(p0 * m0.z * kr[hf], p1 * m1.z * kr[hf], ah[2 * jj + hf], al[2 * jj + hf]);
+                    for (int hf = 0; hf < 2; hf++) {
+                        float s = fmaf(sacc[j][2 * hf + ee], km.x, km.y * qs_r[hf]);
+                        if (t0 + tok > pos_r[hf]) s = -INFINITY;
+                        sacc[j][2 * hf + ee] = s;
+                        mx[hf] = fmaxf(mx[hf], s);
+                    }
+                }
+            float kr[2];
+#pragma unroll
+            for (int hf = 0; hf < 2; hf++) {
+                mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 1));
+                mx[hf] = fmaxf(mx[hf], __shfl_xor_sync(0xffffffffu, mx[hf], 2));
+                const float fac = exp2f(m_r[hf] - mx[hf]);  // 0 on the first half-tile (m = -inf)
+                l_r[hf] *= fac;
+                z_r[hf] *= fac;
+                m_r[hf] = mx[hf];
+                const float rn = fmaxf(R_r[hf], mx[hf] + lvmax);
+                const float ofac = exp2f(R_r[hf] - rn);
+                R_r[hf] = rn;
+                kr[hf] = exp2f(mx[hf] - rn);  // p * vscale * kr <= 1
+#pragma unroll
+                for (int n = 0; n < GG::NTO; n++) {
+                    oacc[n][2 * hf] *= ofac;
+                    oacc[n][2 * hf + 1] *= ofac;
                 }
             }
+            // ---- P, U = P * vscale * kr as hi + lo fp16, O'_u += U.C ----
 #pragma unroll
-            for (int n = 0; n < GG::NTO; n++) {
-                const __half *vrow = vt + (8 * n + g) * GG::VS + 16 * kk + 2 * t;
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vrow);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(vrow + 8);
-                mma_f16(oacc[n], ah[0], ah[1], ah[2], ah[3], b0, b1);
-                mma_f16(oacc[n], al[0], al[1], al[2], al[3], b0, b1);
+            for (int kk = 0; kk < kPfSub / 16; kk++) {
+                uint32_t ah[4], al[4];  // A fragments: (row g, j = 2kk), (row g+8, 2kk), (g, 2kk+1), (g+8, 2kk+1)
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const int j = 2 * kk + jj;
+                    const float2 m0 = *reinterpret_cast<const float2 *>(&meta[th + 8 * j + 2 * t].z);
+                    const float2 m1 = *reinterpret_cast<const float2 *>(&meta[th + 8 * j + 2 * t + 1].z);
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        const float p0 = exp2f(sacc[j][2 * hf] - m_r[hf]);
+                        const float p1 = exp2f(sacc[j][2 * hf + 1] - m_r[hf]);
+                        l_r[hf] += p0 + p1;
+                        z_r[hf] = fmaf(p0, m0.y, fmaf(p1, m1.y, z_r[hf]));
+                        split_h2(p0 * m0.x * kr[hf], p1 * m1.x * kr[hf], ah[2 * jj + hf], al[2 * jj + hf]);
+                    }
+                }
+                // groups of 4 n-tiles: hi products, then lo products
+#pragma unroll
+                for (int n0 = 0; n0 < GG::NTO; n0 += 4) {
+                    uint32_t bv[4][2];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const __half *vrow = vt + (8 * (n0 + i) + g) * GG::VS + th + 16 * kk + 2 * t;
+                        bv[i][0] = *reinterpret_cast<const uint32_t *>(vrow);
+                        bv[i][1] = *reinterpret_cast<const uint32_t *>(vrow + 8);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; i++) mma_f16(oacc[n0 + i], ah[0], ah[1], ah[2], ah[3], bv[i][0], bv[i][1]);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) mma_f16(oacc[n0 + i], al[0], al[1], al[2], al[3], bv[i][0], bv[i][1]);
+                }
             }
         }
     }
@@ -360,15 +387,15 @@ __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(Attend
         }
     }
     __syncthreads();  // the tiles and q' planes are no longer read
-    float *os = reinterpret_cast<float *>(smem) + warp * 16 * D;
+    float *os = reinterpret_cast<float *>(smem) + warp * 16 * GG::OS;
 #pragma unroll
     for (int hf = 0; hf < 2; hf++) {
         const float inv = l_r[hf] > 0.0f ? 1.0f / l_r[hf] : 0.0f;
         const float cu = exp2f(R_r[hf] - m_r[hf]) * inv, cz = z_r[hf] * inv;
 #pragma unroll
         for (int n = 0; n < GG::NTO; n++) {
-            os[(g + 8 * hf) * D + 8 * n + 2 * t] = fmaf(oacc[n][2 * hf], cu, cz);
-            os[(g + 8 * hf) * D + 8 * n + 2 * t + 1] = fmaf(oacc[n][2 * hf + 1], cu, cz);
+            *reinterpret_cast<float2 *>(&os[(g + 8 * hf) * GG::OS + 8 * n + 2 * t]) =
+                make_float2(fmaf(oacc[n][2 * hf], cu, cz), fmaf(oacc[n][2 * hf + 1], cu, cz));
         }
     }
     __syncwarp();
@@ -377,7 +404,7 @@ __global__ void __launch_bounds__(32 * kPfWarps, 2) prefill_attend_kernel(Attend
         if (gr >= nrows) break;
         float x[EPL];
 #pragma unroll
-        for (int r = 0; r < EPL; r++) x[r] = os[i * D + lane * EPL + r];
+        for (int r = 0; r < EPL; r++) x[r] = os[i * GG::OS + lane * EPL + r];
         warp_wht_butterfly<EPL>(x, lane, D);
         const int s = gr / G, hd = gr % G;
         T *dst = static_cast<T *>(a.out) + (((int64_t)b * a.seq_len + s) * (a.heads * G) + h * G + hd) * D;
@@ -400,7 +427,9 @@ int launch_shape(const AttendArgs &a, cudaStream_t stream) {
         if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
     }
     const int rows = a.seq_len * a.group;
-    const dim3 grid((unsigned)((rows + kPfRows - 1) / kPfRows), (unsigned)a.heads, (unsigned)a.batch);
+    const int64_t nblocks = (int64_t)((rows + kPfRows - 1) / kPfRows) * a.heads * a.batch;
+    if (nblocks > 0x7fffffff) return set_error(SA_ERR_UNSUPPORTED, "gqa prefill: %lld blocks", (long long)nblocks);
+    const dim3 grid((unsigned)nblocks);
     kern<<<grid, 32 * kPfWarps, GG::SMEM, stream>>>(a);
     count_launch();
     return check_cuda(cudaGetLastError(), "gqa prefill launch");
