@@ -100,6 +100,18 @@ uint64_t sa_kernel_launches(void);
  *   k_qjl_mag  / v_qjl_mag   float [B][H][T]       c_magnitude = sum|r| / D
  * The reference never reads them back (read_k / read_v, :862-899), and
  * neither does attention here.
+ * With lowrank_k > 0 (KVCacheConfig::kv_lowrank_k) the cache also keeps the
+ * low-rank K state of LowRankKeyDecomposer (:451-671), bit-exact, as
+ * write_kv builds it (:842-853): the first K row of a sequence is decomposed
+ * alone, so the rank is min(lowrank_k, 1, D) = 1 from then on; every later
+ * row appends its projection, and every 512th update re-decomposes the
+ * reconstruction by power iteration:
+ *   lr_vt  float [B][H][D]   the rank-1 V^T row
+ *   lr_us  float [B][H][T]   U*S, one coefficient per written row
+ * read_k then returns the reconstruction lr_us[t] * lr_vt (:862-886), so
+ * attention on such a cache scores keys as lr_us[t] * (q . lr_vt); V still
+ * comes from the PolarQuant codes.  The state follows writes in position
+ * order from 0; rewinding below a re-decomposition point is not supported.
  * ====================================================================== */
 typedef struct sa_kv_cache sa_kv_cache;
 
@@ -115,6 +127,7 @@ typedef struct sa_kv_cache_config {
     int32_t bits;          /* KVCacheConfig::kv_quant_bits: 3, 4 or 8 */
     uint64_t seed;         /* KVCacheConfig::seed (default 0xDEADBEEFCAFE1234) */
     int32_t qjl_residual;  /* KVCacheConfig::kv_qjl_residual: nonzero stores QJL residuals */
+    int32_t lowrank_k;     /* KVCacheConfig::kv_lowrank_k: 0 = None, > 0 keeps low-rank K */
 } sa_kv_cache_config;
 
 /* Raw device pointers of one layer (GpuKvCache::view_at, kv_cache.rs:336-378). */
@@ -135,6 +148,8 @@ typedef struct sa_kv_layer_view {
     uint8_t *v_qjl_bits;
     float *k_qjl_mag;          /* QJL residual c_magnitude, NULL unless qjl_residual */
     float *v_qjl_mag;
+    float *lr_vt;              /* low-rank K state, NULL unless lowrank_k (attention then uses it) */
+    float *lr_us;
 } sa_kv_layer_view;
 
 /* GpuKvCache::allocate (kv_cache.rs:129-193) + CompressedKVCache::new

@@ -240,6 +240,125 @@ float orc_qjl_correction(const uint64_t *a_bits, float a_c, const uint64_t *b_bi
     return a_c * b_c * sign_inner / (float)dim;
 }
 
+/* ---- Low-rank K (LowRankKeyDecomposer, kv_compression.rs:451-690) ------ */
+
+/* norm_vec (:674-681) */
+static float lr_norm_vec(const float *v, size_t n) {
+    float s = 0.0f;
+    for (size_t i = 0; i < n; i++) s += v[i] * v[i];
+    return orc_sqrt_approx(s);
+}
+
+/* normalize_vec (:683-690) */
+static void lr_normalize_vec(float *v, size_t n) {
+    float nn = lr_norm_vec(v, n);
+    if (nn > 1e-30f)
+        for (size_t i = 0; i < n; i++) v[i] /= nn;
+}
+
+/* power_iteration_svd (:583-671): u_s [m][rank], vt [rank][n], zero where the loop stops early */
+static void lr_power_iteration_svd(const float *matrix, size_t m, size_t n, size_t rank, float *u_s, float *vt) {
+    memset(u_s, 0, sizeof(float) * m * rank);
+    memset(vt, 0, sizeof(float) * rank * n);
+    float *deflated = (float *)malloc(sizeof(float) * (m * n > 0 ? m * n : 1));
+    float *v = (float *)malloc(sizeof(float) * (n > 0 ? n : 1));
+    float *u = (float *)malloc(sizeof(float) * (m > 0 ? m : 1));
+    memcpy(deflated, matrix, sizeof(float) * m * n);
+    for (size_t r = 0; r < rank; r++) {
+        for (size_t j = 0; j < n; j++) v[j] = ((j + r) % 2 == 0) ? 1.0f : -1.0f;
+        lr_normalize_vec(v, n);
+        for (int it = 0; it < 10; it++) {
+            for (size_t i = 0; i < m; i++) {
+                float dot = 0.0f;
+                for (size_t j = 0; j < n; j++) dot += deflated[i * n + j] * v[j];
+                u[i] = dot;
+            }
+            for (size_t j = 0; j < n; j++) v[j] = 0.0f;
+            for (size_t i = 0; i < m; i++)
+                for (size_t j = 0; j < n; j++) v[j] += deflated[i * n + j] * u[i];
+            lr_normalize_vec(v, n);
+        }
+        for (size_t i = 0; i < m; i++) {
+            float dot = 0.0f;
+            for (size_t j = 0; j < n; j++) dot += deflated[i * n + j] * v[j];
+            u[i] = dot;
+        }
+        float sigma = lr_norm_vec(u, m);
+        if (sigma < 1e-12f) break;
+        for (size_t i = 0; i < m; i++) u[i] /= sigma;
+        for (size_t i = 0; i < m; i++) u_s[i * rank + r] = u[i] * sigma;
+        for (size_t j = 0; j < n; j++) vt[r * n + j] = v[j];
+        for (size_t i = 0; i < m; i++)
+            for (size_t j = 0; j < n; j++) deflated[i * n + j] -= sigma * u[i] * v[j];
+    }
+    free(deflated);
+    free(v);
+    free(u);
+}
+
+/* LowRankKeyDecomposer::new (:460-465) + decompose (:470-499).  u_s holds rows * min(rank, rows, cols),
+ * vt min(rank, rows, cols) * cols; returns that actual rank. */
+int orc_lowrank_decompose(const float *k, int rows, int cols, int rank, float *u_s, float *vt) {
+    if (rank == 0) rank = 1;
+    if (rows == 0 || cols == 0) return rank;
+    int actual = rank < rows ? rank : rows;
+    if (cols < actual) actual = cols;
+    lr_power_iteration_svd(k, (size_t)rows, (size_t)cols, (size_t)actual, u_s, vt);
+    return actual;
+}
+
+/* LowRankKeyDecomposer::reconstruct (:502-526) */
+void orc_lowrank_reconstruct(const float *u_s, const float *vt, int rows, int cols, int rank, float *out) {
+    for (size_t i = 0; i < (size_t)rows * (size_t)cols; i++) out[i] = 0.0f;
+    if (rows == 0 || cols == 0 || rank == 0) return;
+    for (int i = 0; i < rows; i++)
+        for (int j = 0; j < cols; j++) {
+            float sum = 0.0f;
+            for (int r = 0; r < rank; r++) sum += u_s[(size_t)i * rank + r] * vt[(size_t)r * cols + j];
+            out[(size_t)i * cols + j] = sum;
+        }
+}
+
+/* LowRankKeyDecomposer::update (:529-562) + reorthogonalize (:564-579) on a state whose u_s has room
+ * for rows + 1 rows.  *rows, *write_counter and *rank are updated in place. */
+void orc_lowrank_update(float *u_s, float *vt, int *rows, int cols, int *rank, int *write_counter,
+                        const float *new_row) {
+    int rk = *rank;
+    if (rk == 0 || cols == 0) {
+        *rows += 1;
+        return;
+    }
+    for (int r = 0; r < rk; r++) {
+        float dot = 0.0f;
+        for (int c = 0; c < cols; c++) dot += new_row[c] * vt[(size_t)r * cols + c];
+        u_s[(size_t)(*rows) * rk + r] = dot;
+    }
+    *rows += 1;
+    *write_counter += 1;
+    if (*write_counter % 512 == 0 && *rows > rk) {
+        int m = *rows;
+        float *rec = (float *)malloc(sizeof(float) * (size_t)m * cols);
+        orc_lowrank_reconstruct(u_s, vt, m, cols, rk, rec);
+        int nr = rk < m ? rk : m;
+        if (cols < nr) nr = cols;
+        lr_power_iteration_svd(rec, (size_t)m, (size_t)cols, (size_t)nr, u_s, vt);
+        free(rec);
+        *rank = nr;
+        *write_counter = 0;
+    }
+}
+
+/* CompressedKVCache::write_kv's low-rank branch (:842-853) replayed over rows 0..rows-1 of one
+ * (layer, head): the first row is decomposed, every later row updates.  u_s holds rows * rank_cfg
+ * floats, vt rank_cfg * cols; returns the final rank. */
+int orc_lowrank_replay(const float *k_rows, int rows, int cols, int rank_cfg, float *u_s, float *vt) {
+    if (rows <= 0) return 0;
+    int rank = orc_lowrank_decompose(k_rows, 1, cols, rank_cfg, u_s, vt);
+    int n = 1, counter = 0;
+    for (int i = 1; i < rows; i++) orc_lowrank_update(u_s, vt, &n, cols, &rank, &counter, k_rows + (size_t)i * cols);
+    return rank;
+}
+
 /* ---- RoPE: validate_rope_caches (:71-110) + apply_rope_in_place (:177-231)
  * + rotate_rope_block (:137-160) ---------------------------------------- */
 int orc_apply_rope(float *x, int b, int h, int sq, int d,

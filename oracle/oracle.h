@@ -54,6 +54,11 @@ int orc_polar_decode(const uint8_t *codes, float scale, float zero_point,
 void orc_qjl_encode(const float *original, const float *approx, int dim,
                     uint64_t *sign_bits, float *c_magnitude);
 float orc_qjl_correction(const uint64_t *a_bits, float a_c, const uint64_t *b_bits, float b_c, int dim);
+int orc_lowrank_decompose(const float *k, int rows, int cols, int rank, float *u_s, float *vt);
+void orc_lowrank_reconstruct(const float *u_s, const float *vt, int rows, int cols, int rank, float *out);
+void orc_lowrank_update(float *u_s, float *vt, int *rows, int cols, int *rank, int *write_counter,
+                        const float *new_row);
+int orc_lowrank_replay(const float *k_rows, int rows, int cols, int rank_cfg, float *u_s, float *vt);
 
 /* ---- attention (ops/microsoft.rs) -------------------------------------- */
 /* apply_rope_in_place (:177-231) over a (B, H, Sq, D) f32 tensor.

@@ -54,6 +54,7 @@ class KvCacheConfig(ctypes.Structure):
         ("bits", ctypes.c_int32),
         ("seed", ctypes.c_uint64),
         ("qjl_residual", ctypes.c_int32),
+        ("lowrank_k", ctypes.c_int32),
     ]
 
 
@@ -75,6 +76,8 @@ class KvLayerView(ctypes.Structure):
         ("v_qjl_bits", ctypes.c_void_p),
         ("k_qjl_mag", ctypes.c_void_p),
         ("v_qjl_mag", ctypes.c_void_p),
+        ("lr_vt", ctypes.c_void_p),
+        ("lr_us", ctypes.c_void_p),
     ]
 
 

@@ -506,10 +506,6 @@ extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t pas
                              (long long)(past_len + seq_len - 1), cache_rows);
     }
 
-    StaticScratchSlot slot;
-    int rc = static_scratch_for_current_device(&slot);
-    if (rc != SA_OK) return rc;
-
     AttendArgs a{};
     a.query = query;
     a.out = attn_out;
@@ -535,6 +531,16 @@ extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t pas
     a.cache_rows = cache_rows;
     a.do_rotary = do_rotary ? 1 : 0;
     a.interleaved = rotary_interleaved ? 1 : 0;
+    if (v.lr_us && v.lr_vt) {
+        // low-rank K: one pass per query, no split-K scratch
+        a.lr_vt = v.lr_vt;
+        a.lr_us = v.lr_us;
+        return launch_lowrank_attend(a, static_cast<cudaStream_t>(stream));
+    }
+
+    StaticScratchSlot slot;
+    int rc = static_scratch_for_current_device(&slot);
+    if (rc != SA_OK) return rc;
     a.workspace = slot.ptr;
     a.workspace_floats = kStaticScratchFloats;
     a.sm_count = slot.sm_count;

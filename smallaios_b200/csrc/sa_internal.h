@@ -63,6 +63,11 @@ struct kv_cache_impl {
     float *v_qjl_mag;
     size_t layer_qjl_bytes;    // B*H*T*D/8
     size_t layer_qjl_floats;   // B*H*T
+    float *lr_vt;              // [L][B][H][D], nullptr unless cfg.lowrank_k
+    float *lr_us;              // [L][B][H][T]
+    float *lr_scratch;         // [L][B][H][T]: the power iteration's u vector
+    size_t layer_lr_vt_floats; // B*H*D
+    size_t layer_lr_us_floats; // B*H*T
 };
 
 // Parameters of one append launch (K and V of `batch * seq_len` tokens).
@@ -81,6 +86,8 @@ struct AppendArgs {
     // QJL residuals of the appended vectors (all nullptr: not stored)
     uint8_t *k_qjl_bits, *v_qjl_bits;
     float *k_qjl_mag, *v_qjl_mag;
+    // low-rank K state (all nullptr: off)
+    float *lr_vt, *lr_us, *lr_scratch;
 };
 
 // Parameters of the fused QKV projection's epilogue (one token per row):
@@ -111,9 +118,12 @@ struct AttendArgs {
     uint32_t *qprep;  // decode prep area: per (row, head) q-digit fragments + constants
     int *dev_status;  // device-side status word (bounded waits that gave up)
     GatherOut gather;  // head-sharded output (n = 0: write `out`)
+    const float *lr_vt, *lr_us;  // low-rank K (nullptr: keys from the codes)
 };
 
 int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
+int launch_lowrank_append(const AppendArgs &a, cudaStream_t stream);
+int launch_lowrank_attend(const AttendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
 int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream);
 bool decode_fast_eligible(const AttendArgs &a);

@@ -127,6 +127,7 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     if (c.kv_head_count <= 0 || c.kv_head_begin < 0 || c.kv_head_begin + c.kv_head_count > c.num_kv_heads)
         return set_error(SA_ERR_INVALID_ATTRIBUTE, "kv head range [%d, %d) outside [0, %d)", c.kv_head_begin,
                          c.kv_head_begin + c.kv_head_count, c.num_kv_heads);
+    if (c.lowrank_k < 0) return set_error(SA_ERR_INVALID_ATTRIBUTE, "kv_lowrank_k must be >= 0 (0 = None)");
     if ((int64_t)c.max_seq_len > (int64_t)0x7fffffff - kCapacityAlign)
         return set_error(SA_ERR_INVALID_ARGUMENT, "max_seq_len too large");
 
@@ -161,7 +162,12 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->layer_qjl_floats = c.qjl_residual ? B * H * T : 0;
     const size_t qjl_bits = up(L * k->layer_qjl_bytes);
     const size_t qjl_mag = up(L * k->layer_qjl_floats * sizeof(float));
-    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st + 2 * qjl_bits + 2 * qjl_mag;
+    // low-rank K (KVCacheConfig::kv_lowrank_k): V^T row, U*S column and the power iteration's u
+    k->layer_lr_vt_floats = c.lowrank_k > 0 ? B * H * D : 0;
+    k->layer_lr_us_floats = c.lowrank_k > 0 ? B * H * T : 0;
+    const size_t lr_vt = up(L * k->layer_lr_vt_floats * sizeof(float));
+    const size_t lr_us = up(L * k->layer_lr_us_floats * sizeof(float));
+    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st + 2 * qjl_bits + 2 * qjl_mag + lr_vt + 2 * lr_us;
     const size_t k_bytes = k->base_bytes;
     cudaError_t e = cudaMalloc(&k->base, k->base_bytes);
     if (e != cudaSuccess) {
@@ -195,6 +201,14 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
         k->k_qjl_mag = reinterpret_cast<float *>(p);
         p += qjl_mag;
         k->v_qjl_mag = reinterpret_cast<float *>(p);
+        p += qjl_mag;
+    }
+    if (c.lowrank_k > 0) {
+        k->lr_vt = reinterpret_cast<float *>(p);
+        p += lr_vt;
+        k->lr_us = reinterpret_cast<float *>(p);
+        p += lr_us;
+        k->lr_scratch = reinterpret_cast<float *>(p);
     }
     // Zero-initialise like GpuKvCache::allocate (kv_cache.rs:171-175).
     e = cudaMemset(k->base, 0, k->base_bytes);
@@ -309,6 +323,11 @@ int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config)
     return SA_OK;
 }
 
+// The layer's power-iteration scratch of the low-rank K state (nullptr when off).
+static float *lr_scratch_of(const kv_cache_impl *k, int32_t layer) {
+    return k->lr_scratch ? k->lr_scratch + (size_t)layer * k->layer_lr_us_floats : nullptr;
+}
+
 int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_view *v) {
     if (!cache || !v) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_layer_view: NULL argument");
     const kv_cache_impl *k = reinterpret_cast<const kv_cache_impl *>(cache);
@@ -326,6 +345,9 @@ int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_
     v->code_bytes = k->code_bytes;
     v->capacity = k->capacity;
     v->wht_scale = k->wht_scale;
+    const bool lr = k->lr_vt != nullptr;
+    v->lr_vt = lr ? k->lr_vt + (size_t)layer * k->layer_lr_vt_floats : nullptr;
+    v->lr_us = lr ? k->lr_us + (size_t)layer * k->layer_lr_us_floats : nullptr;
     const bool qjl = k->k_qjl_bits != nullptr;
     v->k_qjl_bits = qjl ? k->k_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
     v->v_qjl_bits = qjl ? k->v_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
@@ -392,6 +414,9 @@ int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void 
     a.v_qjl_bits = v.v_qjl_bits;
     a.k_qjl_mag = v.k_qjl_mag;
     a.v_qjl_mag = v.v_qjl_mag;
+    a.lr_vt = v.lr_vt;
+    a.lr_us = v.lr_us;
+    a.lr_scratch = lr_scratch_of(k, layer);
     a.signs = v.signs;
     a.wht_scale = v.wht_scale;
     a.cos_cache = cos_cache;
@@ -399,7 +424,9 @@ int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void 
     a.cache_rows = cache_rows;
     a.do_rotary = do_rotary ? 1 : 0;
     a.interleaved = rotary_interleaved ? 1 : 0;
-    return launch_kv_append(a, static_cast<cudaStream_t>(stream));
+    int rc2 = launch_kv_append(a, static_cast<cudaStream_t>(stream));
+    if (rc2 != SA_OK || !a.lr_us) return rc2;
+    return launch_lowrank_append(a, static_cast<cudaStream_t>(stream));
 }
 
 // Attention of `seq_len` query tokens over the cache.  When `key`/`value`
@@ -446,6 +473,8 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
     a.v_meta = v.v_meta;
     a.signs = v.signs;
     a.wht_scale = v.wht_scale;
+    a.lr_vt = v.lr_vt;
+    a.lr_us = v.lr_us;
     // GroupQueryAttention scale (ops/microsoft.rs:1160): attribute, else 1/sqrt_f32(D).
     a.scale = has_scale ? scale : 1.0f / host_sqrt_f32((float)v.head_dim);
     a.cos_cache = cos_cache;
@@ -480,6 +509,9 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         ap.v_qjl_bits = v.v_qjl_bits;
         ap.k_qjl_mag = v.k_qjl_mag;
         ap.v_qjl_mag = v.v_qjl_mag;
+        ap.lr_vt = v.lr_vt;
+        ap.lr_us = v.lr_us;
+        ap.lr_scratch = lr_scratch_of(k, layer);
         ap.signs = v.signs;
         ap.wht_scale = v.wht_scale;
         ap.cos_cache = cos_cache;
@@ -487,6 +519,19 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         ap.cache_rows = cache_rows;
         ap.do_rotary = a.do_rotary;
         ap.interleaved = a.interleaved;
+    }
+    if (a.lr_us) {
+        // low-rank K: keys are lr_us[t] * lr_vt (read_k, kv_compression.rs:870-882)
+        if (key) {
+            rc = launch_kv_append(ap, stream);
+            if (rc == SA_OK) rc = launch_lowrank_append(ap, stream);
+            if (rc != SA_OK) return rc;
+        }
+        AttendArgs la = a;
+        la.gather.n = 0;
+        rc = launch_lowrank_attend(la, stream);
+        if (rc != SA_OK || a.gather.n == 0) return rc;
+        return launch_gather_scatter(a, stream);
     }
     if (decode_fast_eligible(a)) return launch_gqa_decode_fast(a, key ? &ap : nullptr, stream);
     if (key) {
@@ -651,6 +696,9 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
     ap.v_qjl_bits = v.v_qjl_bits;
     ap.k_qjl_mag = v.k_qjl_mag;
     ap.v_qjl_mag = v.v_qjl_mag;
+    ap.lr_vt = v.lr_vt;
+    ap.lr_us = v.lr_us;
+    ap.lr_scratch = lr_scratch_of(k, layer);
     ap.signs = v.signs;
     ap.wht_scale = v.wht_scale;
     ap.cos_cache = cos_cache;
@@ -664,8 +712,11 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
     const int64_t n = qc + 2 * kc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((D == 64 || D == 128) && qc % 128 == 0 && kc % 128 == 0 &&
-        matmul_nbits_umma_eligible(x, w_codes, w_scales, nullptr, dtype, batch, n, hidden, 32))
-        return launch_qkv_umma_fused(x, w_codes, w_scales, a, n, hidden, st);
+        matmul_nbits_umma_eligible(x, w_codes, w_scales, nullptr, dtype, batch, n, hidden, 32)) {
+        rc = launch_qkv_umma_fused(x, w_codes, w_scales, a, n, hidden, st);
+        if (rc != SA_OK || !ap.lr_us) return rc;
+        return launch_lowrank_append(ap, st);  // k_out holds the projection before RoPE
+    }
     // the three projections (row ranges of the packed weights), then the epilogue launch
     const int64_t row_codes = hidden / 2, row_scales = (hidden / 32) * 2;
     const uint8_t *sc = static_cast<const uint8_t *>(w_scales);
@@ -677,7 +728,9 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
         rc = launch_matmul_nbits(x, w_codes + (qc + kc) * row_codes, sc + (qc + kc) * row_scales, nullptr, nullptr,
                                  v_out, dtype, batch, kc, hidden, 32, st);
     if (rc != SA_OK) return rc;
-    return launch_qkv_finish(a, st);
+    rc = launch_qkv_finish(a, st);
+    if (rc != SA_OK || !ap.lr_us) return rc;
+    return launch_lowrank_append(ap, st);
 }
 
 int sa_rms_norm(const void *x, const void *skip, const void *bias, const void *weight, void *y, void *pre,

@@ -50,6 +50,9 @@ class LayerView:
     v_qjl_bits: torch.Tensor | None = None
     k_qjl_mag: torch.Tensor | None = None   # f32 (B, H, T): c_magnitude
     v_qjl_mag: torch.Tensor | None = None
+    # low-rank K state (KVCacheConfig::kv_lowrank_k), None unless the cache keeps it
+    lr_vt: torch.Tensor | None = None  # f32 (B, H, D): the rank-1 V^T row
+    lr_us: torch.Tensor | None = None  # f32 (B, H, T): U*S, one coefficient per written row
 
     def v_codes_tokens(self) -> torch.Tensor:
         """V codes in per-token pack_bits order (B, H, T, CB).
@@ -93,12 +96,15 @@ class GpuKvCache:
     codes the unsharded one would.  ``qjl_residual`` (KVCacheConfig::
     kv_qjl_residual) makes every append also store the QJL residual of each
     vector; nothing reads it back, as in the reference, so it is off by default.
+    ``lowrank_k`` (KVCacheConfig::kv_lowrank_k) keeps the low-rank K state of
+    LowRankKeyDecomposer; attention then reads keys as its reconstruction, as
+    read_k does.
     """
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_seq_len: int, *,
                  batch: int = 1, num_heads: int | None = None, bits: int = 4, seed: int = DEFAULT_SEED,
                  kv_head_begin: int = 0, kv_head_count: int | None = None, qjl_residual: bool = False,
-                 device=None):
+                 lowrank_k: int | None = None, device=None):
         self.device = torch.device(device if device is not None else "cuda", )
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
@@ -114,6 +120,8 @@ class GpuKvCache:
         cfg.bits = bits
         cfg.seed = seed & (2**64 - 1)
         cfg.qjl_residual = 1 if qjl_residual else 0
+        # kv_lowrank_k: None = off; Some(0) means rank 1 (LowRankKeyDecomposer::new, :460-465)
+        cfg.lowrank_k = 0 if lowrank_k is None else max(int(lowrank_k), 1)
         self._handle = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             check(lib.sa_kv_cache_create(ctypes.byref(cfg), ctypes.byref(self._handle)))
@@ -181,7 +189,10 @@ class GpuKvCache:
                 k_qjl_bits=_view(v.k_qjl_bits, (B, H, T, D // 8), "|u1", dev),
                 v_qjl_bits=_view(v.v_qjl_bits, (B, H, T, D // 8), "|u1", dev),
                 k_qjl_mag=_view(v.k_qjl_mag, (B, H, T), "<f4", dev),
-                v_qjl_mag=_view(v.v_qjl_mag, (B, H, T), "<f4", dev))))
+                v_qjl_mag=_view(v.v_qjl_mag, (B, H, T), "<f4", dev))),
+            **({} if not v.lr_us else dict(
+                lr_vt=_view(v.lr_vt, (B, H, D), "<f4", dev),
+                lr_us=_view(v.lr_us, (B, H, T), "<f4", dev))))
 
     def close(self) -> None:
         if self._handle:

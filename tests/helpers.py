@@ -72,6 +72,49 @@ def oracle_qjl(k_bshd: np.ndarray, v_bshd: np.ndarray, signs_hd: np.ndarray, bit
     return tuple(out)
 
 
+def oracle_lowrank_state(k_bthd: np.ndarray, rank_cfg: int, cos=None, sin=None, do_rotary=False, interleaved=False):
+    """Low-rank K state that write_kv builds over rows 0..T-1 (kv_compression.rs:842-853).
+
+    k_bthd: (B, T, H, D) keys as appended (RoPE applied here when do_rotary).
+    Returns us (B, H, T) and vt (B, H, D) -- the cache's rank is 1.
+    """
+    b, t, h, d = k_bthd.shape
+    k = np.ascontiguousarray(np.transpose(k_bthd, (0, 2, 1, 3)), np.float32)
+    if do_rotary:
+        k = oracle.apply_rope(k, cos, sin, np.arange(t), interleaved=interleaved)
+    us = np.zeros((b, h, t), np.float32)
+    vt = np.zeros((b, h, d), np.float32)
+    for bi in range(b):
+        for hi in range(h):
+            u_s, v_t, rank = oracle.lowrank_replay(k[bi, hi], rank_cfg)
+            assert rank == 1
+            us[bi, hi], vt[bi, hi] = u_s[:, 0], v_t[0]
+    return us, vt
+
+
+def oracle_lowrank_attend(q_bshd, us, vt, vc, vm, signs_hd, bits, pos0, scale=None, cos=None, sin=None,
+                          do_rotary=False, interleaved=False):
+    """Composite oracle with low-rank K: read_k returns 0 + U*S[t] * V^T (:870-882, :502-526), read_v
+    decodes the codes, then causal SDPA.  q_bshd (B, S, Hq, D); us (B, H, T); vt (B, H, D); codes and
+    meta (B, H, T, ...).  Returns (B, S, Hq*D)."""
+    b, s, hq, d = q_bshd.shape
+    h, t = us.shape[1], us.shape[2]
+    q = np.ascontiguousarray(np.transpose(q_bshd, (0, 2, 1, 3)), np.float32)
+    if do_rotary:
+        q = oracle.apply_rope(q, cos, sin, np.arange(pos0, pos0 + s), interleaved=interleaved)
+    k = (us[..., None] * vt[:, :, None, :]).astype(np.float32) + np.float32(0.0)
+    v = np.zeros((b, h, t, d), np.float32)
+    for bi in range(b):
+        for hi in range(h):
+            for ti in range(t):
+                v[bi, hi, ti] = oracle.polar_decode(vc[bi, hi, ti], vm[bi, hi, ti, 0], vm[bi, hi, ti, 1], d, bits,
+                                                    signs_hd[hi])
+    if scale is None:
+        scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(d)))
+    out = oracle.sdpa(q, k, v, past_sk=pos0, scale=scale, causal=True)  # (B, Hq, S, D)
+    return np.ascontiguousarray(np.transpose(out, (0, 2, 1, 3))).reshape(b, s, hq * d)
+
+
 def oracle_attend(q_bshd: np.ndarray, kc, km, vc, vm, signs_hd, bits, pos0, scale=None, cos=None, sin=None,
                   do_rotary=False, interleaved=False):
     """Composite oracle: RoPE q at positions pos0.., read_k/read_v, causal SDPA.

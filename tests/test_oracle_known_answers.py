@@ -396,3 +396,71 @@ def test_silu_known_answers():
     assert abs(y[0]) < 1e-5
     assert abs(y[1] - 0.7310) < 1e-2 and abs(y[2] - 1.7616) < 1e-2 and abs(y[3] + 0.2689) < 1e-2
     assert np.allclose(oracle.silu_mul(np.array([1.0]), np.array([3.0])), 3 * 0.7310586, atol=1e-4)
+
+
+# ---- LowRankKeyDecomposer (kv_compression.rs:1312-1486, 1591-1612, 1883-1953) ----
+
+def _l2(a, b):
+    return float(np.sqrt(((np.asarray(a, np.float32) - np.asarray(b, np.float32)) ** 2).sum()))
+
+
+def test_lowrank_reconstruction_error_decreases_with_rank():
+    m = np.array([[i + j for j in range(8)] for i in range(16)], np.float32)
+    e = [_l2(m, oracle.LowRankK(m, 16, 8, r).reconstruct()) for r in (1, 2, 4)]
+    assert e[1] <= e[0] + 1e-3 and e[2] <= e[1] + 1e-3
+
+
+def test_lowrank_rank1_matrix():
+    u = np.arange(1, 9, dtype=np.float32)
+    v = np.arange(1, 5, dtype=np.float32) * 0.5
+    m = np.outer(u, v).astype(np.float32)
+    rec = oracle.LowRankK(m, 8, 4, 1).reconstruct()
+    assert _l2(m, rec) / (np.sqrt((m ** 2).sum()) + 1e-10) < 0.6
+
+
+def test_lowrank_incremental_update_and_zero_row():
+    lr = oracle.LowRankK(np.arange(32, dtype=np.float32) * 0.1, 4, 8, 4)
+    assert lr.rows == 4
+    lr.update(np.arange(8, dtype=np.float32) * 0.5)
+    assert lr.rows == 5 and lr.u_s[:5 * lr.rank].size == 5 * lr.rank
+    lr = oracle.LowRankK(np.arange(16, dtype=np.float32), 2, 8, 2)
+    lr.update(np.zeros(8, np.float32))
+    assert lr.rows == 3
+
+
+def test_lowrank_empty_full_rank_single_row():
+    lr = oracle.LowRankK(np.zeros(0, np.float32), 0, 8, 4)
+    assert lr.rows == 0 and lr.reconstruct().size == 0
+    m = np.diag(np.arange(1, 5, dtype=np.float32))
+    rec = oracle.LowRankK(m, 4, 4, 4).reconstruct()
+    assert _l2(m, rec) / (np.sqrt((m ** 2).sum()) + 1e-10) < 0.01
+    row = np.arange(1, 9, dtype=np.float32)
+    assert _l2(row, oracle.LowRankK(row, 1, 8, 4).reconstruct()[0]) < 1.0
+
+
+def test_lowrank_incremental_preserves_cols():
+    lr = oracle.LowRankK(np.arange(16, dtype=np.float32), 1, 16, 4)
+    for r in range(10):
+        lr.update((np.arange(16) + r).astype(np.float32) * 0.1)
+    assert lr.rows == 11 and lr.cols == 16
+
+
+def test_lowrank_cache_replay_rank_is_one_and_bounded():
+    """write_kv decomposes the first K row alone (rows = 1), so the cache's rank is
+    min(rank, 1, D) = 1 from then on (:842-853, :483, :566); integration_lowrank_improves_k_accuracy."""
+    dim, seq = 16, 16
+    b1 = np.arange(dim, dtype=np.float32) * 0.1
+    b2 = (dim - np.arange(dim)).astype(np.float32) * 0.05
+    k = np.stack([np.float32(p * 0.3) * b1 + np.float32((seq - p) * 0.2) * b2 for p in range(seq)]).astype(np.float32)
+    u_s, vt, rank = oracle.lowrank_replay(k, 4)
+    assert rank == 1 and u_s.shape == (seq, 1) and vt.shape == (1, dim)
+    rec = np.zeros((seq, dim), np.float32)
+    oracle.lib().orc_lowrank_reconstruct(oracle._ptr(u_s), oracle._ptr(vt), seq, dim, 1, oracle._ptr(rec))
+    assert _l2(k, rec) / (np.sqrt((k ** 2).sum()) + 1e-6) < 2.0
+    # replay == decompose + update by hand, across a re-orthogonalisation (every 512 writes)
+    kk = np.random.default_rng(1).standard_normal((1030, 32)).astype(np.float32)
+    u_s, vt, _ = oracle.lowrank_replay(kk, 8)
+    lr = oracle.LowRankK(kk[0], 1, 32, 8, capacity=1030)
+    for i in range(1, 1030):
+        lr.update(kk[i])
+    assert np.array_equal(u_s.reshape(-1), lr.u_s[:1030]) and np.array_equal(vt.reshape(-1), lr.vt[:32])
