@@ -186,6 +186,11 @@ int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, 
                            int32_t q_heads_total);
 /* Copy of the cache configuration. */
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config);
+/* CompressedKVCache::memory_bytes (kv_compression.rs:928-957) of the rows
+ * written so far, summed over the batch's sequences and the KV heads held
+ * here (the reference's per-block accounting, :166-168, :352-354, :442-444),
+ * and the bytes this cache holds on the device.  Either pointer may be NULL. */
+int sa_kv_cache_memory_bytes(const sa_kv_cache *cache, uint64_t *reference_bytes, uint64_t *device_bytes);
 /* Device-side status of the kernels that used this cache: 0, or bit 0 set when
  * a bounded wait inside a kernel gave up (the kernel then stopped and its
  * output is not valid).  Synchronises with the device; `clear` resets it.

@@ -32,7 +32,7 @@ SA_DTYPE_BFLOAT16 = 16
 EXPORTED = [
     "sa_last_error_string", "sa_status_string", "sa_version", "sa_kernel_launches",
     "sa_kv_cache_create", "sa_kv_cache_destroy", "sa_kv_cache_reset", "sa_kv_cache_position",
-    "sa_kv_cache_set_position", "sa_kv_cache_advance", "sa_kv_cache_layer_view", "sa_kv_cache_get_config",
+    "sa_kv_cache_set_position", "sa_kv_cache_advance", "sa_kv_cache_layer_view", "sa_kv_cache_get_config", "sa_kv_cache_memory_bytes",
     "sa_kv_cache_device_status", "sa_kv_cache_set_gather",
     "sa_kv_append", "sa_gqa_attend", "sa_group_query_attention", "sa_matmul_nbits", "sa_gqa_attend_no_alloc",
     "sa_matmul_nbits_packed_bytes", "sa_matmul_nbits_prepack", "sa_matmul_nbits_packed",
@@ -112,6 +112,8 @@ def _declare(l: ctypes.CDLL) -> None:
     l.sa_kv_cache_layer_view.argtypes = [_P, _I32, ctypes.POINTER(KvLayerView)]
     l.sa_kv_cache_get_config.restype = ctypes.c_int
     l.sa_kv_cache_get_config.argtypes = [_P, ctypes.POINTER(KvCacheConfig)]
+    l.sa_kv_cache_memory_bytes.restype = ctypes.c_int
+    l.sa_kv_cache_memory_bytes.argtypes = [_P, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     l.sa_kv_cache_device_status.restype = ctypes.c_int
     l.sa_kv_cache_device_status.argtypes = [_P, ctypes.POINTER(_I32), _I32]
     l.sa_kv_cache_set_gather.restype = ctypes.c_int

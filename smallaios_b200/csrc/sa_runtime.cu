@@ -323,6 +323,25 @@ int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config)
     return SA_OK;
 }
 
+// CompressedKVCache::memory_bytes (kv_compression.rs:928-957) of the `position` rows written so
+// far, per sequence of the batch and summed over it: per (layer, head, row) a K and a V
+// QuantizedBlock (code bytes + 4*4 + 8 + 1, :166-168), with QJL two QJLResidual (8*ceil(D/64)
+// + 4 + 8, :352-354); with low-rank K one LowRankK per (layer, head) once a row exists
+// ((rows*rank + rank*D)*4 + 8*4, :442-444, rank 1).  `device_bytes` is the allocation.
+int sa_kv_cache_memory_bytes(const sa_kv_cache *cache, uint64_t *reference_bytes, uint64_t *device_bytes) {
+    if (!cache) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_memory_bytes: NULL cache");
+    const kv_cache_impl *k = reinterpret_cast<const kv_cache_impl *>(cache);
+    const uint64_t rows = (uint64_t)k->position, D = (uint64_t)k->cfg.head_dim;
+    uint64_t per_row = 2 * ((uint64_t)k->code_bytes + 4 * 4 + 8 + 1);
+    if (k->cfg.qjl_residual) per_row += 2 * (8 * ((D + 63) / 64) + 4 + 8);
+    uint64_t per_head = rows * per_row;
+    if (k->cfg.lowrank_k > 0 && rows > 0) per_head += (rows * 1 + 1 * D) * 4 + 8 * 4;
+    const uint64_t heads = (uint64_t)k->cfg.num_layers * (uint64_t)k->cfg.kv_head_count * (uint64_t)k->cfg.batch;
+    if (reference_bytes) *reference_bytes = heads * per_head;
+    if (device_bytes) *device_bytes = (uint64_t)k->base_bytes;
+    return SA_OK;
+}
+
 // The layer's power-iteration scratch of the low-rank K state (nullptr when off).
 static float *lr_scratch_of(const kv_cache_impl *k, int32_t layer) {
     return k->lr_scratch ? k->lr_scratch + (size_t)layer * k->layer_lr_us_floats : nullptr;

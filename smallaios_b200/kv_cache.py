@@ -194,6 +194,67 @@ class GpuKvCache:
                 lr_vt=_view(v.lr_vt, (B, H, D), "<f4", dev),
                 lr_us=_view(v.lr_us, (B, H, T), "<f4", dev))))
 
+    def memory_bytes(self) -> tuple[int, int]:
+        """(CompressedKVCache::memory_bytes of the rows written so far, summed over the batch,
+        bytes held on the device) -- kv_compression.rs:928-957."""
+        ref, dev = ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib.sa_kv_cache_memory_bytes(self.handle, ctypes.byref(ref), ctypes.byref(dev)))
+        return ref.value, dev.value
+
+    # Arrays of a layer that make up the compressed state (signs are derived from the seed).
+    _STATE = ("k_codes", "v_codes", "k_meta", "v_meta", "k_qjl_bits", "v_qjl_bits", "k_qjl_mag", "v_qjl_mag",
+              "lr_vt", "lr_us")
+
+    def state_dict(self) -> dict:
+        """The compressed cache as host tensors: configuration, position and, per layer, the
+        codes, metadata and optional QJL / low-rank state of the rows written so far.  The
+        rotation signs are not stored; they follow from the seed (kv_compression.rs:776-779),
+        so a state saved on one machine replays on another."""
+        pos = self.current_position()
+        torch.cuda.synchronize(self.device)
+        cfg = {f: getattr(self.config, f) for f, _ in _lib.KvCacheConfig._fields_}
+        layers = []
+        for layer in range(self.config.num_layers):
+            v = self.view(layer)
+            st = {}
+            for name in self._STATE:
+                t = getattr(v, name)
+                if t is None:
+                    continue
+                if name == "v_codes":  # 16-token blocks: keep whole blocks up to the position
+                    t = t[:, :, :(pos + 15) // 16]
+                elif name != "lr_vt":
+                    t = t[:, :, :pos]
+                st[name] = t.cpu().clone()
+            layers.append(st)
+        return {"format": "smallaios_b200.kv_cache/1", "config": cfg, "position": pos, "layers": layers}
+
+    @classmethod
+    def from_state_dict(cls, state: dict, device=None) -> "GpuKvCache":
+        """A cache with the saved configuration and contents, positioned where it was saved."""
+        if state.get("format") != "smallaios_b200.kv_cache/1":
+            raise ValueError("not a smallaios_b200 KV-cache state")
+        c = state["config"]
+        cache = cls(c["num_layers"], c["num_kv_heads"], c["head_dim"], c["max_seq_len"], batch=c["batch"],
+                    num_heads=c["num_heads"], bits=c["bits"], seed=c["seed"], kv_head_begin=c["kv_head_begin"],
+                    kv_head_count=c["kv_head_count"], qjl_residual=bool(c["qjl_residual"]),
+                    lowrank_k=c["lowrank_k"] or None, device=device)
+        pos = int(state["position"])
+        for layer, st in enumerate(state["layers"]):
+            v = cache.view(layer)
+            for name, t in st.items():
+                dst = getattr(v, name)
+                if dst is None:
+                    raise ValueError(f"state has {name} but the cache does not keep it")
+                if name == "v_codes":
+                    dst = dst[:, :, :t.shape[2]]
+                elif name != "lr_vt":
+                    dst = dst[:, :, :t.shape[2]]
+                dst.copy_(t.to(cache.device))
+        torch.cuda.synchronize(cache.device)
+        cache.set_position(pos)
+        return cache
+
     def close(self) -> None:
         if self._handle:
             with torch.cuda.device(self.device):
