@@ -1,0 +1,517 @@
+// GroupQueryAttention of a prefill chunk (16 or more query tokens per
+// sequence) on the 5th-generation tensor cores (tcgen05), flash-attention
+// style in the rotated domain, with the codes themselves as the K and V
+// operands (integers below 256 are exact in fp16):
+//
+//   q . k_hat = scale_t * (q' . c_t) + zp_t * sum(q')
+//   sum_t p_t v_hat_t = S.H.(sum_t u_t c_t * 2^(R-m) + (sum_t p_t zp_t) 1)/sqrt(n)
+//
+// with q' = H.S.RoPE(q)/sqrt(n) (PolarQuantizer::decode, kv_compression.rs:
+// 270-286, read backwards) and u_t = p_t * scale_t * 2^(m-R).  q' and u are
+// each split into two fp16 halves (hi + lo), so the products are exact to
+// about 2^-22 and everything else is f32.
+//
+// One CTA of 8 warps takes 128 query rows -- 128/G positions times the G query
+// heads of one KV head -- as the MMA's M = 128 (one TMEM lane per row), and
+// walks the causal range of the cache in tiles of 64 tokens:
+//   all warps  stage the tile: K and V codes as fp16 into shared memory in the
+//              128-byte-swizzle K-major layout the MMA reads, and the tile's
+//              {k scale, k zp, v scale, v zp};
+//   warp 4     one elected lane issues S = (Q'hi + Q'lo).C_K^T (A and B from
+//              shared memory, D = f32 in TMEM, N = 64) and, once the softmax
+//              has written U, O += (Uhi + Ulo).C_V (A from TMEM, N = D);
+//   warps 0-3  one thread per row: tcgen05.ld of its 64 scores, per-token
+//              scale / zero point, causal mask, online softmax in base 2, U
+//              into TMEM (tcgen05.st).  The V reference R (u <= 2^8) moves
+//              only when the row's maximum outgrows it by 8 octaves; then the
+//              thread rescales its row of O in TMEM.
+// At the end O' = (O 2^(R-m) + Z)/L goes through shared memory, one warp
+// butterfly per row rotates it back, and it is stored.  Causal semantics as
+// scaled_dot_product_attention with past_sk = T - S (ops/microsoft.rs:380-438).
+//
+// Every mbarrier wait is bounded (2 s); a wait that gives up sets the abort
+// flag and bit 0 of the cache's status word, every role leaves its loop, the
+// issued MMAs are waited for (bounded) and TMEM is freed; the output is then
+// not written.
+#include "sa_common.cuh"
+#include "sa_internal.h"
+#include "sa_tcgen05.cuh"
+
+namespace sa {
+
+namespace {
+
+constexpr int kPuRows = 128;  // query rows per CTA: UMMA M, TMEM lanes
+constexpr int kPuTok = 64;    // tokens per KV tile: UMMA N of S, K of O += U.C
+constexpr int kPuWarps = 8;
+constexpr int kPuMmaWarp = 4;
+constexpr uint32_t kPuTmemCols = 256;
+constexpr uint32_t kPuS = 0, kPuUh = 64, kPuUl = 96, kPuO = 128;  // TMEM columns
+constexpr float kPuLazy = 8.0f;  // octaves the V reference may lag the row maximum (u <= 2^8)
+
+template <int D>
+struct PuGeo {
+    static constexpr int KBLK = D / 64;                // 64-element (128-byte) k-blocks per row
+    static constexpr int Q_PLANE = kPuRows * D * 2;    // KBLK tiles of [128 rows][128 B]
+    static constexpr int K_BLK = kPuTok * 128;         // one k-block of the K tile: [64 tokens][128 B]
+    static constexpr int K_TILE = KBLK * K_BLK;
+    static constexpr int V_TILE = D * 128;             // [D dims][64 tokens]
+    static constexpr int K_OFF = 2 * Q_PLANE;
+    static constexpr int V_OFF = K_OFF + K_TILE;
+    static constexpr int META_OFF = V_OFF + V_TILE;    // float4 per token
+    static constexpr int QSUM_OFF = META_OFF + kPuTok * 16;
+    static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4;
+    static constexpr int SMEM = BAR_OFF + 64 + 1024;   // + slack to align the base to 1024 B
+    static_assert(kPuRows * D * 4 <= K_OFF, "O' staging reuses the q' planes");
+};
+
+// (lo, hi) -> fp16 pairs h = rn(x) and l = rn(x - h)
+__device__ __forceinline__ void split_h2(float lo, float hi, uint32_t &h, uint32_t &l) {
+    const __half2 hh = __floats2half2_rn(lo, hi);
+    const float2 back = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(lo - back.x, hi - back.y);
+    h = *reinterpret_cast<const uint32_t *>(&hh);
+    l = *reinterpret_cast<const uint32_t *>(&ll);
+}
+
+// bytes of x picked by sel -> fp16 pair of small integers (0x64XX is the fp16 1024 + XX)
+__device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
+    const uint32_t biased = __byte_perm(x, 0x64646464u, sel);
+    const __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&biased), __float2half2_rn(1024.0f));
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r in a [rows][128 B] 128-byte-swizzle tile.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B fp16 (K-major), M = 128, N.
+__host__ __device__ constexpr uint32_t pu_idesc(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kPuRows >> 4) << 24);
+}
+
+// grid = ceil(seq_len * G / 128) * kv heads * batch blocks (1-D), 256 threads.
+template <typename T, int BITS, int D>
+__global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendArgs a) {
+    using GG = PuGeo<D>;
+    constexpr int EPL = D / 32;
+    constexpr int CB = D * BITS / 8;
+    extern __shared__ unsigned char pu_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(pu_raw) + 1023) &
+                                                            ~(uintptr_t)1023);
+    unsigned char *qh = smem, *ql = smem + GG::Q_PLANE;
+    unsigned char *kt_s = smem + GG::K_OFF, *vt_s = smem + GG::V_OFF;
+    float4 *meta = reinterpret_cast<float4 *>(smem + GG::META_OFF);
+    float *qsum = reinterpret_cast<float *>(smem + GG::QSUM_OFF);
+    uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + GG::BAR_OFF);
+    uint64_t *bar_u = bar_s + 1, *bar_o = bar_s + 2, *bar_fin = bar_s + 3;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar_s + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bar_s + 5);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int units = a.heads * a.batch;
+    const int rblocks = (int)(gridDim.x / (unsigned)units);
+    const int h = (int)(blockIdx.x % (unsigned)a.heads), b = (int)(blockIdx.x / (unsigned)a.heads) % a.batch;
+    const int G = a.group;
+    // the last row blocks walk the most tiles: they take the lowest block indices
+    const int r0 = (rblocks - 1 - (int)(blockIdx.x / (unsigned)units)) * kPuRows;  // row = position * G + head
+    const int nrows = a.seq_len * G;
+    const int64_t unit = (int64_t)b * a.heads + h;
+    const float *sg = a.signs + (int64_t)h * D;
+
+    if (tid == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_u, 4);
+        mbar_init(bar_o, 1);
+        mbar_init(bar_fin, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) tmem_alloc(tslot, kPuTmemCols);
+
+    // ---- q' of 16 rows per warp: RoPE, signs, WHT, * scale * log2 e / sqrt(n), as hi + lo fp16 ----
+    const float qmul = a.wht_scale * a.scale * 1.4426950408889634f;
+    for (int i = 0; i < kPuRows / kPuWarps; i++) {
+        const int row = warp * (kPuRows / kPuWarps) + i, gr = r0 + row;
+        float x[EPL];
+        if (gr < nrows) {
+            const int s = gr / G, hd = gr % G;
+            const T *src = static_cast<const T *>(a.query) +
+                           (((int64_t)b * a.seq_len + s) * (a.heads * G) + h * G + hd) * D;
+            const int64_t pos = a.pos0 + s;
+#pragma unroll
+            for (int r = 0; r < EPL; r++) {
+                const int e = lane * EPL + r;
+                x[r] = ld_f32(src + e);
+                if (a.do_rotary) {
+                    const int half = D / 2;
+                    int pair, partner;
+                    bool first;
+                    if (a.interleaved) {
+                        pair = e >> 1;
+                        first = (e & 1) == 0;
+                        partner = first ? e + 1 : e - 1;
+                    } else {
+                        first = e < half;
+                        pair = first ? e : e - half;
+                        partner = first ? e + half : e - half;
+                    }
+                    const float c = a.cos_cache[pos * half + pair], sn = a.sin_cache[pos * half + pair];
+                    const float xo = ld_f32(src + partner);
+                    x[r] = first ? __fsub_rn(__fmul_rn(c, x[r]), __fmul_rn(sn, xo))
+                                 : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x[r]));
+                }
+                x[r] *= sg[e];
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) x[r] = 0.0f;
+        }
+        warp_wht_butterfly<EPL>(x, lane, D);
+        float sum = 0.0f;
+#pragma unroll
+        for (int r = 0; r < EPL; r += 2) {
+            const int e = lane * EPL + r;
+            const float x0 = x[r] * qmul, x1 = x[r + 1] * qmul;
+            sum += x0 + x1;
+            uint32_t hi, lo;
+            split_h2(x0, x1, hi, lo);
+            const uint32_t off = (uint32_t)((e >> 6) * (kPuRows * 128)) + sw_off(row, (e & 63) >> 3) + (e & 7) * 2;
+            *reinterpret_cast<uint32_t *>(qh + off) = hi;
+            *reinterpret_cast<uint32_t *>(ql + off) = lo;
+        }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+        if (lane == 0) qsum[row] = sum;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    // this thread's row (warps 0-3): position (a padding row takes the last position) and sum(q')
+    const int my_row = tid;  // valid for tid < 128
+    int pos_r = 0;
+    float qs_r = 0.0f;
+    if (warp < 4) {
+        int gr = r0 + my_row;
+        if (gr >= nrows) gr = nrows - 1;
+        pos_r = (int)a.pos0 + gr / G;
+        qs_r = qsum[my_row];
+    }
+    const int last_row = min(r0 + kPuRows, nrows) - 1;
+    const int pos_last = (int)a.pos0 + last_row / G;  // the CTA's largest position
+    const int ntiles = pos_last / kPuTok + 1;
+    const uint32_t tl = tbase + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's TMEM lane quarter
+
+    const uint8_t *kc = a.k_codes + unit * a.capacity * (int64_t)CB;
+    const uint8_t *vc = a.v_codes + unit * a.capacity * (int64_t)CB;
+    const float2 *kmeta = reinterpret_cast<const float2 *>(a.k_meta) + unit * a.capacity;
+    const float2 *vmeta = reinterpret_cast<const float2 *>(a.v_meta) + unit * a.capacity;
+
+    // running max m, the V reference R, sums of p and p * zp (rows of warps 0-3)
+    float m_r = -INFINITY, R_r = -INFINITY, l_r = 0.0f, z_r = 0.0f;
+    int issued = 0;  // MMA warp: tiles whose PV MMAs were committed
+    bool aborted = false;
+
+    for (int kt = 0; kt < ntiles; kt++) {
+        const int t0 = kt * kPuTok;
+        // the previous tile's MMAs have read the code tiles and U
+        bool ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+        if (ok) {
+            if (tid < kPuTok) {
+                // tokens past every row's position are masked; zero their (possibly unwritten) metadata
+                float4 m4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (t0 + tid <= pos_last) {
+                    const float2 km = kmeta[t0 + tid], vm = vmeta[t0 + tid];
+                    m4 = make_float4(km.x, km.y, vm.x, vm.y);
+                }
+                meta[tid] = m4;
+            }
+            // K tile: token rows of CB code bytes, 16 bytes per uint4
+            for (int u = tid; u < kPuTok * CB / 16; u += 32 * kPuWarps) {
+                const int tok = u / (CB / 16), ch = u % (CB / 16);
+                const uint4 w = *reinterpret_cast<const uint4 *>(kc + (int64_t)(t0 + tok) * CB + 16 * ch);
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                if constexpr (BITS == 8) {
+                    // 16 dims 16ch.. : two 16-byte chunks of fp16
+                    const int e = 16 * ch;
+                    unsigned char *blk = kt_s + (e >> 6) * GG::K_BLK;
+                    const int c0 = (e & 63) >> 3;
+#pragma unroll
+                    for (int hlf = 0; hlf < 2; hlf++) {
+                        uint4 o;
+                        o.x = bytes_to_h2(wv[2 * hlf], 0x4140u);
+                        o.y = bytes_to_h2(wv[2 * hlf], 0x4342u);
+                        o.z = bytes_to_h2(wv[2 * hlf + 1], 0x4140u);
+                        o.w = bytes_to_h2(wv[2 * hlf + 1], 0x4342u);
+                        *reinterpret_cast<uint4 *>(blk + sw_off(tok, c0 + hlf)) = o;
+                    }
+                } else {
+                    // 32 dims 32ch.. : four chunks; byte i holds dims 2i (low nibble), 2i + 1 (high)
+                    const int e = 32 * ch;
+                    unsigned char *blk = kt_s + (e >> 6) * GG::K_BLK;
+                    const int c0 = (e & 63) >> 3;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const uint32_t lo = wv[q] & 0x0f0f0f0fu, hi = (wv[q] >> 4) & 0x0f0f0f0fu;
+                        const uint32_t d03 = __byte_perm(lo, hi, 0x5140u), d47 = __byte_perm(lo, hi, 0x7362u);
+                        uint4 o;
+                        o.x = bytes_to_h2(d03, 0x4140u);
+                        o.y = bytes_to_h2(d03, 0x4342u);
+                        o.z = bytes_to_h2(d47, 0x4140u);
+                        o.w = bytes_to_h2(d47, 0x4342u);
+                        *reinterpret_cast<uint4 *>(blk + sw_off(tok, c0 + q)) = o;
+                    }
+                }
+            }
+            // V tile: four 16-token blocks of 16*CB contiguous bytes; a uint4 is chunk c of token
+            // group gq of a block: bytes k = 4j + (token & 3) for j = 4c .. 4c+3
+            const uint8_t *vtile = vc + (int64_t)(t0 / 16) * 16 * CB;
+            for (int u = tid; u < kPuTok * CB / 16; u += 32 * kPuWarps) {
+                const int blk = u / CB, rem = u % CB, c = rem / 4, gq = rem % 4;
+                const uint4 w = *reinterpret_cast<const uint4 *>(vtile + (int64_t)blk * 16 * CB + 64 * c + 16 * gq);
+                const int tok0 = blk * 16 + 4 * gq;  // tokens tok0 .. tok0 + 3 of the tile
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    const uint32_t x = wv[jj];
+                    if constexpr (BITS == 8) {
+                        const int dim = 4 * c + jj;
+                        uint2 o;
+                        o.x = bytes_to_h2(x, 0x4140u);
+                        o.y = bytes_to_h2(x, 0x4342u);
+                        *reinterpret_cast<uint2 *>(vt_s + sw_off(dim, tok0 >> 3) + (tok0 & 7) * 2) = o;
+                    } else {
+#pragma unroll
+                        for (int hi = 0; hi < 2; hi++) {
+                            const int dim = 2 * (4 * c + jj) + hi;
+                            const uint32_t nib = (x >> (4 * hi)) & 0x0f0f0f0fu;
+                            uint2 o;
+                            o.x = bytes_to_h2(nib, 0x4140u);
+                            o.y = bytes_to_h2(nib, 0x4342u);
+                            *reinterpret_cast<uint2 *>(vt_s + sw_off(dim, tok0 >> 3) + (tok0 & 7) * 2) = o;
+                        }
+                    }
+                }
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged tiles -> the tensor core
+        if (__syncthreads_or(!ok || *abort_flag)) {
+            aborted = true;
+            break;
+        }
+
+        if (warp == kPuMmaWarp) {
+            // ---- S = (Q'hi + Q'lo).C_K^T ----
+            tc_fence_after();
+            if (elect_one()) {
+                constexpr uint32_t ids = pu_idesc(kPuTok);
+#pragma unroll
+                for (int pl = 0; pl < 2; pl++)
+#pragma unroll
+                    for (int kb = 0; kb < GG::KBLK; kb++)
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++) {
+                            const uint64_t ad = sw128_kmajor_desc(smem_u32((pl ? ql : qh) + kb * (kPuRows * 128)) + 32 * kk);
+                            const uint64_t bd = sw128_kmajor_desc(smem_u32(kt_s + kb * GG::K_BLK) + 32 * kk);
+                            umma_ss(tbase + kPuS, ad, bd, ids, (pl | kb | kk) != 0 ? 1u : 0u);
+                        }
+                umma_commit(bar_s);
+            }
+            __syncwarp();
+        }
+
+        if (warp < 4) {
+            // ---- softmax of this thread's row ----
+            bool sok = tc_wait(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
+            sok = __all_sync(0xffffffffu, sok);
+            if (sok) {
+                tc_fence_after();
+                // pass 1: scores (scale / zero point per token, causal mask) and their maximum
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < kPuTok; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tl + kPuS + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float2 mt = *reinterpret_cast<const float2 *>(&meta[c + i]);
+                        const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
+                        mx = fmaxf(mx, t0 + c + i > pos_r ? -INFINITY : s);
+                    }
+                }
+                float vmax = 0.0f;
+                for (int t = 0; t < kPuTok; t++) vmax = fmaxf(vmax, meta[t].z);
+                const float lvmax = __log2f(fmaxf(vmax, 1.17549435e-38f));
+                const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
+                const float fac = exp2f(m_r - mn);
+                l_r *= fac;
+                z_r *= fac;
+                m_r = mn;
+                const float cand = mn + lvmax;
+                float ofac = 1.0f;
+                if (R_r == -INFINITY) {
+                    R_r = cand;  // first tile: O is still empty
+                } else if (cand > R_r + kPuLazy) {
+                    ofac = exp2f(R_r - cand);
+                    R_r = cand;
+                }
+                const float kr = exp2f(mn - R_r);
+                if (__any_sync(0xffffffffu, ofac != 1.0f)) {
+                    // rescale this warp's rows of O (the previous tile's MMAs have completed)
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 16) {
+                        uint32_t v[16];
+                        tmem_ld16(tl + kPuO + c, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * ofac);
+                        tmem_st16(tl + kPuO + c, v);
+                    }
+                }
+                // pass 2: p, the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
+#pragma unroll 1
+                for (int c = 0; c < kPuTok; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tl + kPuS + c, v);
+                    tmem_wait_ld();
+                    uint32_t uh[8], ul[8];
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        const float4 m0 = meta[c + i], m1 = meta[c + i + 1];
+                        float s0 = fmaf(__uint_as_float(v[i]), m0.x, m0.y * qs_r);
+                        float s1 = fmaf(__uint_as_float(v[i + 1]), m1.x, m1.y * qs_r);
+                        if (t0 + c + i > pos_r) s0 = -INFINITY;
+                        if (t0 + c + i + 1 > pos_r) s1 = -INFINITY;
+                        const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
+                        l_r += p0 + p1;
+                        z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
+                        split_h2(p0 * m0.z * kr, p1 * m1.z * kr, uh[i / 2], ul[i / 2]);
+                    }
+                    tmem_st8(tl + kPuUh + c / 2, uh);
+                    tmem_st8(tl + kPuUl + c / 2, ul);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_u);
+        }
+
+        if (warp == kPuMmaWarp) {
+            // ---- O += (Uhi + Ulo).C_V ----
+            bool uok = tc_wait(bar_u, (uint32_t)(kt & 1), abort_flag, a.dev_status);
+            uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
+            if (uok) {
+                tc_fence_after();
+                if (elect_one()) {
+                    constexpr uint32_t ido = pu_idesc(D);
+#pragma unroll
+                    for (int kk = 0; kk < kPuTok / 16; kk++) {
+                        const uint64_t bd = sw128_kmajor_desc(smem_u32(vt_s) + 32 * kk);
+                        umma_ts(tbase + kPuO, tbase + kPuUh + 8 * kk, bd, ido, (kt | kk) != 0 ? 1u : 0u);
+                        umma_ts(tbase + kPuO, tbase + kPuUl + 8 * kk, bd, ido, 1u);
+                    }
+                    umma_commit(bar_o);
+                }
+                __syncwarp();
+                issued = kt + 1;
+            }
+        }
+    }
+
+    // ---- every issued MMA has completed before TMEM is read or freed ----
+    if (warp == kPuMmaWarp) {
+        if (elect_one()) umma_commit(bar_fin);
+        __syncwarp();
+        const uint64_t tw = um_clock_ns();
+        while (!um_try(bar_fin, 0) && um_clock_ns() - tw < kTcWaitNs) {
+        }
+    }
+    (void)issued;
+    if (__syncthreads_or(aborted || *abort_flag)) {
+        aborted = true;
+    } else {
+        tc_fence_after();
+    }
+
+    if (!aborted) {
+        // ---- O' = (O 2^(R - m) + Z)/L of the row into shared memory (f32, rotated columns) ----
+        float *os = reinterpret_cast<float *>(smem);
+        if (warp < 4) {
+            const float inv = l_r > 0.0f ? 1.0f / l_r : 0.0f;
+            const float cu = exp2f(R_r - m_r) * inv, cz = z_r * inv;
+#pragma unroll 1
+            for (int c = 0; c < D; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(tl + kPuO + c, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    os[my_row * D + ((c + i + my_row) & (D - 1))] = fmaf(__uint_as_float(v[i]), cu, cz);
+            }
+        }
+        __syncthreads();
+        // ---- rotate back and store, one row per warp pass ----
+        for (int i = 0; i < kPuRows / kPuWarps; i++) {
+            const int row = warp * (kPuRows / kPuWarps) + i, gr = r0 + row;
+            if (gr >= nrows) break;
+            float x[EPL];
+#pragma unroll
+            for (int r = 0; r < EPL; r++) x[r] = os[row * D + ((lane * EPL + r + row) & (D - 1))];
+            warp_wht_butterfly<EPL>(x, lane, D);
+            const int s = gr / G, hd = gr % G;
+            T *dst = static_cast<T *>(a.out) + (((int64_t)b * a.seq_len + s) * (a.heads * G) + h * G + hd) * D;
+#pragma unroll
+            for (int r = 0; r < EPL; r++)
+                st_from_f32(dst + lane * EPL + r, x[r] * a.wht_scale * sg[lane * EPL + r]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tbase, kPuTmemCols);
+}
+
+template <typename T, int BITS, int D>
+int launch_shape(const AttendArgs &a, cudaStream_t stream) {
+    using GG = PuGeo<D>;
+    auto kern = prefill_umma_kernel<T, BITS, D>;
+    static int configured[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GG::SMEM);
+        if (e != cudaSuccess) return check_cuda(e, "gqa prefill (tcgen05) smem attribute");
+        if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
+    }
+    const int rows = a.seq_len * a.group;
+    const int64_t nblocks = (int64_t)((rows + kPuRows - 1) / kPuRows) * a.heads * a.batch;
+    if (nblocks > 0x7fffffff)
+        return set_error(SA_ERR_UNSUPPORTED, "gqa prefill (tcgen05): %lld blocks", (long long)nblocks);
+    kern<<<dim3((unsigned)nblocks), 32 * kPuWarps, GG::SMEM, stream>>>(a);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "gqa prefill (tcgen05) launch");
+}
+
+template <typename T>
+int launch_dtype(const AttendArgs &a, cudaStream_t stream) {
+    if (a.bits == 4 && a.head_dim == 128) return launch_shape<T, 4, 128>(a, stream);
+    if (a.bits == 8 && a.head_dim == 128) return launch_shape<T, 8, 128>(a, stream);
+    if (a.bits == 4 && a.head_dim == 64) return launch_shape<T, 4, 64>(a, stream);
+    return launch_shape<T, 8, 64>(a, stream);
+}
+
+}  // namespace
+
+int launch_gqa_prefill_umma(const AttendArgs &a, cudaStream_t stream) {
+    switch (a.dtype) {
+        case SA_DTYPE_FLOAT: return launch_dtype<float>(a, stream);
+        case SA_DTYPE_FLOAT16: return launch_dtype<__half>(a, stream);
+        default: return launch_dtype<__nv_bfloat16>(a, stream);
+    }
+}
+
+}  // namespace sa

@@ -42,6 +42,7 @@
 #include "sa_async.cuh"
 #include "sa_common.cuh"
 #include "sa_internal.h"
+#include "sa_tcgen05.cuh"
 #include "sa_tma.cuh"
 
 namespace sa {
@@ -73,68 +74,6 @@ struct UmGeo {
     static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 };
 
-// ---- tcgen05 wrappers ----------------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// D (f32, TMEM) (+)= A (16-bit, TMEM) * B^T (16-bit, shared memory descriptor)
-__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d),
-        "r"(a), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u)
-        : "memory");
-}
-
-// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15, %16};\n" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15}, [%16];\n"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
-
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte-swizzle
-// canonical layout: rows of 128 B, 8-row groups 1024 B apart (SBO), version 1,
-// layout type 2 (SWIZZLE_128B).  The tile base is 1024-byte aligned; a k step
-// of 16 elements inside the swizzle atom advances the start address by 32 B.
-__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
 // Instruction descriptor, kind::f16: D f32, A and B of type T (K-major), N = BN, M = 128.
 template <typename T, int BN>
 __host__ __device__ constexpr uint32_t umma_idesc() {
@@ -157,36 +96,10 @@ __device__ __forceinline__ float *map_to_rank0(float *p) {
     return reinterpret_cast<float *>(out);
 }
 
-// One lane of the (converged) warp: the lowest active lane.
-__device__ __forceinline__ bool elect_one() {
-    uint32_t pred = 0;
-    asm volatile(
-        "{\n.reg .b32 rx;\n.reg .pred px;\nelect.sync rx|px, 0xffffffff;\nselp.b32 %0, 1, 0, px;\n}\n"
-        : "=r"(pred));
-    return pred != 0;
-}
-
-// Bounded wait that also gives up when another role has aborted.  The
-// hand-offs between the roles are short, so the wait polls (try_wait without
-// a suspend hint) instead of sleeping; the bound is 2 s of %globaltimer.
-__device__ __forceinline__ bool um_try(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t um_clock_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-    return t;
-}
-
 constexpr uint64_t kUmWaitNs = 2000000000ull;
 
+// Bounded wait that also gives up when another role has aborted; the bound is
+// 2 s of %globaltimer.
 __device__ __forceinline__ bool um_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (um_try(bar, parity)) return true;
     const uint64_t t0 = um_clock_ns();

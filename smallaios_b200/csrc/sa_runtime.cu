@@ -557,7 +557,7 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         rc = launch_kv_append(ap, stream);
         if (rc != SA_OK) return rc;
     }
-    if (prefill_eligible(a)) return launch_gqa_prefill(a, stream);  // tensor-core prefill chunk
+    if (prefill_eligible(a)) return launch_gqa_prefill_umma(a, stream);  // tcgen05 prefill chunk
     // the generic kernels write attn_out; a head-sharded output is copied out after
     AttendArgs ga = a;
     ga.gather.n = 0;
