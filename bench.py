@@ -540,9 +540,9 @@ def run_prefill_attention(args):
     One step = one GroupQueryAttention call on a whole prompt per sequence
     (B = 8, S = 2048, 32 query / 8 KV heads, D = 128, int8 KV, theta 5e5):
     quantize-on-append of the 2048 tokens, then causal attention of the 2048
-    queries on the tensor-core prefill kernel.  Roofline: tensor (causal
+    queries on the tcgen05 prefill kernel.  Roofline: tensor (causal
     attention FLOPs 4*B*Hq*S*S/2*D against the measured bf16 peak; the kernel
-    computes in fp16 on mma.sync).
+    computes in fp16 with f32 accumulation, twice over for the hi + lo halves).
     """
     import torch
 
@@ -595,7 +595,7 @@ def run_prefill_attention(args):
         "metric": "prefill attention tokens/s (quantize-on-append + causal GQA of whole prompts), BASELINE config 4 shape",
         "value": b * s / (t_ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8-kv/bf16-act/fp16-mma/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
+        "dtype": "int8-kv/bf16-act/fp16-tcgen05/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
         "config": {"workload": "llama3-8b prefill attention, one layer (BASELINE config 4 shape)", "batch": b,
                    "prompt": s, "q_heads": hq, "kv_heads": hkv, "head_dim": d, "kv_bits": bits,
                    "launch": "host launches"},

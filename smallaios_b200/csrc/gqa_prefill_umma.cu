@@ -60,7 +60,7 @@ struct PuGeo {
     static constexpr int V_OFF = K_OFF + K_TILE;
     static constexpr int META_OFF = V_OFF + V_TILE;    // float4 per token
     static constexpr int QSUM_OFF = META_OFF + kPuTok * 16;
-    static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4;
+    static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4 + 16;  // + the tile's V-scale maxima
     static constexpr int SMEM = BAR_OFF + 64 + 1024;   // + slack to align the base to 1024 B
     static_assert(kPuRows * D * 4 <= K_OFF, "O' staging reuses the q' planes");
 };
@@ -84,6 +84,17 @@ __device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
 // Byte offset of 16-byte chunk c (0..7) of row r in a [rows][128 B] 128-byte-swizzle tile.
 __device__ __forceinline__ uint32_t sw_off(int r, int c) {
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Barrier of warps 4-7 (named barrier 1, 128 threads) returning the OR of `v` over them.
+__device__ __forceinline__ bool bar_or_4to7(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbarrier.cta.red.or.pred p, 1, 128, q;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
 }
 
 // Instruction descriptor, kind::f16: D f32, A and B fp16 (K-major), M = 128, N.
@@ -185,6 +196,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
         for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
         if (lane == 0) qsum[row] = sum;
     }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // q' planes -> the tensor core
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -209,34 +221,52 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
     const uint8_t *vc = a.v_codes + unit * a.capacity * (int64_t)CB;
     const float2 *kmeta = reinterpret_cast<const float2 *>(a.k_meta) + unit * a.capacity;
     const float2 *vmeta = reinterpret_cast<const float2 *>(a.v_meta) + unit * a.capacity;
+    float *vmax_w = qsum + kPuRows;  // [2]: the tile's largest V scale, per staging warp 4 / 5
 
     // running max m, the V reference R, sums of p and p * zp (rows of warps 0-3)
     float m_r = -INFINITY, R_r = -INFINITY, l_r = 0.0f, z_r = 0.0f;
-    int issued = 0;  // MMA warp: tiles whose PV MMAs were committed
     bool aborted = false;
-
-    for (int kt = 0; kt < ntiles; kt++) {
-        const int t0 = kt * kPuTok;
-        // the previous tile's MMAs have read the code tiles and U
-        bool ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
-        if (ok) {
-            if (tid < kPuTok) {
-                // tokens past every row's position are masked; zero their (possibly unwritten) metadata
-                float4 m4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (t0 + tid <= pos_last) {
-                    const float2 km = kmeta[t0 + tid], vm = vmeta[t0 + tid];
-                    m4 = make_float4(km.x, km.y, vm.x, vm.y);
-                }
-                meta[tid] = m4;
-            }
-            // K tile: token rows of CB code bytes, 16 bytes per uint4
-            for (int u = tid; u < kPuTok * CB / 16; u += 32 * kPuWarps) {
+    if (warp >= 4) {
+        // ================= staging warps 4-7 (warp 4 also issues the MMAs) =================
+        const int st = tid - 128;
+        constexpr int NR = CB / 32;  // 16-byte units of K (and of V) per thread per tile
+        uint4 rk[NR], rv[NR];
+        float2 rkm = make_float2(0.0f, 0.0f), rvm = make_float2(0.0f, 0.0f);
+        // raw codes and metadata of tile kt into registers (in flight while the softmax runs)
+        auto fetch = [&](int kt) {
+            const int t0 = kt * kPuTok;
+#pragma unroll
+            for (int i = 0; i < NR; i++) {
+                const int u = st + 128 * i;
                 const int tok = u / (CB / 16), ch = u % (CB / 16);
-                const uint4 w = *reinterpret_cast<const uint4 *>(kc + (int64_t)(t0 + tok) * CB + 16 * ch);
-                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                rk[i] = *reinterpret_cast<const uint4 *>(kc + (int64_t)(t0 + tok) * CB + 16 * ch);
+                const int blk = u / CB, rem = u % CB, c = rem / 4, gq = rem % 4;
+                rv[i] = *reinterpret_cast<const uint4 *>(vc + (int64_t)(t0 / 16) * 16 * CB + (int64_t)blk * 16 * CB +
+                                                        64 * c + 16 * gq);
+            }
+            if (st < kPuTok) {
+                // tokens past every row's position are masked; their (possibly unwritten) metadata is zeroed
+                const bool live = t0 + st <= pos_last;
+                rkm = live ? kmeta[t0 + st] : make_float2(0.0f, 0.0f);
+                rvm = live ? vmeta[t0 + st] : make_float2(0.0f, 0.0f);
+            }
+        };
+        // registers -> the fp16 tiles (128-byte swizzle) and the metadata in shared memory
+        auto stage = [&]() {
+            if (st < kPuTok) {
+                meta[st] = make_float4(rkm.x, rkm.y, rvm.x, rvm.y);
+                float vm = rvm.x;
+#pragma unroll
+                for (int m = 16; m >= 1; m >>= 1) vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, m));
+                if (lane == 0) vmax_w[st >> 5] = vm;
+            }
+#pragma unroll
+            for (int i = 0; i < NR; i++) {
+                const int u = st + 128 * i;
+                const int tok = u / (CB / 16), ch = u % (CB / 16);
+                const uint32_t wv[4] = {rk[i].x, rk[i].y, rk[i].z, rk[i].w};
                 if constexpr (BITS == 8) {
-                    // 16 dims 16ch.. : two 16-byte chunks of fp16
-                    const int e = 16 * ch;
+                    const int e = 16 * ch;  // dims e .. e + 15: two 16-byte chunks of fp16
                     unsigned char *blk = kt_s + (e >> 6) * GG::K_BLK;
                     const int c0 = (e & 63) >> 3;
 #pragma unroll
@@ -249,8 +279,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                         *reinterpret_cast<uint4 *>(blk + sw_off(tok, c0 + hlf)) = o;
                     }
                 } else {
-                    // 32 dims 32ch.. : four chunks; byte i holds dims 2i (low nibble), 2i + 1 (high)
-                    const int e = 32 * ch;
+                    const int e = 32 * ch;  // dims e .. e + 31; byte i holds dims 2i (low nibble), 2i + 1
                     unsigned char *blk = kt_s + (e >> 6) * GG::K_BLK;
                     const int c0 = (e & 63) >> 3;
 #pragma unroll
@@ -265,18 +294,13 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                         *reinterpret_cast<uint4 *>(blk + sw_off(tok, c0 + q)) = o;
                     }
                 }
-            }
-            // V tile: four 16-token blocks of 16*CB contiguous bytes; a uint4 is chunk c of token
-            // group gq of a block: bytes k = 4j + (token & 3) for j = 4c .. 4c+3
-            const uint8_t *vtile = vc + (int64_t)(t0 / 16) * 16 * CB;
-            for (int u = tid; u < kPuTok * CB / 16; u += 32 * kPuWarps) {
-                const int blk = u / CB, rem = u % CB, c = rem / 4, gq = rem % 4;
-                const uint4 w = *reinterpret_cast<const uint4 *>(vtile + (int64_t)blk * 16 * CB + 64 * c + 16 * gq);
-                const int tok0 = blk * 16 + 4 * gq;  // tokens tok0 .. tok0 + 3 of the tile
-                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                // V: chunk c of token group gq of 16-token block blk: byte 4c + jj of tokens tok0 .. tok0 + 3
+                const int blkv = u / CB, rem = u % CB, c = rem / 4, gq = rem % 4;
+                const int tok0 = blkv * 16 + 4 * gq;
+                const uint32_t vv[4] = {rv[i].x, rv[i].y, rv[i].z, rv[i].w};
 #pragma unroll
                 for (int jj = 0; jj < 4; jj++) {
-                    const uint32_t x = wv[jj];
+                    const uint32_t x = vv[jj];
                     if constexpr (BITS == 8) {
                         const int dim = 4 * c + jj;
                         uint2 o;
@@ -296,142 +320,148 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                     }
                 }
             }
-        }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged tiles -> the tensor core
-        if (__syncthreads_or(!ok || *abort_flag)) {
-            aborted = true;
-            break;
-        }
+        };
 
-        if (warp == kPuMmaWarp) {
-            // ---- S = (Q'hi + Q'lo).C_K^T ----
-            tc_fence_after();
-            if (elect_one()) {
-                constexpr uint32_t ids = pu_idesc(kPuTok);
-#pragma unroll
-                for (int pl = 0; pl < 2; pl++)
-#pragma unroll
-                    for (int kb = 0; kb < GG::KBLK; kb++)
-#pragma unroll
-                        for (int kk = 0; kk < 4; kk++) {
-                            const uint64_t ad = sw128_kmajor_desc(smem_u32((pl ? ql : qh) + kb * (kPuRows * 128)) + 32 * kk);
-                            const uint64_t bd = sw128_kmajor_desc(smem_u32(kt_s + kb * GG::K_BLK) + 32 * kk);
-                            umma_ss(tbase + kPuS, ad, bd, ids, (pl | kb | kk) != 0 ? 1u : 0u);
-                        }
-                umma_commit(bar_s);
+        fetch(0);
+        for (int kt = 0; kt < ntiles; kt++) {
+            // the previous tile's MMAs have read the code tiles and U
+            const bool ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+            if (ok) stage();
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged tiles -> the tensor core
+            if (bar_or_4to7(!ok || *abort_flag)) {  // one decision for warps 4-7
+                aborted = true;
+                break;
             }
-            __syncwarp();
+            if (warp == kPuMmaWarp) {
+                // ---- S = (Q'hi + Q'lo).C_K^T ----
+                tc_fence_after();
+                if (elect_one()) {
+                    constexpr uint32_t ids = pu_idesc(kPuTok);
+#pragma unroll
+                    for (int pl = 0; pl < 2; pl++)
+#pragma unroll
+                        for (int kb = 0; kb < GG::KBLK; kb++)
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++) {
+                                const uint64_t ad =
+                                    sw128_kmajor_desc(smem_u32((pl ? ql : qh) + kb * (kPuRows * 128)) + 32 * kk);
+                                const uint64_t bd = sw128_kmajor_desc(smem_u32(kt_s + kb * GG::K_BLK) + 32 * kk);
+                                umma_ss(tbase + kPuS, ad, bd, ids, (pl | kb | kk) != 0 ? 1u : 0u);
+                            }
+                    umma_commit(bar_s);
+                }
+                __syncwarp();
+            }
+            if (kt + 1 < ntiles) fetch(kt + 1);
+            if (warp == kPuMmaWarp) {
+                // ---- O += (Uhi + Ulo).C_V once the softmax has written U ----
+                bool uok = tc_wait(bar_u, (uint32_t)(kt & 1), abort_flag, a.dev_status);
+                uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
+                if (uok) {
+                    tc_fence_after();
+                    if (elect_one()) {
+                        constexpr uint32_t ido = pu_idesc(D);
+#pragma unroll
+                        for (int kk = 0; kk < kPuTok / 16; kk++) {
+                            const uint64_t bd = sw128_kmajor_desc(smem_u32(vt_s) + 32 * kk);
+                            umma_ts(tbase + kPuO, tbase + kPuUh + 8 * kk, bd, ido, (kt | kk) != 0 ? 1u : 0u);
+                            umma_ts(tbase + kPuO, tbase + kPuUl + 8 * kk, bd, ido, 1u);
+                        }
+                        umma_commit(bar_o);
+                    }
+                    __syncwarp();
+                }
+            }
         }
-
-        if (warp < 4) {
-            // ---- softmax of this thread's row ----
+        // every issued MMA has completed before TMEM is read or freed
+        if (warp == kPuMmaWarp) {
+            if (elect_one()) umma_commit(bar_fin);
+            __syncwarp();
+            const uint64_t tw = um_clock_ns();
+            while (!um_try(bar_fin, 0) && um_clock_ns() - tw < kTcWaitNs) {
+            }
+        }
+    } else {
+        // ================= softmax warps 0-3: one thread per row =================
+        for (int kt = 0; kt < ntiles; kt++) {
+            const int t0 = kt * kPuTok;
+            // S of this tile is complete (and with it every earlier MMA: O and U are free)
             bool sok = tc_wait(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
             sok = __all_sync(0xffffffffu, sok);
-            if (sok) {
-                tc_fence_after();
-                // pass 1: scores (scale / zero point per token, causal mask) and their maximum
-                float mx = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < kPuTok; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tl + kPuS + c, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float2 mt = *reinterpret_cast<const float2 *>(&meta[c + i]);
-                        const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
-                        mx = fmaxf(mx, t0 + c + i > pos_r ? -INFINITY : s);
-                    }
-                }
-                float vmax = 0.0f;
-                for (int t = 0; t < kPuTok; t++) vmax = fmaxf(vmax, meta[t].z);
-                const float lvmax = __log2f(fmaxf(vmax, 1.17549435e-38f));
-                const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
-                const float fac = exp2f(m_r - mn);
-                l_r *= fac;
-                z_r *= fac;
-                m_r = mn;
-                const float cand = mn + lvmax;
-                float ofac = 1.0f;
-                if (R_r == -INFINITY) {
-                    R_r = cand;  // first tile: O is still empty
-                } else if (cand > R_r + kPuLazy) {
-                    ofac = exp2f(R_r - cand);
-                    R_r = cand;
-                }
-                const float kr = exp2f(mn - R_r);
-                if (__any_sync(0xffffffffu, ofac != 1.0f)) {
-                    // rescale this warp's rows of O (the previous tile's MMAs have completed)
-#pragma unroll 1
-                    for (int c = 0; c < D; c += 16) {
-                        uint32_t v[16];
-                        tmem_ld16(tl + kPuO + c, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * ofac);
-                        tmem_st16(tl + kPuO + c, v);
-                    }
-                }
-                // pass 2: p, the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
-#pragma unroll 1
-                for (int c = 0; c < kPuTok; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tl + kPuS + c, v);
-                    tmem_wait_ld();
-                    uint32_t uh[8], ul[8];
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2) {
-                        const float4 m0 = meta[c + i], m1 = meta[c + i + 1];
-                        float s0 = fmaf(__uint_as_float(v[i]), m0.x, m0.y * qs_r);
-                        float s1 = fmaf(__uint_as_float(v[i + 1]), m1.x, m1.y * qs_r);
-                        if (t0 + c + i > pos_r) s0 = -INFINITY;
-                        if (t0 + c + i + 1 > pos_r) s1 = -INFINITY;
-                        const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
-                        l_r += p0 + p1;
-                        z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
-                        split_h2(p0 * m0.z * kr, p1 * m1.z * kr, uh[i / 2], ul[i / 2]);
-                    }
-                    tmem_st8(tl + kPuUh + c / 2, uh);
-                    tmem_st8(tl + kPuUl + c / 2, ul);
-                }
-                tmem_wait_st();
-                tc_fence_before();
+            if (!sok) {
+                aborted = true;
+                break;
             }
+            tc_fence_after();
+            // pass 1: scores (scale / zero point per token, causal mask) and their maximum
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kPuTok; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(tl + kPuS + c, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float2 mt = *reinterpret_cast<const float2 *>(&meta[c + i]);
+                    const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
+                    mx = fmaxf(mx, t0 + c + i > pos_r ? -INFINITY : s);
+                }
+            }
+            const float lvmax = __log2f(fmaxf(fmaxf(vmax_w[0], vmax_w[1]), 1.17549435e-38f));
+            const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
+            const float fac = exp2f(m_r - mn);
+            l_r *= fac;
+            z_r *= fac;
+            m_r = mn;
+            const float cand = mn + lvmax;
+            float ofac = 1.0f;
+            if (R_r == -INFINITY) {
+                R_r = cand;  // first tile: O is still empty
+            } else if (cand > R_r + kPuLazy) {
+                ofac = exp2f(R_r - cand);
+                R_r = cand;
+            }
+            const float kr = exp2f(mn - R_r);
+            if (__any_sync(0xffffffffu, ofac != 1.0f)) {
+                // rescale this warp's rows of O
+#pragma unroll 1
+                for (int c = 0; c < D; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tl + kPuO + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * ofac);
+                    tmem_st16(tl + kPuO + c, v);
+                }
+            }
+            // pass 2: p, the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
+#pragma unroll 1
+            for (int c = 0; c < kPuTok; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(tl + kPuS + c, v);
+                tmem_wait_ld();
+                uint32_t uh[8], ul[8];
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                    const float4 m0 = meta[c + i], m1 = meta[c + i + 1];
+                    float s0 = fmaf(__uint_as_float(v[i]), m0.x, m0.y * qs_r);
+                    float s1 = fmaf(__uint_as_float(v[i + 1]), m1.x, m1.y * qs_r);
+                    if (t0 + c + i > pos_r) s0 = -INFINITY;
+                    if (t0 + c + i + 1 > pos_r) s1 = -INFINITY;
+                    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
+                    l_r += p0 + p1;
+                    z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
+                    split_h2(p0 * m0.z * kr, p1 * m1.z * kr, uh[i / 2], ul[i / 2]);
+                }
+                tmem_st8(tl + kPuUh + c / 2, uh);
+                tmem_st8(tl + kPuUl + c / 2, ul);
+            }
+            tmem_wait_st();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_u);
         }
-
-        if (warp == kPuMmaWarp) {
-            // ---- O += (Uhi + Ulo).C_V ----
-            bool uok = tc_wait(bar_u, (uint32_t)(kt & 1), abort_flag, a.dev_status);
-            uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
-            if (uok) {
-                tc_fence_after();
-                if (elect_one()) {
-                    constexpr uint32_t ido = pu_idesc(D);
-#pragma unroll
-                    for (int kk = 0; kk < kPuTok / 16; kk++) {
-                        const uint64_t bd = sw128_kmajor_desc(smem_u32(vt_s) + 32 * kk);
-                        umma_ts(tbase + kPuO, tbase + kPuUh + 8 * kk, bd, ido, (kt | kk) != 0 ? 1u : 0u);
-                        umma_ts(tbase + kPuO, tbase + kPuUl + 8 * kk, bd, ido, 1u);
-                    }
-                    umma_commit(bar_o);
-                }
-                __syncwarp();
-                issued = kt + 1;
-            }
-        }
     }
-
-    // ---- every issued MMA has completed before TMEM is read or freed ----
-    if (warp == kPuMmaWarp) {
-        if (elect_one()) umma_commit(bar_fin);
-        __syncwarp();
-        const uint64_t tw = um_clock_ns();
-        while (!um_try(bar_fin, 0) && um_clock_ns() - tw < kTcWaitNs) {
-        }
-    }
-    (void)issued;
     if (__syncthreads_or(aborted || *abort_flag)) {
         aborted = true;
     } else {
