@@ -58,9 +58,9 @@ struct PuGeo {
     static constexpr int V_TILE = D * 128;             // [D dims][64 tokens]
     static constexpr int K_OFF = 2 * Q_PLANE;
     static constexpr int V_OFF = K_OFF + K_TILE;
-    static constexpr int META_OFF = V_OFF + V_TILE;    // float4 per token
-    static constexpr int QSUM_OFF = META_OFF + kPuTok * 16;
-    static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4 + 16;  // + the tile's V-scale maxima
+    static constexpr int META_OFF = V_OFF + V_TILE;    // [2 tiles][64 tokens] float4
+    static constexpr int QSUM_OFF = META_OFF + 2 * kPuTok * 16;
+    static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4 + 16;  // + the tiles' V-scale maxima [2][2]
     static constexpr int SMEM = BAR_OFF + 64 + 1024;   // + slack to align the base to 1024 B
     static_assert(kPuRows * D * 4 <= K_OFF, "O' staging reuses the q' planes");
 };
@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
     const uint8_t *vc = a.v_codes + unit * a.capacity * (int64_t)CB;
     const float2 *kmeta = reinterpret_cast<const float2 *>(a.k_meta) + unit * a.capacity;
     const float2 *vmeta = reinterpret_cast<const float2 *>(a.v_meta) + unit * a.capacity;
-    float *vmax_w = qsum + kPuRows;  // [2]: the tile's largest V scale, per staging warp 4 / 5
+    float *vmax_w = qsum + kPuRows;  // [2 tiles][2]: the tile's largest V scale, per staging warp 4 / 5
 
     // running max m, the V reference R, sums of p and p * zp (rows of warps 0-3)
     float m_r = -INFINITY, R_r = -INFINITY, l_r = 0.0f, z_r = 0.0f;
@@ -251,14 +251,14 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 rvm = live ? vmeta[t0 + st] : make_float2(0.0f, 0.0f);
             }
         };
-        // registers -> the fp16 tiles (128-byte swizzle) and the metadata in shared memory
-        auto stage = [&]() {
+        // registers -> the metadata (buffer mb) and the fp16 K tile (128-byte swizzle) in shared memory
+        auto stage_k = [&](int mb) {
             if (st < kPuTok) {
-                meta[st] = make_float4(rkm.x, rkm.y, rvm.x, rvm.y);
+                meta[mb * kPuTok + st] = make_float4(rkm.x, rkm.y, rvm.x, rvm.y);
                 float vm = rvm.x;
 #pragma unroll
                 for (int m = 16; m >= 1; m >>= 1) vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, m));
-                if (lane == 0) vmax_w[st >> 5] = vm;
+                if (lane == 0) vmax_w[2 * mb + (st >> 5)] = vm;
             }
 #pragma unroll
             for (int i = 0; i < NR; i++) {
@@ -294,6 +294,13 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                         *reinterpret_cast<uint4 *>(blk + sw_off(tok, c0 + q)) = o;
                     }
                 }
+            }
+        };
+        // registers -> the fp16 V tile ([dims][tokens], 128-byte swizzle)
+        auto stage_v = [&]() {
+#pragma unroll
+            for (int i = 0; i < NR; i++) {
+                const int u = st + 128 * i;
                 // V: chunk c of token group gq of 16-token block blk: byte 4c + jj of tokens tok0 .. tok0 + 3
                 const int blkv = u / CB, rem = u % CB, c = rem / 4, gq = rem % 4;
                 const int tok0 = blkv * 16 + 4 * gq;
@@ -322,55 +329,71 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
             }
         };
 
+        // O += (Uhi + Ulo).C_V of tile kt (the softmax has written U); elected lane of the MMA warp
+        auto issue_pv = [&](int kt) {
+            constexpr uint32_t ido = pu_idesc(D);
+#pragma unroll
+            for (int kk = 0; kk < kPuTok / 16; kk++) {
+                const uint64_t bd = sw128_kmajor_desc(smem_u32(vt_s) + 32 * kk);
+                umma_ts(tbase + kPuO, tbase + kPuUh + 8 * kk, bd, ido, (kt | kk) != 0 ? 1u : 0u);
+                umma_ts(tbase + kPuO, tbase + kPuUl + 8 * kk, bd, ido, 1u);
+            }
+            umma_commit(bar_o);
+        };
+        // S = (Q'hi + Q'lo).C_K^T of the staged K tile
+        auto issue_s = [&]() {
+            constexpr uint32_t ids = pu_idesc(kPuTok);
+#pragma unroll
+            for (int pl = 0; pl < 2; pl++)
+#pragma unroll
+                for (int kb = 0; kb < GG::KBLK; kb++)
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t ad = sw128_kmajor_desc(smem_u32((pl ? ql : qh) + kb * (kPuRows * 128)) + 32 * kk);
+                        const uint64_t bd = sw128_kmajor_desc(smem_u32(kt_s + kb * GG::K_BLK) + 32 * kk);
+                        umma_ss(tbase + kPuS, ad, bd, ids, (pl | kb | kk) != 0 ? 1u : 0u);
+                    }
+            umma_commit(bar_s);
+        };
+
         fetch(0);
         for (int kt = 0; kt < ntiles; kt++) {
-            // the previous tile's MMAs have read the code tiles and U
-            const bool ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
-            if (ok) stage();
+            // K tile and metadata of tile kt: S(kt-1) has read the K tile, and the softmax of
+            // tile kt-2 (metadata buffer kt & 1) finished before S(kt-1) was issued
+            bool ok = kt == 0 || tc_wait(bar_s, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+            if (ok) stage_k(kt & 1);
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged tiles -> the tensor core
             if (bar_or_4to7(!ok || *abort_flag)) {  // one decision for warps 4-7
                 aborted = true;
                 break;
             }
             if (warp == kPuMmaWarp) {
-                // ---- S = (Q'hi + Q'lo).C_K^T ----
-                tc_fence_after();
-                if (elect_one()) {
-                    constexpr uint32_t ids = pu_idesc(kPuTok);
-#pragma unroll
-                    for (int pl = 0; pl < 2; pl++)
-#pragma unroll
-                        for (int kb = 0; kb < GG::KBLK; kb++)
-#pragma unroll
-                            for (int kk = 0; kk < 4; kk++) {
-                                const uint64_t ad =
-                                    sw128_kmajor_desc(smem_u32((pl ? ql : qh) + kb * (kPuRows * 128)) + 32 * kk);
-                                const uint64_t bd = sw128_kmajor_desc(smem_u32(kt_s + kb * GG::K_BLK) + 32 * kk);
-                                umma_ss(tbase + kPuS, ad, bd, ids, (pl | kb | kk) != 0 ? 1u : 0u);
-                            }
-                    umma_commit(bar_s);
-                }
-                __syncwarp();
-            }
-            if (kt + 1 < ntiles) fetch(kt + 1);
-            if (warp == kPuMmaWarp) {
-                // ---- O += (Uhi + Ulo).C_V once the softmax has written U ----
-                bool uok = tc_wait(bar_u, (uint32_t)(kt & 1), abort_flag, a.dev_status);
+                // once the softmax of kt-1 has written U (and read S): PV(kt-1), then S(kt)
+                bool uok = kt == 0 || tc_wait(bar_u, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
                 uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
                 if (uok) {
                     tc_fence_after();
                     if (elect_one()) {
-                        constexpr uint32_t ido = pu_idesc(D);
-#pragma unroll
-                        for (int kk = 0; kk < kPuTok / 16; kk++) {
-                            const uint64_t bd = sw128_kmajor_desc(smem_u32(vt_s) + 32 * kk);
-                            umma_ts(tbase + kPuO, tbase + kPuUh + 8 * kk, bd, ido, (kt | kk) != 0 ? 1u : 0u);
-                            umma_ts(tbase + kPuO, tbase + kPuUl + 8 * kk, bd, ido, 1u);
-                        }
-                        umma_commit(bar_o);
+                        if (kt > 0) issue_pv(kt - 1);
+                        issue_s();
                     }
                     __syncwarp();
                 }
+            }
+            // V tile of kt: PV(kt-1) has read the V tile
+            ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+            if (ok) stage_v();
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            if (kt + 1 < ntiles) fetch(kt + 1);
+        }
+        // PV of the last tile, after every staging warp has written its V tile
+        if (!bar_or_4to7(aborted || *abort_flag) && warp == kPuMmaWarp) {
+            bool uok = tc_wait(bar_u, (uint32_t)((ntiles - 1) & 1), abort_flag, a.dev_status);
+            uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
+            if (uok) {
+                tc_fence_after();
+                if (elect_one()) issue_pv(ntiles - 1);
+                __syncwarp();
             }
         }
         // every issued MMA has completed before TMEM is read or freed
@@ -386,6 +409,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
         for (int kt = 0; kt < ntiles; kt++) {
             const int t0 = kt * kPuTok;
             // S of this tile is complete (and with it every earlier MMA: O and U are free)
+            const float4 *mtile = meta + (kt & 1) * kPuTok;
             bool sok = tc_wait(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
             sok = __all_sync(0xffffffffu, sok);
             if (!sok) {
@@ -402,12 +426,12 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
-                    const float2 mt = *reinterpret_cast<const float2 *>(&meta[c + i]);
+                    const float2 mt = *reinterpret_cast<const float2 *>(&mtile[c + i]);
                     const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
                     mx = fmaxf(mx, t0 + c + i > pos_r ? -INFINITY : s);
                 }
             }
-            const float lvmax = __log2f(fmaxf(fmaxf(vmax_w[0], vmax_w[1]), 1.17549435e-38f));
+            const float lvmax = __log2f(fmaxf(fmaxf(vmax_w[2 * (kt & 1)], vmax_w[2 * (kt & 1) + 1]), 1.17549435e-38f));
             const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
             const float fac = exp2f(m_r - mn);
             l_r *= fac;
@@ -443,7 +467,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 uint32_t uh[8], ul[8];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const float4 m0 = meta[c + i], m1 = meta[c + i + 1];
+                    const float4 m0 = mtile[c + i], m1 = mtile[c + i + 1];
                     float s0 = fmaf(__uint_as_float(v[i]), m0.x, m0.y * qs_r);
                     float s1 = fmaf(__uint_as_float(v[i + 1]), m1.x, m1.y * qs_r);
                     if (t0 + c + i > pos_r) s0 = -INFINITY;
