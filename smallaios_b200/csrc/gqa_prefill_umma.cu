@@ -560,6 +560,15 @@ int launch_dtype(const AttendArgs &a, cudaStream_t stream) {
 
 }  // namespace
 
+// Prefill chunks of 16 or more query tokens, 4/8-bit codes, head_dim 64/128,
+// group 1..8, output to attn_out (no head-sharded gather).
+bool prefill_eligible(const AttendArgs &a) {
+    if (a.seq_len < 16 || a.group < 1 || a.group > 8 || a.gather.n != 0) return false;
+    if ((a.bits != 4 && a.bits != 8) || (a.head_dim != 64 && a.head_dim != 128)) return false;
+    if (a.capacity % kPuTok != 0) return false;
+    return (int64_t)a.seq_len * a.group <= ((int64_t)1 << 30) && a.pos0 + a.seq_len <= ((int64_t)1 << 30);
+}
+
 int launch_gqa_prefill_umma(const AttendArgs &a, cudaStream_t stream) {
     switch (a.dtype) {
         case SA_DTYPE_FLOAT: return launch_dtype<float>(a, stream);

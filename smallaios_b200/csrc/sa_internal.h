@@ -134,7 +134,6 @@ size_t decode8_qprep_words();
 int launch_gqa_decode8(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 int launch_gqa_decode_fast(const AttendArgs &a, const AppendArgs *append, cudaStream_t stream);
 bool prefill_eligible(const AttendArgs &a);
-int launch_gqa_prefill(const AttendArgs &a, cudaStream_t stream);
 int launch_gqa_prefill_umma(const AttendArgs &a, cudaStream_t stream);
 int launch_matmul_nbits(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp,
                         const void *bias, void *y, int dtype, int64_t m, int64_t n, int64_t k,
