@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
         for (int kt = 0; kt < ntiles; kt++) {
             // K tile and metadata of tile kt: S(kt-1) has read the K tile, and the softmax of
             // tile kt-2 (metadata buffer kt & 1) finished before S(kt-1) was issued
-            bool ok = kt == 0 || tc_wait(bar_s, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+            bool ok = kt == 0 || tc_wait_sleep(bar_s, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
             if (ok) stage_k(kt & 1);
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged tiles -> the tensor core
             if (bar_or_4to7(!ok || *abort_flag)) {  // one decision for warps 4-7
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
             }
             if (warp == kPuMmaWarp) {
                 // once the softmax of kt-1 has written U (and read S): PV(kt-1), then S(kt)
-                bool uok = kt == 0 || tc_wait(bar_u, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+                bool uok = kt == 0 || tc_wait_sleep(bar_u, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
                 uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
                 if (uok) {
                     tc_fence_after();
@@ -381,14 +381,14 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 }
             }
             // V tile of kt: PV(kt-1) has read the V tile
-            ok = kt == 0 || tc_wait(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
+            ok = kt == 0 || tc_wait_sleep(bar_o, (uint32_t)((kt - 1) & 1), abort_flag, a.dev_status);
             if (ok) stage_v();
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             if (kt + 1 < ntiles) fetch(kt + 1);
         }
         // PV of the last tile, after every staging warp has written its V tile
         if (!bar_or_4to7(aborted || *abort_flag) && warp == kPuMmaWarp) {
-            bool uok = tc_wait(bar_u, (uint32_t)((ntiles - 1) & 1), abort_flag, a.dev_status);
+            bool uok = tc_wait_sleep(bar_u, (uint32_t)((ntiles - 1) & 1), abort_flag, a.dev_status);
             uok = __all_sync(0xffffffffu, uok) && !*abort_flag;
             if (uok) {
                 tc_fence_after();
@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
             const int t0 = kt * kPuTok;
             // S of this tile is complete (and with it every earlier MMA: O and U are free)
             const float4 *mtile = meta + (kt & 1) * kPuTok;
-            bool sok = tc_wait(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
+            bool sok = tc_wait_sleep(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
             sok = __all_sync(0xffffffffu, sok);
             if (!sok) {
                 aborted = true;

@@ -135,4 +135,25 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
+// The same bound, but the waiting thread sleeps (try_wait with a suspend-time
+// hint of 10 us; the hardware wakes it when the phase completes), so warps that
+// wait long take no issue slots from the warps that compute.
+__device__ __forceinline__ bool tc_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+    const uint64_t t0 = um_clock_ns();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(10000u)
+            : "memory");
+        if (ok) return true;
+        if (*abort_flag) return false;
+        if (um_clock_ns() - t0 > kTcWaitNs) break;
+    }
+    *abort_flag = 1;
+    if (status) atomicOr(status, 1);
+    return false;
+}
+
 }  // namespace sa
