@@ -33,6 +33,8 @@
 // flag and bit 0 of the cache's status word, every role leaves its loop, the
 // issued MMAs are waited for (bounded) and TMEM is freed; the output is then
 // not written.
+#include <type_traits>
+
 #include "sa_common.cuh"
 #include "sa_internal.h"
 #include "sa_tcgen05.cuh"
@@ -79,6 +81,14 @@ __device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
     const uint32_t biased = __byte_perm(x, 0x64646464u, sel);
     const __half2 v = __hsub2(*reinterpret_cast<const __half2 *>(&biased), __float2half2_rn(1024.0f));
     return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// 2^x by the MUFU instruction (ex2.approx.ftz: relative error near 2^-22, subnormal results
+// flushed to zero -- weights below 2^-126 of the row maximum)
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a [rows][128 B] 128-byte-swizzle tile.
@@ -417,69 +427,80 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 break;
             }
             tc_fence_after();
-            // pass 1: scores (scale / zero point per token, causal mask) and their maximum
-            float mx = -INFINITY;
+            // tiles that lie wholly at or before every row of the warp need no causal mask
+            const bool full = __all_sync(0xffffffffu, t0 + kPuTok - 1 <= pos_r);
+            auto softmax_tile = [&](auto masked) {
+                constexpr bool MASK = decltype(masked)::value;
+                // pass 1: scores (scale / zero point per token, causal mask) and their maximum
+                float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < kPuTok; c += 16) {
-                uint32_t v[16];
-                tmem_ld16(tl + kPuS + c, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float2 mt = *reinterpret_cast<const float2 *>(&mtile[c + i]);
-                    const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
-                    mx = fmaxf(mx, t0 + c + i > pos_r ? -INFINITY : s);
-                }
-            }
-            const float lvmax = __log2f(fmaxf(fmaxf(vmax_w[2 * (kt & 1)], vmax_w[2 * (kt & 1) + 1]), 1.17549435e-38f));
-            const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
-            const float fac = exp2f(m_r - mn);
-            l_r *= fac;
-            z_r *= fac;
-            m_r = mn;
-            const float cand = mn + lvmax;
-            float ofac = 1.0f;
-            if (R_r == -INFINITY) {
-                R_r = cand;  // first tile: O is still empty
-            } else if (cand > R_r + kPuLazy) {
-                ofac = exp2f(R_r - cand);
-                R_r = cand;
-            }
-            const float kr = exp2f(mn - R_r);
-            if (__any_sync(0xffffffffu, ofac != 1.0f)) {
-                // rescale this warp's rows of O
-#pragma unroll 1
-                for (int c = 0; c < D; c += 16) {
+                for (int c = 0; c < kPuTok; c += 16) {
                     uint32_t v[16];
-                    tmem_ld16(tl + kPuO + c, v);
+                    tmem_ld16(tl + kPuS + c, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * ofac);
-                    tmem_st16(tl + kPuO + c, v);
+                    for (int i = 0; i < 16; i++) {
+                        const float2 mt = *reinterpret_cast<const float2 *>(&mtile[c + i]);
+                        const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
+                        mx = fmaxf(mx, (MASK && t0 + c + i > pos_r) ? -INFINITY : s);
+                    }
                 }
-            }
-            // pass 2: p, the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
+                const float lvmax =
+                    __log2f(fmaxf(fmaxf(vmax_w[2 * (kt & 1)], vmax_w[2 * (kt & 1) + 1]), 1.17549435e-38f));
+                const float mn = fmaxf(m_r, mx);  // finite: every row sees token 0 in the first tile
+                const float fac = exp2f(m_r - mn);
+                l_r *= fac;
+                z_r *= fac;
+                m_r = mn;
+                const float cand = mn + lvmax;
+                float ofac = 1.0f;
+                if (R_r == -INFINITY) {
+                    R_r = cand;  // first tile: O is still empty
+                } else if (cand > R_r + kPuLazy) {
+                    ofac = exp2f(R_r - cand);
+                    R_r = cand;
+                }
+                const float kr = exp2f(mn - R_r);
+                if (__any_sync(0xffffffffu, ofac != 1.0f)) {
+                    // rescale this warp's rows of O
 #pragma unroll 1
-            for (int c = 0; c < kPuTok; c += 16) {
-                uint32_t v[16];
-                tmem_ld16(tl + kPuS + c, v);
-                tmem_wait_ld();
-                uint32_t uh[8], ul[8];
+                    for (int c = 0; c < D; c += 16) {
+                        uint32_t v[16];
+                        tmem_ld16(tl + kPuO + c, v);
+                        tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    const float4 m0 = mtile[c + i], m1 = mtile[c + i + 1];
-                    float s0 = fmaf(__uint_as_float(v[i]), m0.x, m0.y * qs_r);
-                    float s1 = fmaf(__uint_as_float(v[i + 1]), m1.x, m1.y * qs_r);
-                    if (t0 + c + i > pos_r) s0 = -INFINITY;
-                    if (t0 + c + i + 1 > pos_r) s1 = -INFINITY;
-                    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
-                    l_r += p0 + p1;
-                    z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
-                    split_h2(p0 * m0.z * kr, p1 * m1.z * kr, uh[i / 2], ul[i / 2]);
+                        for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * ofac);
+                        tmem_st16(tl + kPuO + c, v);
+                    }
                 }
-                tmem_st8(tl + kPuUh + c / 2, uh);
-                tmem_st8(tl + kPuUl + c / 2, ul);
-            }
+                // pass 2: p = 2^(s - m), the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
+#pragma unroll 1
+                for (int c = 0; c < kPuTok; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tl + kPuS + c, v);
+                    tmem_wait_ld();
+                    uint32_t uh[8], ul[8];
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        const float4 m0 = mtile[c + i], m1 = mtile[c + i + 1];
+                        // s - m = acc * kscale + (kzp * sum(q') - m)
+                        float e0 = fmaf(__uint_as_float(v[i]), m0.x, fmaf(m0.y, qs_r, -mn));
+                        float e1 = fmaf(__uint_as_float(v[i + 1]), m1.x, fmaf(m1.y, qs_r, -mn));
+                        if (MASK) {
+                            if (t0 + c + i > pos_r) e0 = -INFINITY;
+                            if (t0 + c + i + 1 > pos_r) e1 = -INFINITY;
+                        }
+                        const float p0 = ex2_ftz(e0), p1 = ex2_ftz(e1);
+                        l_r += p0 + p1;
+                        z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
+                        split_h2(p0 * (m0.z * kr), p1 * (m1.z * kr), uh[i / 2], ul[i / 2]);
+                    }
+                    tmem_st8(tl + kPuUh + c / 2, uh);
+                    tmem_st8(tl + kPuUl + c / 2, ul);
+                }
+            };
+            if (full) softmax_tile(std::false_type{});
+            else softmax_tile(std::true_type{});
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
