@@ -102,31 +102,60 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
     const float range = __fsub_rn(mx, mn);
     const float scale = range > 0.0f ? __fdiv_rn(range, (float)levels) : 1.0f;
     const float zp = mn;
+    uint32_t qc[EPL];  // the codes of this lane's elements
 #pragma unroll
     for (int r = 0; r < EPL; r++) {
-        if (active) {
-            uint32_t q = 0u;
-            if (scale > 0.0f) q = __float2uint_rz(rust_round_f32(__fdiv_rn(__fsub_rn(x[r], zp), scale)));
-            s_codes[lane * EPL + r] = (uint8_t)(q < levels ? q : levels);
-        }
+        uint32_t q = 0u;
+        if (active && scale > 0.0f) q = __float2uint_rz(rust_round_f32(__fdiv_rn(__fsub_rn(x[r], zp), scale)));
+        qc[r] = q < levels ? q : levels;
     }
-    __syncwarp();
 
     // pack_bits (kv_compression.rs:294-312): LSB-first contiguous bit stream.
     const int cb = a.code_bytes;
     const int64_t row = ((int64_t)b * a.heads + h);
-    for (int j = lane; j < cb; j += 32) {
-        uint32_t byte = 0;
+    uint8_t *kdst = a.k_codes + (row * a.capacity + pos) * cb;
+    uint8_t *vdst = a.v_codes + row * a.capacity * cb;
+    if (a.bits == 8 || (a.bits == 4 && EPL >= 2)) {
+        // 8 bits: byte e is element e; 4 bits: byte i is elements 2i (low nibble) and 2i + 1 --
+        // this lane's elements make whole bytes lane*NB .. lane*NB + NB - 1 (NB = EPL*bits/8)
+        uint64_t word = 0;
+        int nb;
+        if (a.bits == 8) {
 #pragma unroll
-        for (int bit = 0; bit < 8; bit++) {
-            const int g = 8 * j + bit;
-            const int e = g / a.bits, eb = g % a.bits;
-            if (e < d) byte |= ((uint32_t)(s_codes[e] >> eb) & 1u) << bit;
-        }
-        if (which == 0) {
-            a.k_codes[(row * a.capacity + pos) * cb + j] = (uint8_t)byte;
+            for (int r = 0; r < EPL; r++) word |= (uint64_t)qc[r] << (8 * r);
+            nb = EPL;
         } else {
-            a.v_codes[row * a.capacity * cb + v_byte_offset(pos, j, cb)] = (uint8_t)byte;
+#pragma unroll
+            for (int r = 0; r + 1 < EPL; r += 2) word |= (uint64_t)(qc[r] | (qc[r + 1] << 4)) << (4 * r);
+            nb = EPL / 2;
+        }
+        if (active) {
+            if (which == 0) {
+                uint8_t *dst = kdst + lane * nb;  // cb = 32 * nb: aligned to nb bytes
+                if (nb == 8) *reinterpret_cast<uint64_t *>(dst) = word;
+                else if (nb == 4) *reinterpret_cast<uint32_t *>(dst) = (uint32_t)word;
+                else if (nb == 2) *reinterpret_cast<uint16_t *>(dst) = (uint16_t)word;
+                else *dst = (uint8_t)word;
+            } else {
+                for (int i = 0; i < nb; i++) vdst[v_byte_offset(pos, lane * nb + i, cb)] = (uint8_t)(word >> (8 * i));
+            }
+        }
+    } else {
+        // 3 bits, or 4 bits with one element per lane: the bit stream through shared memory
+        if (active)
+#pragma unroll
+            for (int r = 0; r < EPL; r++) s_codes[lane * EPL + r] = (uint8_t)qc[r];
+        __syncwarp();
+        for (int j = lane; j < cb; j += 32) {
+            uint32_t byte = 0;
+#pragma unroll
+            for (int bit = 0; bit < 8; bit++) {
+                const int g = 8 * j + bit;
+                const int e = g / a.bits, eb = g % a.bits;
+                if (e < d) byte |= ((uint32_t)(s_codes[e] >> eb) & 1u) << bit;
+            }
+            if (which == 0) kdst[j] = (uint8_t)byte;
+            else vdst[v_byte_offset(pos, j, cb)] = (uint8_t)byte;
         }
     }
     if (lane == 0) {
@@ -144,7 +173,7 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
         float y[EPL];
 #pragma unroll
         for (int r = 0; r < EPL; r++)
-            y[r] = active ? __fadd_rn(__fmul_rn((float)s_codes[lane * EPL + r], scale), zp) : 0.0f;
+            y[r] = active ? __fadd_rn(__fmul_rn((float)qc[r], scale), zp) : 0.0f;
         warp_wht_butterfly<EPL>(y, lane, d);
         uint32_t pos_bits[EPL];  // bit l: element l * EPL + r of the residual is >= 0
 #pragma unroll
