@@ -153,58 +153,74 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
 
     // ---- q' of 16 rows per warp: RoPE, signs, WHT, * scale * log2 e / sqrt(n), as hi + lo fp16 ----
     const float qmul = a.wht_scale * a.scale * 1.4426950408889634f;
-    for (int i = 0; i < kPuRows / kPuWarps; i++) {
-        const int row = warp * (kPuRows / kPuWarps) + i, gr = r0 + row;
-        float x[EPL];
-        if (gr < nrows) {
-            const int s = gr / G, hd = gr % G;
+    constexpr int RB = 4;  // rows whose global loads are in flight together
+    for (int i0 = 0; i0 < kPuRows / kPuWarps; i0 += RB) {
+        // loads of RB rows: the elements, their rotary partners and the cos / sin entries
+        float xv[RB][EPL], xo[RB][EPL], cv[RB][EPL], sv[RB][EPL];
+#pragma unroll
+        for (int j = 0; j < RB; j++) {
+            const int gr = r0 + warp * (kPuRows / kPuWarps) + i0 + j;
+            const bool live = gr < nrows;
+            const int s = live ? gr / G : 0, hd = live ? gr % G : 0;
             const T *src = static_cast<const T *>(a.query) +
                            (((int64_t)b * a.seq_len + s) * (a.heads * G) + h * G + hd) * D;
             const int64_t pos = a.pos0 + s;
 #pragma unroll
             for (int r = 0; r < EPL; r++) {
                 const int e = lane * EPL + r;
-                x[r] = ld_f32(src + e);
-                if (a.do_rotary) {
+                xv[j][r] = live ? ld_f32(src + e) : 0.0f;
+                cv[j][r] = 1.0f;
+                sv[j][r] = 0.0f;
+                xo[j][r] = 0.0f;
+                if (a.do_rotary && live) {
                     const int half = D / 2;
                     int pair, partner;
-                    bool first;
                     if (a.interleaved) {
                         pair = e >> 1;
-                        first = (e & 1) == 0;
-                        partner = first ? e + 1 : e - 1;
+                        partner = (e & 1) == 0 ? e + 1 : e - 1;
                     } else {
-                        first = e < half;
-                        pair = first ? e : e - half;
-                        partner = first ? e + half : e - half;
+                        pair = e < half ? e : e - half;
+                        partner = e < half ? e + half : e - half;
                     }
-                    const float c = a.cos_cache[pos * half + pair], sn = a.sin_cache[pos * half + pair];
-                    const float xo = ld_f32(src + partner);
-                    x[r] = first ? __fsub_rn(__fmul_rn(c, x[r]), __fmul_rn(sn, xo))
-                                 : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x[r]));
+                    cv[j][r] = a.cos_cache[pos * half + pair];
+                    sv[j][r] = a.sin_cache[pos * half + pair];
+                    xo[j][r] = ld_f32(src + partner);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < RB; j++) {
+            const int row = warp * (kPuRows / kPuWarps) + i0 + j;
+            float x[EPL];
+#pragma unroll
+            for (int r = 0; r < EPL; r++) {
+                const int e = lane * EPL + r;
+                x[r] = xv[j][r];
+                if (a.do_rotary) {
+                    const bool first = a.interleaved ? (e & 1) == 0 : e < D / 2;
+                    x[r] = first ? __fsub_rn(__fmul_rn(cv[j][r], x[r]), __fmul_rn(sv[j][r], xo[j][r]))
+                                 : __fadd_rn(__fmul_rn(sv[j][r], xo[j][r]), __fmul_rn(cv[j][r], x[r]));
                 }
                 x[r] *= sg[e];
             }
-        } else {
+            warp_wht_butterfly<EPL>(x, lane, D);
+            float sum = 0.0f;
 #pragma unroll
-            for (int r = 0; r < EPL; r++) x[r] = 0.0f;
+            for (int r = 0; r < EPL; r += 2) {
+                const int e = lane * EPL + r;
+                const float x0 = x[r] * qmul, x1 = x[r + 1] * qmul;
+                sum += x0 + x1;
+                uint32_t hi, lo;
+                split_h2(x0, x1, hi, lo);
+                const uint32_t off =
+                    (uint32_t)((e >> 6) * (kPuRows * 128)) + sw_off(row, (e & 63) >> 3) + (e & 7) * 2;
+                *reinterpret_cast<uint32_t *>(qh + off) = hi;
+                *reinterpret_cast<uint32_t *>(ql + off) = lo;
+            }
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+            if (lane == 0) qsum[row] = sum;
         }
-        warp_wht_butterfly<EPL>(x, lane, D);
-        float sum = 0.0f;
-#pragma unroll
-        for (int r = 0; r < EPL; r += 2) {
-            const int e = lane * EPL + r;
-            const float x0 = x[r] * qmul, x1 = x[r + 1] * qmul;
-            sum += x0 + x1;
-            uint32_t hi, lo;
-            split_h2(x0, x1, hi, lo);
-            const uint32_t off = (uint32_t)((e >> 6) * (kPuRows * 128)) + sw_off(row, (e & 63) >> 3) + (e & 7) * 2;
-            *reinterpret_cast<uint32_t *>(qh + off) = hi;
-            *reinterpret_cast<uint32_t *>(ql + off) = lo;
-        }
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
-        if (lane == 0) qsum[row] = sum;
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // q' planes -> the tensor core
     tc_fence_before();
