@@ -450,12 +450,13 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                 // pass 1: scores (scale / zero point per token, causal mask) and their maximum
                 float mx = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < kPuTok; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tl + kPuS + c, v);
+                for (int c = 0; c < kPuTok; c += 32) {
+                    uint32_t v[32];  // two loads in flight per wait
+                    tmem_ld16(tl + kPuS + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+                    tmem_ld16(tl + kPuS + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
+                    for (int i = 0; i < 32; i++) {
                         const float2 mt = *reinterpret_cast<const float2 *>(&mtile[c + i]);
                         const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
                         mx = fmaxf(mx, (MASK && t0 + c + i > pos_r) ? -INFINITY : s);
