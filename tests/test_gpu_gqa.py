@@ -176,6 +176,15 @@ def test_prefill_whole_prompt_half(cuda_device, dtype):
     _check(got, want, dtype)
 
 
+@pytest.mark.parametrize("d,hq,hkv,bits", [(64, 6, 2, 4), (128, 10, 2, 8), (64, 12, 2, 8), (128, 14, 2, 4)])
+def test_prefill_groups_not_dividing_the_row_block(cuda_device, d, hq, hkv, bits):
+    """Groups 3, 5, 6 and 7: a 128-row block ends inside a position, so one position's heads are
+    split between two CTAs; a 150-token chunk after 40 cached tokens."""
+    got, want = _decode_case(cuda_device, b=2, hq=hq, hkv=hkv, d=d, bits=bits, t=190, s=150, seed=d + hq,
+                             chunks=(40,))
+    _check(got, want, torch.float32)
+
+
 def test_prefill_long_sharp_softmax(cuda_device):
     """A 1100-token prompt (18 KV tiles, the running max and V reference moving across tiles)
     with wide activations (std 3), so the softmax is peaked and scores span a large range."""
