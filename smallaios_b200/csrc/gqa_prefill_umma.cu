@@ -14,12 +14,15 @@
 // One CTA of 8 warps takes 128 query rows -- 128/G positions times the G query
 // heads of one KV head -- as the MMA's M = 128 (one TMEM lane per row), and
 // walks the causal range of the cache in tiles of 64 tokens:
-//   all warps  stage the tile: K and V codes as fp16 into shared memory in the
-//              128-byte-swizzle K-major layout the MMA reads, and the tile's
-//              {k scale, k zp, v scale, v zp};
-//   warp 4     one elected lane issues S = (Q'hi + Q'lo).C_K^T (A and B from
-//              shared memory, D = f32 in TMEM, N = 64) and, once the softmax
-//              has written U, O += (Uhi + Ulo).C_V (A from TMEM, N = D);
+//   warps 4-7  stage the tiles: K and V codes as fp16 into shared memory in the
+//              128-byte-swizzle K-major layout the MMA reads (K once S(kt-1)
+//              has read the previous one, V once PV(kt-1) has), and the tile's
+//              {k scale, k zp, v scale, v zp}; the next tile's codes are loaded
+//              into registers while the softmax runs;
+//   warp 4     one elected lane issues, once the softmax of tile kt-1 has
+//              written U, O += (Uhi + Ulo).C_V of kt-1 (A from TMEM, N = D) and
+//              then S = (Q'hi + Q'lo).C_K^T of kt (A and B from shared memory,
+//              D = f32 in TMEM, N = 64);
 //   warps 0-3  one thread per row: tcgen05.ld of its 64 scores, per-token
 //              scale / zero point, causal mask, online softmax in base 2, U
 //              into TMEM (tcgen05.st).  The V reference R (u <= 2^8) moves
