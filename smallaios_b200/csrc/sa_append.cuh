@@ -11,6 +11,13 @@
 
 namespace sa {
 
+// Signed-integer key with the order of the (non-NaN) float x: non-negative floats keep their
+// bits, negative ones flip the magnitude bits.
+__device__ __forceinline__ int order_key(float x) {
+    const int i = __float_as_int(x);
+    return i >= 0 ? i : (i ^ 0x7fffffff);
+}
+
 // RoPE of element e of a vector at `pos` (rotate_rope_block,
 // ops/microsoft.rs:137-160): y0 = c*x0 - s*x1, y1 = s*x0 + c*x1, each product
 // rounded before the add.  `x` is element e, `src` the whole input vector.
@@ -82,20 +89,18 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
             }
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float omn = __shfl_xor_sync(0xffffffffu, mn, o);
-        const int oimn = __shfl_xor_sync(0xffffffffu, imn, o);
-        const float omx = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int oimx = __shfl_xor_sync(0xffffffffu, imx, o);
-        if (omn < mn || (omn == mn && oimn < imn)) {
-            mn = omn;
-            imn = oimn;
-        }
-        if (omx > mx || (omx == mx && oimx < imx)) {
-            mx = omx;
-            imx = oimx;
-        }
+    // Across the warp: the extreme value by an integer reduction over an order-preserving key
+    // (-0 and +0 share the key of +0, since they compare equal), then the lowest element index
+    // among the lanes holding that value, and that element's own bits.
+    {
+        const int kmn = __reduce_min_sync(0xffffffffu, order_key(mn + 0.0f));
+        const int kmx = __reduce_max_sync(0xffffffffu, order_key(mx + 0.0f));
+        const int wmn = __reduce_min_sync(0xffffffffu, order_key(mn + 0.0f) == kmn ? imn : 0x7fffffff);
+        const int wmx = __reduce_min_sync(0xffffffffu, order_key(mx + 0.0f) == kmx ? imx : 0x7fffffff);
+        const unsigned lmn = __ballot_sync(0xffffffffu, order_key(mn + 0.0f) == kmn && imn == wmn);
+        const unsigned lmx = __ballot_sync(0xffffffffu, order_key(mx + 0.0f) == kmx && imx == wmx);
+        mn = __shfl_sync(0xffffffffu, mn, __ffs(lmn) - 1);
+        mx = __shfl_sync(0xffffffffu, mx, __ffs(lmx) - 1);
     }
 
     const uint32_t levels = (1u << a.bits) - 1u;
