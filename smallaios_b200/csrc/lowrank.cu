@@ -17,7 +17,8 @@
 //  - lowrank_attend_kernel: attention with keys read as read_k returns them
 //    (:870-882): k_t = U*S[t] * V^T, so q . k_t = U*S[t] * (q . V^T); values
 //    from the PolarQuant codes, accumulated in the rotated domain and rotated
-//    back once.  One warp per query row.
+//    back once.  One block of four warps per query row, each warp every fourth
+//    token.
 #include "sa_append.cuh"
 
 namespace sa {
@@ -154,13 +155,15 @@ __device__ __forceinline__ uint32_t lr_v_code(const uint8_t *vc, int64_t t, int 
     return (w >> sh) & ((1u << bits) - 1u);
 }
 
-// grid ceil(B * S * Hq / kLrAttWarps), one warp per (row, query token, query head).
+// grid B * S * Hq blocks, one per (row, query token, query head); the block's kLrAttWarps warps
+// take every kLrAttWarps-th token and their sums are added at the end.
 template <typename T, int EPL>
 __global__ void __launch_bounds__(32 * kLrAttWarps) lowrank_attend_kernel(AttendArgs a) {
+    __shared__ float s_red[kLrAttWarps];
+    __shared__ float s_acc[kLrAttWarps][256];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int d = a.head_dim, G = a.group, hq_all = a.heads * G;
-    const int64_t qi = (int64_t)blockIdx.x * kLrAttWarps + warp;
-    if (qi >= (int64_t)a.batch * a.seq_len * hq_all) return;
+    const int64_t qi = blockIdx.x;
     const int hq = (int)(qi % hq_all);
     const int s = (int)((qi / hq_all) % a.seq_len);
     const int b = (int)(qi / ((int64_t)hq_all * a.seq_len));
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(32 * kLrAttWarps) lowrank_attend_kernel(Attend
     const float *vt = a.lr_vt + unit * d;
     const float *us = a.lr_us + unit * a.capacity;
 
-    // q (RoPE at its position) . V^T
+    // q (RoPE at its position) . V^T (every warp computes it)
     float qv = 0.0f;
     if (active) {
 #pragma unroll
@@ -189,11 +192,16 @@ __global__ void __launch_bounds__(32 * kLrAttWarps) lowrank_attend_kernel(Attend
     const float c = qv * a.scale * 1.4426950408889634f;  // score of token t, base 2: U*S[t] * c
 
     float mx = -INFINITY;
-    for (int64_t t = lane; t <= pos; t += 32) mx = fmaxf(mx, us[t] * c);
+    for (int64_t t = threadIdx.x; t <= pos; t += 32 * kLrAttWarps) mx = fmaxf(mx, us[t] * c);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kLrAttWarps; w++) mx = fmaxf(mx, s_red[w]);
 
-    // sum_t p_t (code * scale + zp) in the rotated domain; lanes own EPL dimensions
+    // sum_t p_t (code * scale + zp) in the rotated domain; lanes own EPL dimensions, this warp
+    // every kLrAttWarps-th token
     const int cb = a.code_bytes;
     const uint8_t *vc = a.v_codes + unit * a.capacity * (int64_t)cb;
     const float2 *vm = reinterpret_cast<const float2 *>(a.v_meta) + unit * a.capacity;
@@ -201,7 +209,7 @@ __global__ void __launch_bounds__(32 * kLrAttWarps) lowrank_attend_kernel(Attend
 #pragma unroll
     for (int r = 0; r < EPL; r++) acc[r] = 0.0f;
     float l = 0.0f;
-    for (int64_t t = 0; t <= pos; t++) {
+    for (int64_t t = warp; t <= pos; t += kLrAttWarps) {
         const float p = exp2f(us[t] * c - mx);
         const float2 m = vm[t];
         l += p;
@@ -213,10 +221,28 @@ __global__ void __launch_bounds__(32 * kLrAttWarps) lowrank_attend_kernel(Attend
             }
         }
     }
-    float x[EPL];
-    const float inv = 1.0f / l;  // l >= 1: the maximum term is exp2(0)
+    __syncthreads();  // s_red is read: reuse it for the weight sums
+    if (lane == 0) s_red[warp] = l;
+    if (active) {
 #pragma unroll
-    for (int r = 0; r < EPL; r++) x[r] = active ? acc[r] * inv : 0.0f;
+        for (int r = 0; r < EPL; r++) s_acc[warp][lane * EPL + r] = acc[r];
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float lt = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kLrAttWarps; w++) lt += s_red[w];
+    const float inv = 1.0f / lt;  // lt >= 1: the maximum term is exp2(0)
+    float x[EPL];
+#pragma unroll
+    for (int r = 0; r < EPL; r++) {
+        float v = 0.0f;
+        if (active) {
+#pragma unroll
+            for (int w = 0; w < kLrAttWarps; w++) v += s_acc[w][lane * EPL + r];
+        }
+        x[r] = v * inv;
+    }
     warp_wht_butterfly<EPL>(x, lane, d);
     if (active) {
         T *dst = static_cast<T *>(a.out) + row * d;
@@ -239,7 +265,7 @@ int append_t(const AppendArgs &a, cudaStream_t stream) {
 template <typename T>
 int attend_t(const AttendArgs &a, cudaStream_t stream) {
     const int64_t n = (int64_t)a.batch * a.seq_len * a.heads * a.group;
-    const int64_t blocks = (n + kLrAttWarps - 1) / kLrAttWarps;
+    const int64_t blocks = n;  // one block per query row
     if (blocks > 0x7fffffff) return set_error(SA_ERR_UNSUPPORTED, "lowrank attend: %lld queries", (long long)n);
     const dim3 grid((unsigned)blocks), block(32 * kLrAttWarps);
     switch (a.head_dim) {
