@@ -110,8 +110,11 @@ uint64_t sa_kernel_launches(void);
  *   lr_us  float [B][H][T]   U*S, one coefficient per written row
  * read_k then returns the reconstruction lr_us[t] * lr_vt (:862-886), so
  * attention on such a cache scores keys as lr_us[t] * (q . lr_vt); V still
- * comes from the PolarQuant codes.  The state follows writes in position
- * order from 0; rewinding below a re-decomposition point is not supported.
+ * comes from the PolarQuant codes.  The attention kernels get this from the
+ * same identity they use for the codes, q.k = scale*(q'.c) + zp*sum(q'):
+ * with {scale 0, zp lr_us[t]} as K metadata (lr_kmeta) and q'.lr_vtr in
+ * place of sum(q').  The state follows writes in position order from 0;
+ * rewinding below a re-decomposition point is not supported.
  * ====================================================================== */
 typedef struct sa_kv_cache sa_kv_cache;
 
@@ -150,6 +153,8 @@ typedef struct sa_kv_layer_view {
     float *v_qjl_mag;
     float *lr_vt;              /* low-rank K state, NULL unless lowrank_k (attention then uses it) */
     float *lr_us;
+    float *lr_kmeta;           /* [B][H][T][2] {0, lr_us[t]}: the K metadata attention reads */
+    float *lr_vtr;             /* [B][H][D] lr_vt rotated like the queries (signs, WHT, 1/sqrt(n)) */
 } sa_kv_layer_view;
 
 /* GpuKvCache::allocate (kv_cache.rs:129-193) + CompressedKVCache::new

@@ -78,6 +78,8 @@ class KvLayerView(ctypes.Structure):
         ("v_qjl_mag", ctypes.c_void_p),
         ("lr_vt", ctypes.c_void_p),
         ("lr_us", ctypes.c_void_p),
+        ("lr_kmeta", ctypes.c_void_p),
+        ("lr_vtr", ctypes.c_void_p),
     ]
 
 

@@ -119,9 +119,10 @@ __global__ void __launch_bounds__(32 * kWarps) attend_split_kernel(AttendArgs a,
         float part = 0.0f;
         if (lane * EPL < d) {
 #pragma unroll
+            const float *vtr = a.lr_vtr ? a.lr_vtr + ((int64_t)b * a.heads + h) * d : nullptr;
             for (int r = 0; r < EPL; r++) {
                 s_q[g * d + lane * EPL + r] = x[r];
-                part += x[r];
+                part += vtr ? x[r] * vtr[lane * EPL + r] : x[r];  // sum(q'), or q'.V^T with low-rank K
             }
         }
         part = warp_sum(part);
@@ -531,11 +532,10 @@ extern "C" int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t pas
     a.cache_rows = cache_rows;
     a.do_rotary = do_rotary ? 1 : 0;
     a.interleaved = rotary_interleaved ? 1 : 0;
-    if (v.lr_us && v.lr_vt) {
-        // low-rank K: one pass per query, no split-K scratch
-        a.lr_vt = v.lr_vt;
-        a.lr_us = v.lr_us;
-        return launch_lowrank_attend(a, static_cast<cudaStream_t>(stream));
+    if (v.lr_kmeta && v.lr_vtr) {
+        // low-rank K: {0, U*S[t]} metadata and the rotated V^T
+        a.k_meta = v.lr_kmeta;
+        a.lr_vtr = v.lr_vtr;
     }
 
     StaticScratchSlot slot;

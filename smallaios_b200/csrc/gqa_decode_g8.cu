@@ -104,11 +104,12 @@ __global__ void __launch_bounds__(320) decode_prep8_kernel(AttendArgs a, AppendA
         }
         warp_wht_butterfly<EPL>(x, lane, D);
         float mabs = 0.0f;
+        const float *vtr = a.lr_vtr ? a.lr_vtr + bh * D : nullptr;
 #pragma unroll
         for (int r = 0; r < EPL; r++) {
             x[r] *= a.wht_scale;
             s_q[g][lane * EPL + r] = x[r];
-            sum += x[r];
+            sum += vtr ? x[r] * vtr[lane * EPL + r] : x[r];  // sum(q'), or q'.V^T with low-rank K
             mabs = fmaxf(mabs, fabsf(x[r]));
         }
         sum = warp_sum(sum);

@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
 
     // ---- q' of 16 rows per warp: RoPE, signs, WHT, * scale * log2 e / sqrt(n), as hi + lo fp16 ----
     const float qmul = a.wht_scale * a.scale * 1.4426950408889634f;
+    const float *vtr = a.lr_vtr ? a.lr_vtr + unit * D : nullptr;
     constexpr int RB = 4;  // rows whose global loads are in flight together
     for (int i0 = 0; i0 < kPuRows / kPuWarps; i0 += RB) {
         // loads of RB rows: the elements, their rotary partners and the cos / sin entries
@@ -212,7 +213,8 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
             for (int r = 0; r < EPL; r += 2) {
                 const int e = lane * EPL + r;
                 const float x0 = x[r] * qmul, x1 = x[r + 1] * qmul;
-                sum += x0 + x1;
+                // sum(q'), or q'.V^T with low-rank K
+                sum += vtr ? fmaf(x0, vtr[e], x1 * vtr[e + 1]) : x0 + x1;
                 uint32_t hi, lo;
                 split_h2(x0, x1, hi, lo);
                 const uint32_t off =

@@ -66,6 +66,8 @@ struct kv_cache_impl {
     float *lr_vt;              // [L][B][H][D], nullptr unless cfg.lowrank_k
     float *lr_us;              // [L][B][H][T]
     float *lr_scratch;         // [L][B][H][T]: the power iteration's u vector
+    float *lr_kmeta;           // [L][B][H][T][2]: {0, U*S[t]}, the K metadata attention reads
+    float *lr_vtr;             // [L][B][H][D]: V^T rotated like q' (signs, WHT, 1/sqrt(n))
     size_t layer_lr_vt_floats; // B*H*D
     size_t layer_lr_us_floats; // B*H*T
 };
@@ -87,7 +89,7 @@ struct AppendArgs {
     uint8_t *k_qjl_bits, *v_qjl_bits;
     float *k_qjl_mag, *v_qjl_mag;
     // low-rank K state (all nullptr: off)
-    float *lr_vt, *lr_us, *lr_scratch;
+    float *lr_vt, *lr_us, *lr_scratch, *lr_kmeta, *lr_vtr;
 };
 
 // Parameters of the fused QKV projection's epilogue (one token per row):
@@ -118,12 +120,13 @@ struct AttendArgs {
     uint32_t *qprep;  // decode prep area: per (row, head) q-digit fragments + constants
     int *dev_status;  // device-side status word (bounded waits that gave up)
     GatherOut gather;  // head-sharded output (n = 0: write `out`)
-    const float *lr_vt, *lr_us;  // low-rank K (nullptr: keys from the codes)
+    // low-rank K: V^T rotated like q' (nullptr: off).  With it, k_meta holds {0, U*S[t]} and the
+    // zero-point term's sum(q') becomes q'.lr_vtr, so scores are U*S[t] * (q . V^T).
+    const float *lr_vtr;
 };
 
 int launch_kv_append(const AppendArgs &a, cudaStream_t stream);
 int launch_lowrank_append(const AppendArgs &a, cudaStream_t stream);
-int launch_lowrank_attend(const AttendArgs &a, cudaStream_t stream);
 int launch_gqa_attend(const AttendArgs &a, cudaStream_t stream);
 int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream);
 bool decode_fast_eligible(const AttendArgs &a);

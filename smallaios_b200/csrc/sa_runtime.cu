@@ -167,7 +167,7 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
     k->layer_lr_us_floats = c.lowrank_k > 0 ? B * H * T : 0;
     const size_t lr_vt = up(L * k->layer_lr_vt_floats * sizeof(float));
     const size_t lr_us = up(L * k->layer_lr_us_floats * sizeof(float));
-    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st + 2 * qjl_bits + 2 * qjl_mag + lr_vt + 2 * lr_us;
+    k->base_bytes = 2 * codes + 2 * meta + signs + ws + qp + st + 2 * qjl_bits + 2 * qjl_mag + 2 * lr_vt + 4 * lr_us;
     const size_t k_bytes = k->base_bytes;
     cudaError_t e = cudaMalloc(&k->base, k->base_bytes);
     if (e != cudaSuccess) {
@@ -209,6 +209,10 @@ int sa_kv_cache_create(const sa_kv_cache_config *cfg, sa_kv_cache **out) {
         k->lr_us = reinterpret_cast<float *>(p);
         p += lr_us;
         k->lr_scratch = reinterpret_cast<float *>(p);
+        p += lr_us;
+        k->lr_kmeta = reinterpret_cast<float *>(p);  // two floats per row: 2 * lr_us bytes
+        p += 2 * lr_us;
+        k->lr_vtr = reinterpret_cast<float *>(p);
     }
     // Zero-initialise like GpuKvCache::allocate (kv_cache.rs:171-175).
     e = cudaMemset(k->base, 0, k->base_bytes);
@@ -367,6 +371,8 @@ int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_
     const bool lr = k->lr_vt != nullptr;
     v->lr_vt = lr ? k->lr_vt + (size_t)layer * k->layer_lr_vt_floats : nullptr;
     v->lr_us = lr ? k->lr_us + (size_t)layer * k->layer_lr_us_floats : nullptr;
+    v->lr_kmeta = lr ? k->lr_kmeta + (size_t)layer * 2 * k->layer_lr_us_floats : nullptr;
+    v->lr_vtr = lr ? k->lr_vtr + (size_t)layer * k->layer_lr_vt_floats : nullptr;
     const bool qjl = k->k_qjl_bits != nullptr;
     v->k_qjl_bits = qjl ? k->k_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
     v->v_qjl_bits = qjl ? k->v_qjl_bits + (size_t)layer * k->layer_qjl_bytes : nullptr;
@@ -436,6 +442,8 @@ int sa_kv_append(sa_kv_cache *cache, int32_t layer, const void *key, const void 
     a.lr_vt = v.lr_vt;
     a.lr_us = v.lr_us;
     a.lr_scratch = lr_scratch_of(k, layer);
+    a.lr_kmeta = v.lr_kmeta;
+    a.lr_vtr = v.lr_vtr;
     a.signs = v.signs;
     a.wht_scale = v.wht_scale;
     a.cos_cache = cos_cache;
@@ -492,8 +500,6 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
     a.v_meta = v.v_meta;
     a.signs = v.signs;
     a.wht_scale = v.wht_scale;
-    a.lr_vt = v.lr_vt;
-    a.lr_us = v.lr_us;
     // GroupQueryAttention scale (ops/microsoft.rs:1160): attribute, else 1/sqrt_f32(D).
     a.scale = has_scale ? scale : 1.0f / host_sqrt_f32((float)v.head_dim);
     a.cos_cache = cos_cache;
@@ -531,6 +537,8 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         ap.lr_vt = v.lr_vt;
         ap.lr_us = v.lr_us;
         ap.lr_scratch = lr_scratch_of(k, layer);
+        ap.lr_kmeta = v.lr_kmeta;
+        ap.lr_vtr = v.lr_vtr;
         ap.signs = v.signs;
         ap.wht_scale = v.wht_scale;
         ap.cos_cache = cos_cache;
@@ -539,18 +547,15 @@ static int attend_impl(kv_cache_impl *k, int32_t layer, const void *query, void 
         ap.do_rotary = a.do_rotary;
         ap.interleaved = a.interleaved;
     }
-    if (a.lr_us) {
-        // low-rank K: keys are lr_us[t] * lr_vt (read_k, kv_compression.rs:870-882)
+    if (v.lr_vtr) {
+        // low-rank K: keys are lr_us[t] * lr_vt (read_k, kv_compression.rs:870-882); the state of
+        // the new tokens first, then the usual kernels on {0, U*S[t]} metadata
         if (key) {
-            rc = launch_kv_append(ap, stream);
-            if (rc == SA_OK) rc = launch_lowrank_append(ap, stream);
+            rc = launch_lowrank_append(ap, stream);
             if (rc != SA_OK) return rc;
         }
-        AttendArgs la = a;
-        la.gather.n = 0;
-        rc = launch_lowrank_attend(la, stream);
-        if (rc != SA_OK || a.gather.n == 0) return rc;
-        return launch_gather_scatter(a, stream);
+        a.k_meta = v.lr_kmeta;
+        a.lr_vtr = v.lr_vtr;
     }
     if (decode_fast_eligible(a)) return launch_gqa_decode_fast(a, key ? &ap : nullptr, stream);
     if (key) {
@@ -718,6 +723,8 @@ int sa_qkv_project_append(sa_kv_cache *cache, int32_t layer, const void *x, cons
     ap.lr_vt = v.lr_vt;
     ap.lr_us = v.lr_us;
     ap.lr_scratch = lr_scratch_of(k, layer);
+    ap.lr_kmeta = v.lr_kmeta;
+    ap.lr_vtr = v.lr_vtr;
     ap.signs = v.signs;
     ap.wht_scale = v.wht_scale;
     ap.cos_cache = cos_cache;

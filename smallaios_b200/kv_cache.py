@@ -53,6 +53,8 @@ class LayerView:
     # low-rank K state (KVCacheConfig::kv_lowrank_k), None unless the cache keeps it
     lr_vt: torch.Tensor | None = None  # f32 (B, H, D): the rank-1 V^T row
     lr_us: torch.Tensor | None = None  # f32 (B, H, T): U*S, one coefficient per written row
+    lr_kmeta: torch.Tensor | None = None  # f32 (B, H, T, 2): {0, U*S[t]}, the K metadata attention reads
+    lr_vtr: torch.Tensor | None = None    # f32 (B, H, D): V^T rotated like the queries
 
     def v_codes_tokens(self) -> torch.Tensor:
         """V codes in per-token pack_bits order (B, H, T, CB).
@@ -192,7 +194,9 @@ class GpuKvCache:
                 v_qjl_mag=_view(v.v_qjl_mag, (B, H, T), "<f4", dev))),
             **({} if not v.lr_us else dict(
                 lr_vt=_view(v.lr_vt, (B, H, D), "<f4", dev),
-                lr_us=_view(v.lr_us, (B, H, T), "<f4", dev))))
+                lr_us=_view(v.lr_us, (B, H, T), "<f4", dev),
+                lr_kmeta=_view(v.lr_kmeta, (B, H, T, 2), "<f4", dev),
+                lr_vtr=_view(v.lr_vtr, (B, H, D), "<f4", dev))))
 
     def memory_bytes(self) -> tuple[int, int]:
         """(CompressedKVCache::memory_bytes of the rows written so far, summed over the batch,
@@ -203,7 +207,7 @@ class GpuKvCache:
 
     # Arrays of a layer that make up the compressed state (signs are derived from the seed).
     _STATE = ("k_codes", "v_codes", "k_meta", "v_meta", "k_qjl_bits", "v_qjl_bits", "k_qjl_mag", "v_qjl_mag",
-              "lr_vt", "lr_us")
+              "lr_vt", "lr_us", "lr_kmeta", "lr_vtr")
 
     def state_dict(self) -> dict:
         """The compressed cache as host tensors: configuration, position and, per layer, the
@@ -223,7 +227,7 @@ class GpuKvCache:
                     continue
                 if name == "v_codes":  # 16-token blocks: keep whole blocks up to the position
                     t = t[:, :, :(pos + 15) // 16]
-                elif name != "lr_vt":
+                elif name not in ("lr_vt", "lr_vtr"):
                     t = t[:, :, :pos]
                 st[name] = t.cpu().clone()
             layers.append(st)
@@ -248,7 +252,7 @@ class GpuKvCache:
                     raise ValueError(f"state has {name} but the cache does not keep it")
                 if name == "v_codes":
                     dst = dst[:, :, :t.shape[2]]
-                elif name != "lr_vt":
+                elif name not in ("lr_vt", "lr_vtr"):
                     dst = dst[:, :, :t.shape[2]]
                 dst.copy_(t.to(cache.device))
         torch.cuda.synchronize(cache.device)

@@ -199,4 +199,5 @@ def test_no_alloc_entry_reads_low_rank_view(cuda_device):
                                           torch.cuda.current_stream(cuda_device).cuda_stream))
     torch.cuda.synchronize()
     cache.close()
-    assert torch.equal(got, want)
+    # the no-alloc entry runs the general split-K kernel, the attend-only entry the decode kernel
+    assert (got - want).abs().max().item() <= 1e-3
