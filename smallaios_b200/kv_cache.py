@@ -244,18 +244,20 @@ class GpuKvCache:
                     kv_head_count=c["kv_head_count"], qjl_residual=bool(c["qjl_residual"]),
                     lowrank_k=c["lowrank_k"] or None, device=device)
         pos = int(state["position"])
-        for layer, st in enumerate(state["layers"]):
-            v = cache.view(layer)
-            for name, t in st.items():
-                dst = getattr(v, name)
-                if dst is None:
-                    raise ValueError(f"state has {name} but the cache does not keep it")
-                if name == "v_codes":
-                    dst = dst[:, :, :t.shape[2]]
-                elif name not in ("lr_vt", "lr_vtr"):
-                    dst = dst[:, :, :t.shape[2]]
-                dst.copy_(t.to(cache.device))
-        torch.cuda.synchronize(cache.device)
+        try:
+            for layer, st in enumerate(state["layers"]):
+                v = cache.view(layer)
+                for name, t in st.items():
+                    dst = getattr(v, name)
+                    if dst is None:
+                        raise ValueError(f"state has {name} but the cache does not keep it")
+                    if name not in ("lr_vt", "lr_vtr"):  # arrays with a token (or token-block) axis
+                        dst = dst[:, :, :t.shape[2]]
+                    dst.copy_(t.to(cache.device))
+            torch.cuda.synchronize(cache.device)
+        except Exception:
+            cache.close()
+            raise
         cache.set_position(pos)
         return cache
 
