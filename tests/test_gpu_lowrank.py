@@ -174,6 +174,39 @@ def test_fused_qkv_projection_and_qjl_together(cuda_device):
     _bits_equal("lr_vt", vt, want_vt)
 
 
+def test_general_kernel_three_bits_short_chunk(cuda_device):
+    """3-bit codes and a 5-token chunk take the general split-K kernel through the operator; its
+    scores read the low-rank metadata and q'.R(V^T) like the other kernels."""
+    import smallaios_b200 as sa
+
+    b, hq, hkv, d, bits, past, s = 2, 8, 2, 64, 3, 70, 5
+    t = past + s
+    r = rng(13)
+    k = (r.standard_normal((b, t, hkv, d)) * 1.28).astype(np.float32)
+    v = (r.standard_normal((b, t, hkv, d)) * 1.28).astype(np.float32)
+    q = (r.standard_normal((b, s, hq, d)) * 1.28).astype(np.float32)
+    cos, sin = rope_tables(t + 1, d)
+    tcos, tsin = torch.from_numpy(cos).to(cuda_device), torch.from_numpy(sin).to(cuda_device)
+    cache = sa.GpuKvCache(1, hkv, d, t + 1, batch=b, num_heads=hq, bits=bits, lowrank_k=2, device=cuda_device)
+    cache.append(0, torch.from_numpy(k[:, :past]).reshape(b, past, hkv * d).to(cuda_device),
+                 torch.from_numpy(v[:, :past]).reshape(b, past, hkv * d).to(cuda_device), cos_cache=tcos,
+                 sin_cache=tsin, do_rotary=True)
+    cache.advance_position(past)
+    out = sa.group_query_attention(torch.from_numpy(q).reshape(b, s, hq * d).to(cuda_device),
+                                   torch.from_numpy(k[:, past:]).reshape(b, s, hkv * d).to(cuda_device),
+                                   torch.from_numpy(v[:, past:]).reshape(b, s, hkv * d).to(cuda_device), cache, 0,
+                                   num_heads=hq, kv_num_heads=hkv, cos_cache=tcos, sin_cache=tsin)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    signs = cache.view(0).signs.cpu().numpy().astype(np.int8)
+    cache.close()
+    us, vt = oracle_lowrank_state(k, 2, cos, sin, True)
+    kc, km, vc, vm = oracle_append(k, v, signs, bits, 0, cos, sin, True)
+    want = oracle_lowrank_attend(q, us, vt, vc, vm, signs, bits, past, cos=cos, sin=sin, do_rotary=True)
+    err = np.abs(got - want)
+    assert err.max() <= 1e-3, f"max err {err.max():.3e}"
+
+
 def test_no_alloc_entry_reads_low_rank_view(cuda_device):
     import ctypes
 
