@@ -183,6 +183,47 @@ def rope_np(rows, d, theta):
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
+def parity_sample(torch, cache, q, k, out, cos_np, sin_np, kv_count, rows):
+    """Check the timed step's own output against the CPU oracle on a sample of batch rows.
+
+    Runs after the timed region.  The cache then holds every token the last step attended to,
+    the newest (appended by that step at position T-1) included.  Checks (1) the newest
+    token's K codes and metadata bit for bit against PolarQuantizer::encode of RoPE(k), and
+    (2) the attention output of every query head of the sampled rows against the composite
+    oracle (read_k/read_v of all T tokens + causal SDPA) within 1e-3 + half a bf16 ulp.
+    """
+    import oracle  # the checker
+
+    hq = kv_count * (HQ // HKV)
+    rows = sorted(set(r for r in rows if 0 <= r < B))
+    view = cache.view(0)
+    kc = view.k_codes[rows, :, :T].cpu().numpy()
+    km = view.k_meta[rows, :, :T].cpu().numpy()
+    vc = view.v_codes_tokens()[rows][:, :, :T].cpu().numpy()
+    vm = view.v_meta[rows, :, :T].cpu().numpy()
+    signs = view.signs.cpu().numpy().astype(np.int8)
+    nt = os.cpu_count() or 1
+    # (1) the step's append: RoPE(k) at T-1, then PolarQuantizer::encode per KV head
+    kn = k[rows].float().cpu().numpy().reshape(len(rows), 1, kv_count, D).transpose(0, 2, 1, 3)
+    kr = oracle.apply_rope(np.ascontiguousarray(kn), cos_np, sin_np, np.array([T - 1]))
+    codes_ok = True
+    for h in range(kv_count):
+        c, m = oracle.polar_encode_many(kr[:, h, 0], BITS, signs[h], nthreads=nt)
+        codes_ok &= bool(np.array_equal(c, kc[:, h, T - 1]) and
+                         np.array_equal(m.view(np.uint32), km[:, h, T - 1].view(np.uint32)))
+    # (2) attention of the sampled rows
+    qn = q[rows].float().cpu().numpy().reshape(len(rows), 1, hq, D).transpose(0, 2, 1, 3)
+    qr = oracle.apply_rope(np.ascontiguousarray(qn), cos_np, sin_np, np.array([T - 1]))
+    scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(D)))
+    want = oracle.compressed_gqa(qr, kc, km, vc, vm, signs, BITS, scale, nthreads=nt)
+    got = out[rows].float().cpu().numpy().reshape(want.shape)
+    err = np.abs(got - want)
+    bound = 1e-3 + np.abs(want) * 2.0 ** -8
+    return {"max_abs": float(err.max()), "ok": bool(np.all(err <= bound)) and codes_ok,
+            "codes_bit_exact": codes_ok, "rows": rows, "units": len(rows) * kv_count,
+            "bar": "max-abs 1e-3 + half a bf16 ulp vs the composite CPU oracle; newest token's codes bit-exact"}
+
+
 def cpu_oracle_step_time(cache_view_np, q_np, k_new, v_new, signs, units, nthreads):
     """One CPU step of the reference path on `units` (b, kv_head) pairs:
     encode the new token (write_kv) + read_k/read_v of all T tokens + SDPA."""
@@ -227,8 +268,87 @@ def cpu_sample(torch, cache, q, k, v, dev, target_s=10.0, nthreads=1):
     return B / step_time, desc
 
 
+def reference_step(data, q_new, k_new, v_new, signs, cos_np, sin_np, units, nthreads):
+    """One step of the reference CPU path on the first ``units`` (row, KV head) units, timed:
+    RoPE of q and k at position T-1 (apply_rope_in_place), PolarQuantizer::encode of the new
+    K and V into the cache (write_kv), then read_k/read_v of all T tokens and causal SDPA
+    (the composite oracle), all host threads."""
+    import oracle
+
+    kc, km, vc, vm = data
+    nb = (units + HKV - 1) // HKV
+    scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(D)))
+    t0 = time.perf_counter()
+    pos = np.array([T - 1])
+    qr = oracle.apply_rope(q_new[:nb], cos_np, sin_np, pos)   # (nb, HQ, 1, D)
+    kr = oracle.apply_rope(k_new[:nb], cos_np, sin_np, pos)   # (nb, HKV, 1, D)
+    for h in range(HKV):
+        c, m = oracle.polar_encode_many(kr[:, h, 0], BITS, signs[h], nthreads=nthreads)
+        kc[:nb, h, T - 1], km[:nb, h, T - 1] = c, m
+        c, m = oracle.polar_encode_many(v_new[:nb, h, 0], BITS, signs[h], nthreads=nthreads)
+        vc[:nb, h, T - 1], vm[:nb, h, T - 1] = c, m
+    out = oracle.compressed_gqa(qr, kc[:nb], km[:nb], vc[:nb], vm[:nb], signs, BITS, scale, nthreads=nthreads,
+                                unit_begin=0, unit_end=units)
+    return time.perf_counter() - t0, out
+
+
+def reference_inputs():
+    """The GPU arm's step inputs, staged to host memory before any timing: the cache after
+    its T-1 seeded appends (rank 0's seed) and the step's q/k/v.  On a machine without a GPU
+    the same shapes are generated on the host and encoded with the CPU restatement."""
+    import oracle
+
+    try:
+        import torch
+
+        have_gpu = torch.cuda.is_available()
+    except ImportError:
+        have_gpu = False
+    if have_gpu:
+        import smallaios_b200 as sa
+
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        cache, _, _, q, k, v = build_workload(torch, sa, dev, seed=1000)
+        view = cache.view(0)
+        data = (view.k_codes[:, :, :T].cpu().numpy(), view.k_meta[:, :, :T].cpu().numpy(),
+                view.v_codes_tokens()[:, :, :T].cpu().numpy(), view.v_meta[:, :, :T].cpu().numpy())
+        signs = view.signs.cpu().numpy().astype(np.int8)
+        qn = q.float().cpu().numpy().reshape(B, 1, HQ, D).transpose(0, 2, 1, 3).copy()
+        kn = k.float().cpu().numpy().reshape(B, 1, HKV, D).transpose(0, 2, 1, 3).copy()
+        vn = v.float().cpu().numpy().reshape(B, 1, HKV, D).transpose(0, 2, 1, 3).copy()
+        cache.close()
+        src = "the GPU arm's own cache bytes (rank 0's seed, T-1 tokens appended), copied to host"
+    else:
+        rng = np.random.default_rng(1000)
+        signs = oracle.cache_signs(oracle.DEFAULT_SEED, 1, HKV, D)[0]
+        cos_np, sin_np = rope_np(T, D, THETA)
+        kc = np.zeros((B, HKV, T, CB), np.uint8)
+        vc = np.zeros_like(kc)
+        km = np.zeros((B, HKV, T, 2), np.float32)
+        vm = np.zeros_like(km)
+        for b in range(B):
+            kx = (rng.standard_normal((1, HKV, T - 1, D)) * 1.28).astype(np.float32)
+            vx = (rng.standard_normal((HKV, T - 1, D)) * 1.28).astype(np.float32)
+            kx = oracle.apply_rope(kx, cos_np, sin_np, np.arange(T - 1))[0]
+            for h in range(HKV):
+                kc[b, h, :T - 1], km[b, h, :T - 1] = oracle.polar_encode_many(kx[h], BITS, signs[h])
+                vc[b, h, :T - 1], vm[b, h, :T - 1] = oracle.polar_encode_many(vx[h], BITS, signs[h])
+        data = (kc, km, vc, vm)
+        qn = (rng.standard_normal((B, HQ, 1, D)) * 1.28).astype(np.float32)
+        kn = (rng.standard_normal((B, HKV, 1, D)) * 1.28).astype(np.float32)
+        vn = (rng.standard_normal((B, HKV, 1, D)) * 1.28).astype(np.float32)
+        src = "seeded host normals (std 1.28) encoded by the CPU restatement (no GPU on this machine)"
+    return data, qn, kn, vn, signs, src
+
+
 def run_reference(args):
-    """--impl reference: the CPU restatement, all host threads, rank 0 only."""
+    """--impl reference: the CPU restatement of the reference path, all host threads, rank 0 only.
+
+    Every timed step is the whole reference step over all B x Hkv units (RoPE, write_kv of the
+    new token, read_k/read_v of T tokens, SDPA) unless that would not fit a few minutes; then
+    each step runs a fixed subset of units and the line says so.
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -236,34 +356,42 @@ def run_reference(args):
 
     oracle.build()
     nthreads = os.cpu_count() or 1
-    rng = np.random.default_rng(1234)
-    nb = max(1, (nthreads + HKV - 1) // HKV)
-    units = nb * HKV
-    signs = oracle.cache_signs(oracle.DEFAULT_SEED, 1, HKV, D)[0]
-    # seeded cache contents: codes uniform, meta like int4 PolarQuant of std-1.28 vectors
-    kc = rng.integers(0, 256, size=(nb, HKV, T, CB), dtype=np.uint8)
-    vc = rng.integers(0, 256, size=(nb, HKV, T, CB), dtype=np.uint8)
-    km = np.stack([rng.uniform(0.3, 0.5, (nb, HKV, T)), rng.uniform(-4, -2.5, (nb, HKV, T))], -1).astype(np.float32)
-    vm = km.copy()
-    q = (rng.standard_normal((nb, HQ, 1, D)) * 1.28).astype(np.float32)
-    kn = (rng.standard_normal((nb, HKV, D)) * 1.28).astype(np.float32)
-    vn = (rng.standard_normal((nb, HKV, D)) * 1.28).astype(np.float32)
-    data = (kc, km, vc, vm)
-    for _ in range(max(0, args.warmup)):
-        cpu_oracle_step_time(data, q, kn, vn, signs, min(units, nthreads), nthreads)
-    times = [cpu_oracle_step_time(data, q, kn, vn, signs, units, nthreads) for _ in range(args.steps)]
-    step = float(np.mean(times)) * (B * HKV) / units
+    data, qn, kn, vn, signs, src = reference_inputs()
+    cos_np, sin_np = rope_np(T, D, THETA)
+    total = B * HKV
+    # one probe step on a thread's worth of units sizes the run
+    probe_units = min(total, max(HKV, nthreads))
+    dt, _ = reference_step(data, qn, kn, vn, signs, cos_np, sin_np, probe_units, nthreads)
+    est_full = dt * total / probe_units
+    budget_s = 240.0
+    units = total
+    if est_full * (args.steps + args.warmup) > budget_s:
+        units = max(probe_units, int(budget_s / (args.steps + args.warmup) / dt * probe_units) // HKV * HKV)
+        units = min(units, total)
+    for _ in range(args.warmup):
+        reference_step(data, qn, kn, vn, signs, cos_np, sin_np, units, nthreads)
+    times = [reference_step(data, qn, kn, vn, signs, cos_np, sin_np, units, nthreads)[0] for _ in range(args.steps)]
+    measured = float(np.mean(times))
+    step = measured * total / units
     value = B / step
+    if units == total:
+        sample = (f"every step is the full step: all {total} (batch row, kv head) units, T={T}, on {src}; "
+                  f"the C restatement of the reference Rust CPU path (-O2, no FMA; no rustc here), "
+                  f"{nthreads} threads")
+    else:
+        sample = (f"{units} of {total} (batch row, kv head) units per step (a full step would not fit the run), "
+                  f"scaled by {total}/{units}; T={T}, on {src}; the C restatement of the reference Rust CPU path, "
+                  f"{nthreads} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-                   "context": T, "kv_bits": BITS},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
-                         "sample": f"{units} of {B * HKV} (batch row, kv head) units per step, scaled; the C "
-                                   "restatement of the reference Rust CPU path (reference not compilable: no rustc)"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded normal, std 1.28)",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B, "q_heads": HQ, "kv_heads": HKV,
+                   "head_dim": D, "context": T, "kv_bits": BITS, "rope_theta": THETA},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads,
+                         "kind": "port" if units == total else "port (sampled, scaled)", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "measured_s_per_step": measured, "units_per_step": units,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -617,6 +745,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the check of the timed step's output against the CPU oracle (after timing)")
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS),
                     help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
     ap.add_argument("--batch", type=int, default=None,
@@ -824,11 +954,26 @@ def main():
         e2e_mode = ("host launches; step i+1's copy-in and step i-1's copy-out overlap step i "
                     "(two copy streams, double buffers)")
 
+    # Parity of the timed step's own output (outside every timed region): every rank checks a
+    # sample of its rows against the CPU oracle; the worst error over ranks is reported.
+    parity = None
+    if not args.no_parity:
+        torch.cuda.synchronize(dev)
+        res = out
+        if heads and peer is not None:  # the fused gather wrote the rank's heads into `gathered` only
+            res = gathered[..., shard.q_begin * D:(shard.q_begin + shard.q_count) * D]
+        cos_np, sin_np = rope_np(T, D, THETA)
+        parity = parity_sample(torch, cache, q, k, res, cos_np, sin_np, kv_count, [0, B // 2, B - 1])
+
     # max over ranks
-    times = torch.tensor([t_ms, e2e_ms, attend_ms, e2e_eager_ms], device=dev, dtype=torch.float64)
+    pmax = -1.0 if parity is None else parity["max_abs"]
+    pbad = 0.0 if parity is None or parity["ok"] else 1.0
+    times = torch.tensor([t_ms, e2e_ms, attend_ms, e2e_eager_ms, pmax, pbad], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, attend_ms, e2e_eager_ms = times.tolist()
+    t_ms, e2e_ms, attend_ms, e2e_eager_ms, pmax, pbad = times.tolist()
+    if parity is not None:
+        parity.update(max_abs=pmax, ok=pbad == 0.0, ranks=world)
     rows_mult = 1 if heads else world  # sequences decoded per step = B * rows_mult
 
     peak, peak_kind = load_peaks()
@@ -864,6 +1009,9 @@ def main():
         "step_gbs": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)) / (t_ms * 1e-3) / 1e9,
         "clocks": clocks,
     }
+    if parity is not None:
+        line["parity_max_abs"] = parity["max_abs"]
+        line["parity"] = parity
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle  # checker / CPU baseline only
 

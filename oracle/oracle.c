@@ -217,6 +217,49 @@ int orc_polar_decode(const uint8_t *codes, float scale, float zp, int dim, int b
     return ORC_OK;
 }
 
+/* PolarQuantizer::encode of n independent vectors sharing one sign vector,
+ * split over nthreads threads (each vector is encoded exactly as
+ * orc_polar_encode does; the threads only change which core runs it). */
+typedef struct {
+    const float *x;
+    const int8_t *signs;
+    uint8_t *codes;
+    float *meta;
+    size_t begin, end;
+    int dim, bits, rc;
+} encode_job;
+
+static void *encode_worker(void *arg) {
+    encode_job *j = (encode_job *)arg;
+    size_t cb = ((size_t)j->dim * j->bits + 7) / 8;
+    for (size_t i = j->begin; i < j->end && j->rc == ORC_OK; i++)
+        j->rc = orc_polar_encode(j->x + i * j->dim, j->dim, j->bits, j->signs, j->codes + i * cb,
+                                 j->meta + 2 * i, j->meta + 2 * i + 1, NULL, NULL);
+    return NULL;
+}
+
+int orc_polar_encode_batch(const float *x, size_t n, int dim, int bits, const int8_t *signs,
+                           uint8_t *codes, float *meta, int nthreads) {
+    if (!is_pow2(dim) || !valid_bits(bits)) return ORC_INVALID_ATTRIBUTE;
+    if (nthreads < 1) nthreads = 1;
+    if ((size_t)nthreads > n) nthreads = n > 0 ? (int)n : 1;
+    encode_job *jobs = (encode_job *)calloc((size_t)nthreads, sizeof(encode_job));
+    pthread_t *th = (pthread_t *)calloc((size_t)nthreads, sizeof(pthread_t));
+    int rc = ORC_OK;
+    for (int i = 0; i < nthreads; i++) {
+        jobs[i] = (encode_job){x, signs, codes, meta, n * i / nthreads, n * (i + 1) / nthreads, dim, bits, ORC_OK};
+        if (nthreads > 1) pthread_create(&th[i], NULL, encode_worker, &jobs[i]);
+        else encode_worker(&jobs[i]);
+    }
+    for (int i = 0; i < nthreads; i++) {
+        if (nthreads > 1) pthread_join(th[i], NULL);
+        if (jobs[i].rc != ORC_OK) rc = jobs[i].rc;
+    }
+    free(jobs);
+    free(th);
+    return rc;
+}
+
 /* QJLResidualEncoder::encode (kv_compression.rs:365-395) */
 void orc_qjl_encode(const float *original, const float *approx, int dim,
                     uint64_t *sign_bits, float *c_magnitude) {

@@ -47,6 +47,10 @@ void orc_unpack_bits(const uint8_t *data, int nbytes, int count, int bits, uint3
 int orc_polar_encode(const float *in, int dim, int bits, const int8_t *signs,
                      uint8_t *codes, float *scale, float *zero_point,
                      float *min_val, float *max_val);
+/* orc_polar_encode of n vectors x[n][dim] with one sign vector, split over
+ * nthreads threads; codes[n][ceil(dim*bits/8)], meta[n][2] = {scale, zp}. */
+int orc_polar_encode_batch(const float *x, size_t n, int dim, int bits, const int8_t *signs,
+                           uint8_t *codes, float *meta, int nthreads);
 /* PolarQuantizer::decode (:270-286). */
 int orc_polar_decode(const uint8_t *codes, float scale, float zero_point,
                      int dim, int bits, const int8_t *signs, float *out);

@@ -40,17 +40,23 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_build():
         return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
     objdir = ROOT / "_build"
     objdir.mkdir(exist_ok=True)
-    objs = []
+    cmds, objs = [], []
     for s in SOURCES:
-        src = CSRC / s
         obj = objdir / (Path(s).stem + ".o")
-        cmd = [NVCC, *ARCH, *FLAGS, "-I", str(ROOT / "include"), "-dc" if False else "-c", str(src), "-o", str(obj)]
+        cmds.append([NVCC, *ARCH, *FLAGS, "-I", str(ROOT / "include"), "-c", str(CSRC / s), "-o", str(obj)])
+        objs.append(str(obj))
+
+    def compile_one(cmd):
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.check_call(cmd)
-        objs.append(str(obj))
+
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as pool:
+        list(pool.map(compile_one, cmds))  # re-raises the first failed compile
     tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *objs]
     if verbose:

@@ -118,8 +118,8 @@ __global__ void __launch_bounds__(32 * kWarps) attend_split_kernel(AttendArgs a,
         rope_and_rotate<T, EPL>(src, x, lane, d, qpos, a, sg);
         float part = 0.0f;
         if (lane * EPL < d) {
-#pragma unroll
             const float *vtr = a.lr_vtr ? a.lr_vtr + ((int64_t)b * a.heads + h) * d : nullptr;
+#pragma unroll
             for (int r = 0; r < EPL; r++) {
                 s_q[g * d + lane * EPL + r] = x[r];
                 part += vtr ? x[r] * vtr[lane * EPL + r] : x[r];  // sum(q'), or q'.V^T with low-rank K

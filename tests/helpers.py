@@ -4,6 +4,8 @@ The oracle (oracle/) is only used here as the checker.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 import oracle
@@ -128,7 +130,7 @@ def oracle_attend(q_bshd: np.ndarray, kc, km, vc, vm, signs_hd, bits, pos0, scal
         q = oracle.apply_rope(q, cos, sin, np.arange(pos0, pos0 + s), interleaved=interleaved)
     if scale is None:
         scale = np.float32(1.0) / np.float32(oracle.sqrt_f32(float(d)))
-    return oracle.compressed_gqa(q, kc, km, vc, vm, signs_hd, bits, scale)
+    return oracle.compressed_gqa(q, kc, km, vc, vm, signs_hd, bits, scale, nthreads=os.cpu_count() or 1)
 
 
 def interleave_v(vc_tokens: np.ndarray) -> np.ndarray:
