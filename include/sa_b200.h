@@ -381,6 +381,42 @@ int sa_rms_norm(const void *x, const void *skip, const void *bias, const void *w
 int sa_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int32_t dtype, int64_t rows,
                 int64_t cols, sa_stream_t stream);
 
+/* ======================================================================
+ * com.microsoft.RotaryEmbedding as its own node: replaces dispatch_rotary_
+ * embedding -> rotary_gpu (onnx-rt/src/cuda/gpu_executor.rs:814-850,
+ * onnx-rt/src/cuda/kernels/rotary.rs:274-346) for graphs that rotate Q and
+ * K in separate RotaryEmbedding nodes ahead of GroupQueryAttention with
+ * do_rotary = 0 (onnx-rt/src/model_loader/gemma.rs:13-36).
+ *
+ * x, y: layout 0 = (batch, num_heads, seq_len, head_dim) (rank 4), layout 1 =
+ * (batch, seq_len, num_heads * head_dim) (rank 3); y may equal x (in place).
+ * Tables cos/sin: (table_rows, table_cols) of table_dtype (Float, or BFloat16
+ * widened in the kernel as the executor's cast does), table_cols =
+ * rotary_dim / 2.  rotary_dim <= 0 means head_dim; elements at or past
+ * rotary_dim pass through (apply_rope_in_place, ops/microsoft.rs:190-231).
+ * Pairs (x[i], x[i + rotary_dim/2]), or (x[2i], x[2i+1]) when interleaved;
+ * y0 = c*x0 - s*x1, y1 = s*x0 + c*x1 with every product and sum rounded to
+ * f32 (rotate_rope_block, ops/microsoft.rs:137-162), so f32 outputs are
+ * bit-exact with the CPU op.
+ *
+ * Positions: with position_ids == NULL, token s uses table row
+ * start_position + s (the executor passes the cache's current position:
+ * pick_rotary_position, gpu_executor.rs:761-773; the caller checks
+ * start_position + seq_len <= table_rows on the host, no D2H read).  With a
+ * DEVICE position_ids array of position_dtype INT64 (7) or INT32 (6) and
+ * position_count = seq_len or batch * seq_len entries, token (b, s) uses
+ * position_ids[s] or position_ids[b * seq_len + s] (rope_position_for,
+ * ops/microsoft.rs:112-120); the reference GPU path reads only the first id
+ * back to the host instead.  A position id outside [0, table_rows) cannot be
+ * reported by the call's status: that row is passed through unrotated and
+ * bit 0 of *device_status is set when device_status (a device int) is given.
+ * ====================================================================== */
+int sa_rotary_embedding(const void *x, void *y, int32_t dtype, int32_t layout, int64_t batch, int64_t num_heads,
+                        int64_t seq_len, int32_t head_dim, const void *cos_cache, const void *sin_cache,
+                        int32_t table_dtype, int64_t table_rows, int32_t table_cols, const void *position_ids,
+                        int32_t position_dtype, int64_t position_count, int64_t start_position,
+                        int32_t interleaved, int32_t rotary_dim, int32_t *device_status, sa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

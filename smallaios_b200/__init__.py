@@ -9,8 +9,8 @@ operator interface; all compute runs in the CUDA library.
 from .kv_cache import DEFAULT_SEED, GpuKvCache, LayerView, qjl_correction
 from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatchCtx, OpError, PackedNBitsWeight,
                   ShapeMismatch, UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend,
-                  group_query_attention, matmul_nbits, matmul_nbits_packed, qkv_project_append, rms_norm, silu_mul,
-                  supports_op)
+                  group_query_attention, matmul_nbits, matmul_nbits_packed, qkv_project_append, rms_norm,
+                  rotary_device_status, rotary_embedding, silu_mul, supports_op)
 from .layer import LayerWeights, decoder_layer_step
 
 __all__ = [
@@ -18,5 +18,5 @@ __all__ = [
     "KvCacheDispatchCtx", "OpError", "ShapeMismatch", "UnsupportedOp", "dispatch_gpu_node", "finalize_kv_cache",
     "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight",
     "qkv_project_append", "rms_norm", "silu_mul", "supports_op", "LayerWeights", "decoder_layer_step",
-    "qjl_correction",
+    "qjl_correction", "rotary_embedding", "rotary_device_status",
 ]

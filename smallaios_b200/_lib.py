@@ -36,7 +36,7 @@ EXPORTED = [
     "sa_kv_cache_device_status", "sa_kv_cache_set_gather",
     "sa_kv_append", "sa_gqa_attend", "sa_group_query_attention", "sa_matmul_nbits", "sa_gqa_attend_no_alloc",
     "sa_matmul_nbits_packed_bytes", "sa_matmul_nbits_prepack", "sa_matmul_nbits_packed",
-    "sa_qkv_project_append", "sa_rms_norm", "sa_silu_mul",
+    "sa_qkv_project_append", "sa_rms_norm", "sa_silu_mul", "sa_rotary_embedding",
 ]
 SA_STATIC_SCRATCH_BYTES = 8 << 20
 
@@ -142,6 +142,9 @@ def _declare(l: ctypes.CDLL) -> None:
     l.sa_rms_norm.argtypes = [_P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _F, _P]
     l.sa_silu_mul.restype = ctypes.c_int
     l.sa_silu_mul.argtypes = [_P, _P, _I64, _P, _I32, _I64, _I64, _P]
+    l.sa_rotary_embedding.restype = ctypes.c_int
+    l.sa_rotary_embedding.argtypes = [_P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32,
+                                      _I64, _I64, _I32, _I32, _P, _P]
     l.sa_qkv_project_append.restype = ctypes.c_int
     l.sa_qkv_project_append.argtypes = [_P, _I32, _P, _P, _P, _I32, _I32, _I64, _P, _P, _I32, _I32, _I32, _P, _P,
                                         _P, _P]

@@ -16,9 +16,9 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libsa_b200.so"
 SOURCES = ["sa_runtime.cu", "kv_append.cu", "gqa_attend.cu", "gqa_decode_mma.cu", "gqa_decode_g8.cu",
            "matmul_nbits.cu", "matmul_nbits_umma.cu",
-           "qkv_project.cu", "layer_glue.cu", "gqa_prefill_umma.cu", "lowrank.cu"]
+           "qkv_project.cu", "layer_glue.cu", "gqa_prefill_umma.cu", "lowrank.cu", "rotary.cu"]
 HEADERS = ["sa_common.cuh", "sa_internal.h", "sa_append.cuh", "sa_async.cuh", "sa_decode_common.cuh", "sa_tma.cuh",
-           "sa_qkv.cuh", "sa_tcgen05.cuh"]
+           "sa_qkv.cuh", "sa_tcgen05.cuh", "sa_gather.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",

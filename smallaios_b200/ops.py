@@ -307,6 +307,88 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor | None = None, *, out: torch.T
     return out
 
 
+_POS_DTYPES = {torch.int64: 7, torch.int32: 6}
+_ROTARY_STATUS: dict = {}  # device index -> int32 device word that rotary_embedding calls flag
+
+
+def rotary_device_status(device=None, clear: bool = True) -> int:
+    """Bit 0 set when a ``rotary_embedding`` call on ``device`` met a position id outside its
+    cos/sin table (that row was passed through unrotated).  Synchronises with the device."""
+    dev = torch.device(device if device is not None else "cuda")
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    word = _ROTARY_STATUS.get(idx)
+    if word is None:
+        return 0
+    v = int(word.item())
+    if clear:
+        word.zero_()
+    return v
+
+
+def _rotary_status_word(device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    word = _ROTARY_STATUS.get(idx)
+    if word is None:
+        word = _ROTARY_STATUS[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+    return word
+
+
+def rotary_embedding(x: torch.Tensor, cos_cache: torch.Tensor, sin_cache: torch.Tensor, *,
+                     position_ids: torch.Tensor | None = None, position: int = 0, interleaved: bool = False,
+                     num_heads: int | None = None, rotary_embedding_dim: int = 0, out: torch.Tensor | None = None,
+                     stream=None) -> torch.Tensor:
+    """com.microsoft.RotaryEmbedding on the GPU (rotary_gpu, onnx-rt/src/cuda/kernels/rotary.rs:274-346;
+    arithmetic and partial rotation as op_rotary_embedding / apply_rope_in_place,
+    ops/microsoft.rs:137-231, 556-650).
+
+    ``x``: rank-4 ``(B, H, S, D)`` or rank-3 ``(B, S, H*D)`` (then ``num_heads`` is needed).
+    Without ``position_ids`` token s uses table row ``position + s`` (the executor passes the
+    cache's current position); with ``position_ids`` (``S`` or ``B*S`` int32/int64 entries, read on
+    the device) token (b, s) uses its own id.  Returns a new tensor unless ``out`` is given
+    (``out`` may be ``x``).
+    """
+    _cuda(x, "X")
+    for name, t in (("cos_cache", cos_cache), ("sin_cache", sin_cache)):
+        _cuda(t, name)
+        if t.dtype not in (torch.float32, torch.bfloat16):
+            raise UnsupportedOp("rotary_gpu: cos/sin tables must be Float or BFloat16")
+        if t.dim() != 2:
+            raise ShapeMismatch("apply_rope_in_place: cos/sin caches must be rank-2")
+    if cos_cache.shape != sin_cache.shape or cos_cache.dtype != sin_cache.dtype:
+        raise ShapeMismatch("rotary_gpu: cos/sin tables must share max_seq_len and inner dim")
+    if x.dim() == 4:
+        layout, (b, h, s, d) = 0, x.shape
+    elif x.dim() == 3:
+        if num_heads is None or num_heads <= 0:
+            raise InvalidAttribute("RotaryEmbedding: num_heads must be > 0 for rank-3 input")
+        b, s, hidden = x.shape
+        if hidden % num_heads:
+            raise ShapeMismatch("RotaryEmbedding: hidden not divisible by num_heads")
+        layout, h, d = 1, num_heads, hidden // num_heads
+    else:
+        raise ShapeMismatch("RotaryEmbedding: input must be rank-3 or rank-4")
+    pos_ptr, pos_dtype, pos_count = None, 0, 0
+    if position_ids is not None:
+        if position_ids.dtype not in _POS_DTYPES:
+            raise ShapeMismatch("RotaryEmbedding: position_ids must be int32 or int64")
+        if not position_ids.is_cuda:
+            position_ids = position_ids.to(x.device, non_blocking=True)
+        position_ids = position_ids.contiguous()
+        pos_ptr, pos_dtype, pos_count = position_ids.data_ptr(), _POS_DTYPES[position_ids.dtype], position_ids.numel()
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous():
+        raise ShapeMismatch("RotaryEmbedding: out must be a contiguous tensor of x's shape and dtype")
+    status = _rotary_status_word(x.device) if position_ids is not None else None
+    rc = lib.sa_rotary_embedding(x.data_ptr(), out.data_ptr(), _dtype_code(x), layout, b, h, s, d,
+                                 cos_cache.data_ptr(), sin_cache.data_ptr(), _dtype_code(cos_cache),
+                                 cos_cache.shape[0], cos_cache.shape[1], pos_ptr, pos_dtype, pos_count, int(position),
+                                 int(bool(interleaved)), int(rotary_embedding_dim),
+                                 None if status is None else status.data_ptr(), _stream_handle(stream, x.device))
+    _raise_op(rc, "RotaryEmbedding")
+    return out
+
+
 class PackedNBitsWeight:
     """A MatMulNBits weight repacked once for the decode GEMV (``sa_matmul_nbits_prepack``).
 
@@ -350,8 +432,8 @@ def matmul_nbits_packed(a: torch.Tensor, w: PackedNBitsWeight, bias: torch.Tenso
 
 
 # ---- executor glue ------------------------------------------------------------
-SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits", "RMSNormalization", "SimplifiedLayerNormalization",
-                 "SkipSimplifiedLayerNormalization")
+SUPPORTED_OPS = ("GroupQueryAttention", "MatMulNBits", "RMSNormalization", "RotaryEmbedding",
+                 "SimplifiedLayerNormalization", "SkipSimplifiedLayerNormalization")
 
 
 def supports_op(op_type: str) -> bool:
@@ -393,6 +475,26 @@ def dispatch_gpu_node(op_type: str, inputs: list, attrs: dict, kv_cache_ctx: KvC
             cos_cache=inp[7] if inp[7] is not None else kv_cache_ctx.rope.get("cos_cache"),
             sin_cache=inp[8] if inp[8] is not None else kv_cache_ctx.rope.get("sin_cache"))
         return [out]
+    if op_type == "RotaryEmbedding":
+        # inputs [X, position_ids, cos_cache, sin_cache] (com.microsoft) or [X, cos_cache, sin_cache]
+        # (the gemma builder); resolve_rotary_inputs, gpu_executor.rs:719-759
+        x = inputs[0]
+        if len(inputs) >= 4:
+            pos_ids, cos, sin = inputs[1], inputs[2], inputs[3]
+        else:
+            pos_ids, cos, sin = None, inputs[1], inputs[2]
+        if x is None or cos is None or sin is None:
+            raise ShapeMismatch("RotaryEmbedding: missing input")
+        # no explicit ids: the cache's current position (pick_rotary_position, :761-773), read on the host
+        position = kv_cache_ctx.cache.current_position() if (pos_ids is None and kv_cache_ctx is not None) else 0
+        num_heads = attrs.get("num_heads")
+        if x.dim() == 3 and num_heads is None:  # rotary_num_heads_for_rank3, :794-811
+            hd = cos.shape[-1] * 2
+            num_heads = x.shape[2] // hd if hd > 0 and x.shape[2] % hd == 0 else None
+        return [rotary_embedding(x, cos, sin, position_ids=pos_ids, position=position,
+                                 interleaved=bool(int(attrs.get("interleaved", 0))),
+                                 num_heads=None if num_heads is None else int(num_heads),
+                                 rotary_embedding_dim=int(attrs.get("rotary_embedding_dim", 0)))]
     if op_type in ("RMSNormalization", "SimplifiedLayerNormalization"):
         # inputs (X, scale[, bias]); attributes epsilon (1e-5), axis (-1: the last axis only)
         if int(attrs.get("axis", -1)) not in (-1, inputs[0].dim() - 1):

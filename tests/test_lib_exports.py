@@ -86,6 +86,29 @@ def test_matmul_nbits_validation_without_gpu():
     assert lib.sa_matmul_nbits(None, None, None, None, None, None, 1, 1, 8, 64, 4, 32, None) == 9
 
 
+def test_rotary_embedding_validation_without_gpu():
+    from smallaios_b200 import ops
+    from smallaios_b200._lib import lib
+
+    def call(dtype=1, layout=0, heads=2, seq=4, d=64, table_dtype=1, rows=8, cols=32, pos=None, pos_dtype=7,
+             pos_count=0, start=0, rdim=0, x=None):
+        return lib.sa_rotary_embedding(x, x, dtype, layout, 1, heads, seq, d, None, None, table_dtype, rows, cols,
+                                       pos, pos_dtype, pos_count, start, 0, rdim, None, None)
+
+    assert call(dtype=7) == 3
+    assert call(table_dtype=10) == 3
+    assert call(layout=2) == 2
+    assert call(heads=0) == 1
+    assert call(d=63) == 2
+    assert call(rdim=70) == 1 and b"rotary_dim must be in 1..=head_dim" in lib.sa_last_error_string()
+    assert call(rdim=31, cols=15) == 1 and b"rotary_dim must be even" in lib.sa_last_error_string()
+    assert call(cols=16) == 2 and b"cache inner dim 16" in lib.sa_last_error_string()
+    assert call(start=5) == 2 and b"exceeds cos/sin table length" in lib.sa_last_error_string()
+    assert call(seq=0) == 0
+    assert call() == 9  # NULL tensors
+    assert ops.supports_op("RotaryEmbedding")
+
+
 def test_product_package_does_not_import_oracle():
     """The shipped package never reaches the CPU oracle."""
     pkg = ROOT / "smallaios_b200"
