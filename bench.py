@@ -760,6 +760,8 @@ def main():
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="heads mode: peer = the decode epilogue stores every rank's copy over NVLink "
                          "(symmetric memory) + one barrier; nccl = NCCL all-gather of attn_out")
+    ap.add_argument("--no-heads", action="store_true",
+                    help="N>1: time only the batch-sharded mode (by default the head-sharded mode is timed too)")
     ap.add_argument("--mode", default="batch", choices=["batch", "heads"],
                     help="N>1: batch = every rank decodes its own 64 sequences (weak scaling, no collective); "
                          "heads = the 64 sequences' KV heads split over the ranks, attn_out all-gathered over "
@@ -781,23 +783,19 @@ def main():
     if args.workload == "prefill":
         return run_prefill_attention(args)
 
-    import torch
-    import torch.distributed as dist
+    return run_gqa_decode(args)
 
-    import smallaios_b200 as sa
-    from smallaios_b200._lib import lib
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        from datetime import timedelta
+def measure_decode(args, torch, dist, sa, lib, dev, world, rank, local, *, heads, gather, e2e, cpu):
+    """Build the workload, time it and check it; returns the measurements (max over ranks).
 
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-
-    heads = args.mode == "heads" and world > 1
+    heads=False: every rank decodes its own B sequences (batch sharding, no collective).
+    heads=True (world > 1): the B sequences' KV heads are split over the ranks and attn_out is
+    gathered ("peer": the decode merge stores every rank's copy over NVLink and completes the
+    gather on the device; "nccl": NCCL all-gather after the local operator).
+    """
+    peer = None
+    shard = None
     if heads:
         from smallaios_b200 import sharding
 
@@ -806,38 +804,44 @@ def main():
         cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank, kv_begin=shard.kv_begin,
                                                   kv_count=kv_count)
         gathered = torch.empty(B, 1, HQ * D, dtype=q.dtype, device=dev)
-        peer = sharding.PeerGather((B, 1, HQ * D), q.dtype, dev) if args.gather == "peer" else None
+        peer = sharding.PeerGather((B, 1, HQ * D), q.dtype, dev) if gather == "peer" else None
     else:
         kv_count = HKV
         cache, cos, sin, q, k, v = build_workload(torch, sa, dev, seed=1000 + rank)
+        gathered = None
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
 
-    def gqa(q_, k_, v_):
+    def gqa(q_, k_, v_, out_=None, res_=None):
         cache.set_position(T - 1)
         if heads:
+            dst = gathered if res_ is None else res_
             res = sharding.sharded_group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV,
                                                          shard=shard, cos_cache=cos, sin_cache=sin, do_rotary=True,
-                                                         local_out=out, out=None if peer else gathered, gather=peer)
+                                                         local_out=out, out=None if peer else dst, gather=peer)
             if peer is not None:
-                gathered.copy_(res)
+                dst.copy_(res)
         else:
             sa.group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
-                                     sin_cache=sin, do_rotary=True, out=out)
-
-    def step():
-        gqa(q, k, v)
+                                     sin_cache=sin, do_rotary=True, out=out if out_ is None else out_)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
+    # Steps per graph: the fused gather alternates two buffer sets, so a graph holds one step per set.
+    spg = 2 if peer is not None else 1
+    replays = (args.steps + spg - 1) // spg
+    steps = replays * spg
+
+    def step():
+        for _ in range(spg):
+            gqa(q, k, v)
+
     for _ in range(args.warmup):
         step()
     barrier()
-    # One step captured as a CUDA graph (the library's calls are capturable:
-    # no host sync, no allocation); replays remove the host's per-launch cost.
     run, graph_launches, graph = step, None, None
     if not args.no_graph:
         graph = torch.cuda.CUDAGraph()
@@ -856,15 +860,15 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(replays):
         run()
     e1.record(stream)
     barrier()
-    launches = lib.sa_kernel_launches() - launches0 if graph_launches is None else graph_launches * args.steps
-    t_ms = e0.elapsed_time(e1) / args.steps
+    launches = lib.sa_kernel_launches() - launches0 if graph_launches is None else graph_launches * replays
+    t_ms = e0.elapsed_time(e1) / steps
     clocks = sampler.stop()
 
-    # Attention kernel(s) alone, for the roofline (no append).
+    # The attention call alone (prep + decode + merge, no append, no gather), for the roofline.
     for _ in range(3):
         cache.set_position(T - 1)
         sa.gqa_attend(q, cache, 0, num_heads=HQ, cos_cache=cos, sin_cache=sin, do_rotary=True, out=out)
@@ -879,83 +883,14 @@ def main():
     attend_launches = (lib.sa_kernel_launches() - la0) // args.steps
     attend_ms = a0.elapsed_time(a1) / args.steps
 
-    # End to end: pinned host q/k/v in, attn_out back to pinned host, every step.
-    hq_ = q.cpu().pin_memory()
-    hk_ = k.cpu().pin_memory()
-    hv_ = v.cpu().pin_memory()
-    hout = torch.empty_like(out, device="cpu").pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    e2e_res = None
+    if e2e:
+        e2e_res = measure_e2e(args, torch, sa, dev, stream, barrier, cache, cos, sin, q, k, v, out, gqa, heads,
+                              gathered, spg)
+    if heads:  # the last timed step's output again (the roofline loop above wrote only `out`)
+        step()
+        torch.cuda.synchronize(dev)
 
-    if heads:
-        hout = torch.empty_like(gathered, device="cpu").pin_memory()
-
-    def e2e_step():
-        dq.copy_(hq_, non_blocking=True)
-        dk.copy_(hk_, non_blocking=True)
-        dv.copy_(hv_, non_blocking=True)
-        gqa(dq, dk, dv)
-        hout.copy_(gathered if heads else out, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    barrier()
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    x1.record(stream)
-    barrier()
-    e2e_eager_ms = x0.elapsed_time(x1) / args.steps
-    # The same steps as a serving loop runs them: the copy-in of step i+1 (one stream)
-    # and the copy-out of step i-1 (another stream) overlap the compute of step i, with
-    # double-buffered device inputs/outputs.  Every step still copies its inputs in from
-    # pinned host memory and its attn_out back; the timed region covers all copies.
-    e2e_ms, e2e_mode = e2e_eager_ms, "host launches, copies serial with the compute"
-    if not heads:
-        cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        bufs = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(out))
-                for _ in range(2)]
-        houts = [torch.empty_like(out, device="cpu").pin_memory() for _ in range(2)]
-        ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("ready", "done", "copied")}
-
-        def pipelined(steps):
-            for i in range(steps):
-                sl = i % 2
-                dq_, dk_, dv_, do_ = bufs[sl]
-                with torch.cuda.stream(cs_in):
-                    if i >= 2:
-                        cs_in.wait_event(ev["done"][sl])  # step i-2 has read this slot's inputs
-                    dq_.copy_(hq_, non_blocking=True)
-                    dk_.copy_(hk_, non_blocking=True)
-                    dv_.copy_(hv_, non_blocking=True)
-                    ev["ready"][sl].record(cs_in)
-                stream.wait_event(ev["ready"][sl])
-                if i >= 2:
-                    stream.wait_event(ev["copied"][sl])  # step i-2's output has left this slot
-                cache.set_position(T - 1)
-                sa.group_query_attention(dq_, dk_, dv_, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
-                                         sin_cache=sin, do_rotary=True, out=do_)
-                ev["done"][sl].record(stream)
-                with torch.cuda.stream(cs_out):
-                    cs_out.wait_event(ev["done"][sl])
-                    houts[sl].copy_(do_, non_blocking=True)
-                    ev["copied"][sl].record(cs_out)
-            for sl in range(2):
-                stream.wait_event(ev["copied"][sl])
-
-        pipelined(4)
-        barrier()
-        x0.record(stream)
-        cs_in.wait_event(x0)
-        pipelined(args.steps)
-        x1.record(stream)
-        barrier()
-        e2e_ms = x0.elapsed_time(x1) / args.steps
-        e2e_mode = ("host launches; step i+1's copy-in and step i-1's copy-out overlap step i "
-                    "(two copy streams, double buffers)")
-
-    # Parity of the timed step's own output (outside every timed region): every rank checks a
-    # sample of its rows against the CPU oracle; the worst error over ranks is reported.
     parity = None
     if not args.no_parity:
         torch.cuda.synchronize(dev)
@@ -965,69 +900,236 @@ def main():
         cos_np, sin_np = rope_np(T, D, THETA)
         parity = parity_sample(torch, cache, q, k, res, cos_np, sin_np, kv_count, [0, B // 2, B - 1])
 
-    # max over ranks
+    status = cache.device_status(clear=True)
+
+    # max over ranks (every rank takes the same collective steps)
+    e2e_ms = e2e_res["ms_per_step"] if e2e_res else -1.0
+    e2e_host_ms = e2e_res["host_ms_per_step"] if e2e_res else -1.0
+    e2e_serial_ms = e2e_res["serial_ms_per_step"] if e2e_res else -1.0
     pmax = -1.0 if parity is None else parity["max_abs"]
     pbad = 0.0 if parity is None or parity["ok"] else 1.0
-    times = torch.tensor([t_ms, e2e_ms, attend_ms, e2e_eager_ms, pmax, pbad], device=dev, dtype=torch.float64)
+    vals = torch.tensor([t_ms, e2e_ms, attend_ms, e2e_host_ms, e2e_serial_ms, pmax, pbad, float(status)],
+                        device=dev, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, attend_ms, e2e_eager_ms, pmax, pbad = times.tolist()
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, attend_ms, e2e_host_ms, e2e_serial_ms, pmax, pbad, status = vals.tolist()
     if parity is not None:
         parity.update(max_abs=pmax, ok=pbad == 0.0, ranks=world)
-    rows_mult = 1 if heads else world  # sequences decoded per step = B * rows_mult
+    if e2e_res:
+        e2e_res.update(ms_per_step=e2e_ms, host_ms_per_step=e2e_host_ms, serial_ms_per_step=e2e_serial_ms)
 
-    peak, peak_kind = load_peaks()
-    abytes = attend_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV))  # this rank's share
-    achieved = abytes / (attend_ms * 1e-3) / 1e9
-    line = {
-        "metric": METRIC, "value": B * rows_mult / (t_ms * 1e-3), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms, "higher_is_better": True,
-        "scaling": "strong" if heads else "weak", "vs_baseline": None,
-        "dtype": "int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
-        "config": {"workload": WORKLOAD,
-                   "batch_per_gpu": B if not heads else f"{B} (kv heads {kv_count} of {HKV})",
-                   "global_batch": B * rows_mult, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": T,
-                   "kv_bits": BITS, "rope_theta": THETA,
-                   "parallelism": ((f"kv-head-sharded x{world}, " + ("attn_out stored to every rank by the decode "
-                                                                      "epilogue over NVLink + barrier"
-                                                                      if args.gather == "peer" else
-                                                                      "NCCL all-gather of attn_out"))
-                                   if heads else f"batch-sharded x{world} (no collective)"),
-                   "l2": f"cache {2 * B * HKV * T * (CB + 8) / 1e6:.0f} MB > 126 MB L2 per step; no flush",
-                   "launch": "host launches" if args.no_graph else "CUDA graph of one step, replayed"},
-        "gpu_launches": int(launches),
-        "e2e": {"value": B * rows_mult / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": int((q.numel() + k.numel() + v.numel()) * 2),
-                "d2h_bytes_per_step": int(hout.numel() * 2), "ms_per_step": e2e_ms, "mode": e2e_mode,
-                "serial_value": B * rows_mult / (e2e_eager_ms * 1e-3), "serial_ms_per_step": e2e_eager_ms},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": NCU_TRAFFIC_PER_CALL, "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM,
-                     "kernel": KERNEL_NOTE, "launches_per_call": attend_launches,
-                     "algorithmic_bytes": abytes, "ms_per_call": attend_ms,
-                     "peak_source": f"{peak_kind} hbm_gbs"},
-        "step_bytes": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)),  # per rank
-        "step_gbs": algorithmic_bytes(hkv=kv_count, hq=kv_count * (HQ // HKV)) / (t_ms * 1e-3) / 1e9,
-        "clocks": clocks,
-    }
-    if parity is not None:
-        line["parity_max_abs"] = parity["max_abs"]
-        line["parity"] = parity
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    cpu_line = None
+    if cpu:
         import oracle  # checker / CPU baseline only
 
         oracle.build()
         val, desc = cpu_sample(torch, cache, q, k, v, dev, target_s=8.0, nthreads=1)
-        line["cpu_baseline"] = {"value": val, "unit": UNIT, "cores": 1, "kind": "port", "sample": desc}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+        cpu_line = {"value": val, "unit": UNIT, "cores": 1, "kind": "port (sampled, scaled)", "sample": desc}
     cache.close()
     # a graph that holds NCCL calls must be released before the process group
     if graph is not None:
         torch.cuda.synchronize(dev)
         graph.reset()
         del graph
+    if e2e_res is not None:
+        e2e_res.pop("graph", None)
+    h2d = int((q.numel() + k.numel() + v.numel()) * 2)
+    d2h = int((gathered if heads else out).numel() * 2)
+    return dict(t_ms=t_ms, steps=steps, launches=launches, attend_ms=attend_ms, attend_launches=attend_launches,
+                kv_count=kv_count, clocks=clocks, parity=parity, e2e=e2e_res, h2d=h2d, d2h=d2h, cpu=cpu_line,
+                device_status=int(status), gather=gather if heads else None)
 
+
+def measure_e2e(args, torch, sa, dev, stream, barrier, cache, cos, sin, q, k, v, out, gqa, heads, gathered, spg):
+    """End to end: every step copies q/k/v in from pinned host memory and its attn_out back.
+
+    Three loops, all timed with CUDA events on the compute stream:
+      serial    copy-in, the operator, copy-out, one after the other (host launches);
+      host      step i+1's copy-in (one stream) and step i-1's copy-out (another stream) overlap
+                step i, double-buffered device inputs/outputs, launched from the host;
+      graph     the same pipeline for S consecutive steps captured as one CUDA graph and replayed
+                (the reported `e2e`; S divides the step count).
+    """
+    hq_ = q.cpu().pin_memory()
+    hk_ = k.cpu().pin_memory()
+    hv_ = v.cpu().pin_memory()
+    res_t = gathered if heads else out
+    hout = torch.empty_like(res_t, device="cpu").pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def serial_step():
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        gqa(dq, dk, dv)
+        hout.copy_(res_t, non_blocking=True)
+
+    for _ in range(3):
+        serial_step()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(args.steps):
+        serial_step()
+    x1.record(stream)
+    barrier()
+    serial_ms = x0.elapsed_time(x1) / args.steps
+
+    cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    bufs = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(res_t))
+            for _ in range(2)]
+    houts = [torch.empty_like(res_t, device="cpu").pin_memory() for _ in range(2)]
+    ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("ready", "done", "copied")}
+
+    def pipeline(nsteps, cur):
+        cs_in.wait_stream(cur)
+        cs_out.wait_stream(cur)
+        for i in range(nsteps):
+            sl = i % 2
+            dq_, dk_, dv_, do_ = bufs[sl]
+            with torch.cuda.stream(cs_in):
+                if i >= 2:
+                    cs_in.wait_event(ev["done"][sl])  # step i-2 has read this slot's inputs
+                dq_.copy_(hq_, non_blocking=True)
+                dk_.copy_(hk_, non_blocking=True)
+                dv_.copy_(hv_, non_blocking=True)
+                ev["ready"][sl].record(cs_in)
+            cur.wait_event(ev["ready"][sl])
+            if i >= 2:
+                cur.wait_event(ev["copied"][sl])  # step i-2's output has left this slot
+            if heads:
+                gqa(dq_, dk_, dv_, res_=do_)
+            else:
+                gqa(dq_, dk_, dv_, out_=do_)
+            ev["done"][sl].record(cur)
+            with torch.cuda.stream(cs_out):
+                cs_out.wait_event(ev["done"][sl])
+                houts[sl].copy_(do_, non_blocking=True)
+                ev["copied"][sl].record(cs_out)
+        cur.wait_stream(cs_in)
+        cur.wait_stream(cs_out)
+
+    pipeline(4, stream)
+    barrier()
+    x0.record(stream)
+    pipeline(args.steps, stream)
+    x1.record(stream)
+    barrier()
+    host_ms = x0.elapsed_time(x1) / args.steps
+
+    per_graph = next(s for s in (10, 8, 6, 5, 4, 2, 1) if args.steps % s == 0 and s % spg == 0) \
+        if args.steps % spg == 0 else None
+    graph_ms, mode = host_ms, "host launches (the step count does not split into graph replays)"
+    g = None
+    if per_graph is not None and not args.no_graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            pipeline(per_graph, torch.cuda.current_stream(dev))
+        for _ in range(2):
+            g.replay()
+        barrier()
+        x0.record(stream)
+        for _ in range(args.steps // per_graph):
+            g.replay()
+        x1.record(stream)
+        barrier()
+        graph_ms = x0.elapsed_time(x1) / args.steps
+        mode = (f"CUDA graph of {per_graph} pipelined steps, replayed: step i+1's copy-in and step i-1's "
+                f"copy-out overlap step i (two copy streams, double buffers); every step copies its q/k/v "
+                f"in from pinned host memory and its attn_out back")
+        torch.cuda.synchronize(dev)
+        g.reset()
+    return {"ms_per_step": graph_ms, "mode": mode, "host_ms_per_step": host_ms, "serial_ms_per_step": serial_ms}
+
+
+def decode_line(r, world, heads):
+    """The JSON fields of one measured decode mode."""
+    peak, peak_kind = load_peaks()
+    kv_count = r["kv_count"]
+    hq_local = kv_count * (HQ // HKV)
+    rows_mult = 1 if heads else world  # sequences decoded per step = B * rows_mult
+    abytes = attend_bytes(hkv=kv_count, hq=hq_local)  # this rank's share
+    achieved = abytes / (r["attend_ms"] * 1e-3) / 1e9
+    line = {
+        "value": B * rows_mult / (r["t_ms"] * 1e-3), "ms_per_step": r["t_ms"], "steps": r["steps"],
+        "gpu_launches": int(r["launches"]),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC_PER_CALL if not heads else None,
+                     "traffic_decode_stream": NCU_TRAFFIC_DECODE_STREAM if not heads else None,
+                     "kernel": KERNEL_NOTE, "launches_per_call": r["attend_launches"],
+                     "algorithmic_bytes": abytes, "ms_per_call": r["attend_ms"],
+                     "peak_source": f"{peak_kind} hbm_gbs", "per": "rank"},
+        "step_bytes": algorithmic_bytes(hkv=kv_count, hq=hq_local),  # per rank
+        "step_gbs": algorithmic_bytes(hkv=kv_count, hq=hq_local) / (r["t_ms"] * 1e-3) / 1e9,
+        "clocks": r["clocks"],
+        "device_status": r["device_status"],
+    }
+    if r["e2e"] is not None:
+        e = r["e2e"]
+        line["e2e"] = {"value": B * rows_mult / (e["ms_per_step"] * 1e-3), "unit": UNIT,
+                       "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+                       "ms_per_step": e["ms_per_step"], "mode": e["mode"],
+                       "host_launch_value": B * rows_mult / (e["host_ms_per_step"] * 1e-3),
+                       "serial_value": B * rows_mult / (e["serial_ms_per_step"] * 1e-3),
+                       "serial_ms_per_step": e["serial_ms_per_step"]}
+    if r["parity"] is not None:
+        line["parity_max_abs"] = r["parity"]["max_abs"]
+        line["parity"] = r["parity"]
+    return line
+
+
+def run_gqa_decode(args):
+    import torch
+    import torch.distributed as dist
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    heads = args.mode == "heads" and world > 1
+    r = measure_decode(args, torch, dist, sa, lib, dev, world, rank, local, heads=heads, gather=args.gather,
+                       e2e=True, cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
+    gather_desc = {"peer": "attn_out stored to every rank by the decode merge over NVLink, gather completed "
+                           "on the device (epoch signals, bounded wait)",
+                   "nccl": "NCCL all-gather of attn_out"}
+    line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong" if heads else "weak", "vs_baseline": None,
+            "dtype": "int4-kv/bf16-act/f32-acc", "data": "synthetic (seeded normal, std 1.28)",
+            "config": {"workload": WORKLOAD,
+                       "batch_per_gpu": B if not heads else f"{B} (kv heads {r['kv_count']} of {HKV})",
+                       "global_batch": B * (1 if heads else world), "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                       "context": T, "kv_bits": BITS, "rope_theta": THETA,
+                       "parallelism": (f"kv-head-sharded x{world}, {gather_desc[args.gather]}" if heads
+                                       else f"batch-sharded x{world} (no collective)"),
+                       "l2": f"cache {2 * B * HKV * T * (CB + 8) / 1e6:.0f} MB > 126 MB L2 per step; no flush",
+                       "launch": "host launches" if args.no_graph else "CUDA graph of the step, replayed"}}
+    line.update(decode_line(r, world, heads))
+    if r["cpu"] is not None:
+        line["cpu_baseline"] = r["cpu"]
+    if world > 1 and not heads and not args.no_heads:
+        # The head-sharded mode on the same ranks: the same B sequences split by KV head, gathered.
+        h = measure_decode(args, torch, dist, sa, lib, dev, world, rank, local, heads=True, gather=args.gather,
+                           e2e=False, cpu=False)
+        hl = decode_line(h, world, True)
+        t1 = r["t_ms"]  # every rank of the batch mode runs the whole one-GPU step
+        hl.update(gather=args.gather, gather_kind=gather_desc[args.gather], scaling="strong",
+                  global_batch=B, kv_heads_per_rank=h["kv_count"],
+                  efficiency_vs_1gpu=t1 / (world * h["t_ms"]),
+                  note="efficiency_vs_1gpu = (this mode's tokens/s) / (N x one GPU's tokens/s on the whole "
+                       "step); one GPU's step time is the batch mode's per-rank step")
+        line["heads"] = hl
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
 

@@ -184,11 +184,25 @@ int sa_kv_cache_layer_view(const sa_kv_cache *cache, int32_t layer, sa_kv_layer_
  * the local operator in the head-sharded mode: the decode kernel's epilogue
  * writes every rank's copy over NVLink.  q_heads_total must equal the cache's
  * num_heads and q_head_offset its kv_head_begin * group.  n = 0 turns it off.
- * The caller runs a cross-rank barrier after the call before any rank reads
- * its buffer, and alternates buffers between steps so that no rank writes a
- * buffer a peer may still be reading.  At most 8 buffers. */
-int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, int32_t q_head_offset,
-                           int32_t q_heads_total);
+ * At most 8 buffers.
+ *
+ * Completing the gather.  With signals == NULL the caller runs a cross-rank
+ * barrier after each call before any rank reads its buffer.  With `signals`
+ * (rank i's array of 10 uint32 words, zeroed before first use and mapped
+ * here like the buffers; this rank is index `rank`), the writing kernel
+ * completes it on the device: its last CTA publishes a step epoch into every
+ * peer's array (st.release.sys over NVLink) and waits until every peer has
+ * published it into this rank's (ld.acquire.sys), so the kernels that follow
+ * on the stream see the whole gathered tensor -- no host barrier, no extra
+ * launch, and a CUDA graph of the step stays valid (the epoch lives on the
+ * device).  The wait is bounded by timeout_us: when it runs out the kernel
+ * sets bit 0 of the device status (sa_kv_cache_device_status) and returns.
+ * Either way every rank makes the same calls in the same order, and
+ * alternates buffers between steps (at least two) so that no rank writes a
+ * buffer a peer may still be reading.  This has no counterpart in the
+ * reference, which runs on one device (onnx-rt/src/cuda/mod.rs:653-690). */
+int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, uint32_t *const *signals, int32_t n,
+                           int32_t rank, int32_t q_head_offset, int32_t q_heads_total, int64_t timeout_us);
 /* Copy of the cache configuration. */
 int sa_kv_cache_get_config(const sa_kv_cache *cache, sa_kv_cache_config *config);
 /* CompressedKVCache::memory_bytes (kv_compression.rs:928-957) of the rows

@@ -119,7 +119,8 @@ def _declare(l: ctypes.CDLL) -> None:
     l.sa_kv_cache_device_status.restype = ctypes.c_int
     l.sa_kv_cache_device_status.argtypes = [_P, ctypes.POINTER(_I32), _I32]
     l.sa_kv_cache_set_gather.restype = ctypes.c_int
-    l.sa_kv_cache_set_gather.argtypes = [_P, ctypes.POINTER(ctypes.c_void_p), _I32, _I32, _I32]
+    l.sa_kv_cache_set_gather.argtypes = [_P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _I32,
+                                         _I32, _I32, _I32, _I64]
     l.sa_kv_append.restype = ctypes.c_int
     l.sa_kv_append.argtypes = [_P, _I32, _P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _I32, _P]
     l.sa_gqa_attend.restype = ctypes.c_int

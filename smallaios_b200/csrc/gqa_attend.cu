@@ -13,6 +13,7 @@
 // rotates q once, streams codes without ever decoding a vector, and applies
 // the inverse rotation once per output row.
 #include "sa_common.cuh"
+#include "sa_gather.cuh"
 #include "sa_internal.h"
 
 namespace sa {
@@ -370,6 +371,7 @@ __global__ void __launch_bounds__(256) gather_scatter_kernel(const uint4 *src, G
         const uint4 x = s[i];
         for (int r = 0; r < g.n; r++) static_cast<uint4 *>(g.p[r])[row * dst_row_vecs + col_vecs + i] = x;
     }
+    if (g.sig[0]) gather_complete(g);
 }
 
 int launch_gather_scatter(const AttendArgs &a, cudaStream_t stream) {

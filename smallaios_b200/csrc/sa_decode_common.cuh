@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "sa_append.cuh"
+#include "sa_gather.cuh"
 
 namespace sa {
 namespace dec {
@@ -111,16 +112,27 @@ struct RecGeo {
     static constexpr int R = HPR * D, L = HPR * D + HPR, Z = HPR * D + 2 * HPR;
 };
 
+template <typename T, int D, int HPR>
+__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane);
+
 // Merge of each unit's partial records (one warp per query head), then
 // normalisation, inverse rotation and the store.  The records of unit u are
 // w_lo + u .. w_hi + u, one per decode warp whose range touched the unit.
+// In the head-sharded mode with signal arrays the launch also completes the
+// gather (sa_gather.cuh).
 template <typename T, int D, int HPR>
 __global__ void __launch_bounds__(32 * HPR) decode_merge_kernel(AttendArgs a, int ncu, int F, int W) {
-    using RG = RecGeo<D, HPR>;
-    constexpr int EPL = D / 32;
     const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
     griddep_wait();  // the decode grid's records
-    if (g >= a.group) return;
+    if (g < a.group) decode_merge_head<T, D, HPR>(a, ncu, F, W, g, lane);
+    if (a.gather.sig[0]) gather_complete(a.gather);  // every rank's heads are in this rank's buffer
+}
+
+// One query head's merge (warp g of the unit's CTA).
+template <typename T, int D, int HPR>
+__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane) {
+    using RG = RecGeo<D, HPR>;
+    constexpr int EPL = D / 32;
     const int u = blockIdx.x;
     const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
     const float *base = a.workspace + ((int64_t)u + w_lo) * RG::REC;  // record w_lo + u, then one per warp

@@ -26,11 +26,20 @@ constexpr int kMaxGather = 8;        // ranks of one node in the head-sharded mo
 // Head-sharded output: the attention output of this rank's query heads goes
 // to every buffer p[0..n) (this GPU's and its peers', mapped into this
 // process) at columns [col0, col0 + heads*group) of a [B][S][cols*D] tensor.
+// With signal arrays (sig[0] != nullptr) the writing kernel also completes
+// the gather on the device (sa_gather.cuh): sig[r] is rank r's array of
+// kMaxGather + 2 words, mapped here (one epoch per peer, then this rank's
+// CTA counter and epoch), and this rank is buffer `rank`.
 struct GatherOut {
     void *p[kMaxGather];
     int n;     // 0: plain attn_out
     int col0;  // first global query head of this rank
     int cols;  // query heads in total
+    uint32_t *sig[kMaxGather];  // nullptr: the caller synchronises the ranks itself
+    int rank;
+    uint32_t *state;      // sig[rank] + kMaxGather: {CTA counter, epoch}
+    int *status;          // this cache's device status word
+    uint64_t timeout_ns;  // bound of the wait for the peers' epochs
 };
 
 struct kv_cache_impl {

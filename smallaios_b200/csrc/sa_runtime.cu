@@ -291,8 +291,8 @@ int sa_kv_cache_device_status(sa_kv_cache *cache, int32_t *status, int32_t clear
     return rc;
 }
 
-int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, int32_t q_head_offset,
-                           int32_t q_heads_total) {
+int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, uint32_t *const *signals, int32_t n,
+                           int32_t rank, int32_t q_head_offset, int32_t q_heads_total, int64_t timeout_us) {
     if (!cache) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: NULL cache");
     kv_cache_impl *k = reinterpret_cast<kv_cache_impl *>(cache);
     if (n == 0) {
@@ -313,6 +313,22 @@ int sa_kv_cache_set_gather(sa_kv_cache *cache, void *const *buffers, int32_t n, 
     for (int i = 0; i < n; i++) {
         if (!buffers[i]) return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: NULL buffer %d", i);
         g.p[i] = buffers[i];
+    }
+    if (signals) {
+        if (rank < 0 || rank >= n)
+            return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: rank %d outside %d buffers", rank, n);
+        if (timeout_us <= 0)
+            return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: timeout must be > 0 (got %lld us)",
+                             (long long)timeout_us);
+        for (int i = 0; i < n; i++) {
+            if (!signals[i])
+                return set_error(SA_ERR_INVALID_ARGUMENT, "kv_cache_set_gather: NULL signal array %d", i);
+            g.sig[i] = signals[i];
+        }
+        g.rank = rank;
+        g.state = signals[rank] + kMaxGather;  // {CTA counter, epoch} beside this rank's signals
+        g.status = k->dev_status;
+        g.timeout_ns = (uint64_t)timeout_us * 1000u;
     }
     g.n = n;
     g.col0 = q_head_offset;

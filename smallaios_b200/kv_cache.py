@@ -255,11 +255,18 @@ class GpuKvCache:
                         dst = dst[:, :, :t.shape[2]]
                     dst.copy_(t.to(cache.device))
             torch.cuda.synchronize(cache.device)
+            cache.set_position(pos)
         except Exception:
             cache.close()
             raise
-        cache.set_position(pos)
         return cache
+
+    def device_status(self, clear: bool = False) -> int:
+        """Device-side status bits of the kernels that used this cache: 0, or bit 0 when a bounded
+        wait inside a kernel gave up (that call's output is not valid).  Synchronises."""
+        st = ctypes.c_int32()
+        check(lib.sa_kv_cache_device_status(self.handle, ctypes.byref(st), int(bool(clear))))
+        return st.value
 
     def close(self) -> None:
         if self._handle:

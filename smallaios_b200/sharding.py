@@ -12,8 +12,9 @@ without a collective on its data path except in the head-sharded mode:
   ``B*S*(Hq/G)*D`` activations), and the gathered ``[G][B][S][Hq/G*D]`` is
   returned in the operator's ``[B][S][Hq*D]`` head order.  With a
   ``PeerGather`` the collective disappears into the decode kernel instead: its
-  epilogue stores every rank's copy over NVLink into symmetric-memory buffers
-  (``sa_kv_cache_set_gather``), and one signal-pad barrier completes them.
+  merge epilogue stores every rank's copy over NVLink into symmetric-memory
+  buffers (``sa_kv_cache_set_gather``) and completes the gather on the device
+  with per-step epoch signals and a bounded wait.
 * **Batch sharding.** Rank r owns whole sequences; no collective.
 
 The reference runs one process on one device; its executor would call the
@@ -91,18 +92,27 @@ def gather_head_shards(local_out: torch.Tensor, shard: HeadShard, group=None,
 class PeerGather:
     """Gathered-output buffers in symmetric memory for the fused head-sharded gather.
 
-    Every rank allocates ``nbuf`` buffers of ``shape`` (``(B, S, Hq*D)``) with
-    torch's symmetric memory, so each rank's buffers are mapped into every
-    rank.  A step points the cache at one buffer set (``sa_kv_cache_set_gather``),
-    the decode writes this rank's heads into all ranks' copies, and the
-    buffer's signal-pad barrier makes the gathered output complete on every
-    rank.  Buffers alternate between steps, so a rank never writes a buffer a
-    peer may still be reading.
+    Every rank allocates ``nbuf`` buffers of ``shape`` (``(B, S, Hq*D)``) and one
+    signal array with torch's symmetric memory, so each rank's buffers and
+    signals are mapped into every rank.  A step points the cache at one buffer
+    set (``sa_kv_cache_set_gather``): the attention's merge kernel stores this
+    rank's heads into all ranks' copies over NVLink, then its last CTA publishes
+    the step's epoch to every peer and waits (bounded by ``timeout_ms``) until
+    every peer has published it here.  When the operator's kernels finish, the
+    gathered output is complete on this rank: no host barrier, no extra launch.
+    Buffers alternate between steps, so a rank never writes a buffer a peer may
+    still be reading; a CUDA graph of the loop therefore holds one step per
+    buffer (the epoch itself lives on the device and advances on every replay).
+    A wait that runs out sets the cache's device status (``cache.device_status()``).
     """
 
-    def __init__(self, shape, dtype, device, group=None, nbuf: int = 2):
+    SIGNAL_WORDS = 16  # one epoch per rank (up to 8), the CTA counter and the epoch, padded
+
+    def __init__(self, shape, dtype, device, group=None, nbuf: int = 2, timeout_ms: float = 1000.0):
         from torch.distributed import _symmetric_memory as symm_mem
 
+        if nbuf < 2:
+            raise ValueError("PeerGather: at least two buffers alternate")
         group = group if group is not None else dist.group.WORLD
         self.bufs, self.handles, self.ptrs = [], [], []
         for _ in range(nbuf):
@@ -112,6 +122,16 @@ class PeerGather:
             self.bufs.append(t)
             self.handles.append(h)
             self.ptrs.append((ctypes.c_void_p * len(ptrs))(*ptrs))
+        self.signals = symm_mem.empty((self.SIGNAL_WORDS,), dtype=torch.int32, device=device)
+        self.signals.zero_()
+        self.sig_handle = symm_mem.rendezvous(self.signals, group)
+        sp = list(self.sig_handle.buffer_ptrs)
+        self.sig_ptrs = (ctypes.c_void_p * len(sp))(*sp)
+        self.rank = self.sig_handle.rank
+        self.timeout_us = max(1, int(timeout_ms * 1000))
+        # every rank's signals are zero before any rank's kernel can publish into them
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group, device_ids=[torch.device(device).index])
         self.next = 0
 
     def step(self, cache, shard: HeadShard, num_heads: int, run):
@@ -119,13 +139,12 @@ class PeerGather:
         i = self.next
         self.next = (i + 1) % len(self.bufs)
         ptrs = self.ptrs[i]
-        _raise_op(lib.sa_kv_cache_set_gather(cache.handle, ptrs, len(ptrs), shard.q_begin, num_heads),
-                  "kv_cache_set_gather")
+        _raise_op(lib.sa_kv_cache_set_gather(cache.handle, ptrs, self.sig_ptrs, len(ptrs), self.rank, shard.q_begin,
+                                             num_heads, self.timeout_us), "kv_cache_set_gather")
         try:
             run()
         finally:
-            _raise_op(lib.sa_kv_cache_set_gather(cache.handle, None, 0, 0, 0), "kv_cache_set_gather")
-        self.handles[i].barrier(channel=0)
+            _raise_op(lib.sa_kv_cache_set_gather(cache.handle, None, None, 0, 0, 0, 0, 0), "kv_cache_set_gather")
         return self.bufs[i]
 
 

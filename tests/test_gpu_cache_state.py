@@ -90,3 +90,22 @@ def test_state_rejects_mismatched_options(cuda_device):
         sa.GpuKvCache.from_state_dict(st, device=cuda_device)
     with pytest.raises(ValueError):
         sa.GpuKvCache.from_state_dict({"format": "other"}, device=cuda_device)
+
+
+def test_state_with_position_beyond_capacity_frees_the_new_cache(cuda_device):
+    """A saved position past max_seq_len raises, and the cache built for it is released."""
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import SaError
+
+    a = sa.GpuKvCache(1, 2, 64, 32, device=cuda_device)
+    a.append(0, torch.zeros(1, 4, 128, device=cuda_device), torch.ones(1, 4, 128, device=cuda_device))
+    a.advance_position(4)
+    st = a.state_dict()
+    a.close()
+    st["position"] = 33
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(cuda_device)[0]
+    with pytest.raises(SaError, match="position"):
+        sa.GpuKvCache.from_state_dict(st, device=cuda_device)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda_device)[0] >= free0

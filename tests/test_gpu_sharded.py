@@ -72,6 +72,38 @@ def _worker(rank, world, port, result_path):
                 kv_num_heads=HKV, shard=shard, cos_cache=tcos, sin_cache=tsin, do_rotary=True, gather=gather)
             torch.cuda.synchronize(dev)
             peer_ok = peer_ok and torch.equal(got, out)
+        # A CUDA graph of two fused steps (one per buffer), replayed with new queries each time:
+        # every replay's gathered outputs must equal the NCCL gather of the same step.
+        qd = local(q, qs).clone()
+        kd, vd = local(k[:, T - 1:], ks).clone(), local(v[:, T - 1:], ks).clone()
+        res = [torch.empty(B, 1, HQ * D, device=dev) for _ in range(2)]
+
+        def two_steps():
+            for j in range(2):
+                cache.set_position(T - 1)
+                g = sharding.sharded_group_query_attention(
+                    qd, kd, vd, cache, LAYER, num_heads=HQ, kv_num_heads=HKV, shard=shard, cos_cache=tcos,
+                    sin_cache=tsin, do_rotary=True, gather=gather)
+                res[j].copy_(g)
+
+        two_steps()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            two_steps()
+        for it in range(4):
+            qn = (rng(500 + it).standard_normal((B, 1, HQ, D)) * 1.28).astype(np.float32)
+            qd.copy_(local(qn, qs))
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            cache.set_position(T - 1)
+            ref = sharding.sharded_group_query_attention(
+                qd, kd, vd, cache, LAYER, num_heads=HQ, kv_num_heads=HKV, shard=shard, cos_cache=tcos,
+                sin_cache=tsin, do_rotary=True)
+            torch.cuda.synchronize(dev)
+            peer_ok = peer_ok and torch.equal(res[0], ref) and torch.equal(res[1], ref)
+        graph.reset()
+        peer_ok = peer_ok and cache.device_status() == 0
         # this rank's codes against the oracle for its global heads
         signs = oracle.cache_signs(oracle.DEFAULT_SEED, LAYERS, HKV, D)[LAYER]
         kc, km, vc, vm = oracle_append(k[:, :, ks], v[:, :, ks], signs[ks], BITS, 0, cos, sin, True, False)
