@@ -812,18 +812,27 @@ def measure_decode(args, torch, dist, sa, lib, dev, world, rank, local, *, heads
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
 
+    last = {}
+
     def gqa(q_, k_, v_, out_=None, res_=None):
+        """One operator call; returns the tensor holding the step's attn_out.  With the fused
+        gather that is the gather buffer itself (valid until two steps later) unless `res_` asks
+        for a copy, which the end-to-end loop makes before its copy-out stream reads it."""
         cache.set_position(T - 1)
         if heads:
             dst = gathered if res_ is None else res_
             res = sharding.sharded_group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV,
                                                          shard=shard, cos_cache=cos, sin_cache=sin, do_rotary=True,
                                                          local_out=out, out=None if peer else dst, gather=peer)
-            if peer is not None:
-                dst.copy_(res)
+            if peer is not None and res_ is not None:
+                res_.copy_(res)
+                res = res_
         else:
+            res = out if out_ is None else out_
             sa.group_query_attention(q_, k_, v_, cache, 0, num_heads=HQ, kv_num_heads=HKV, cos_cache=cos,
-                                     sin_cache=sin, do_rotary=True, out=out if out_ is None else out_)
+                                     sin_cache=sin, do_rotary=True, out=res)
+        last["res"] = res
+        return res
 
     def barrier():
         if world > 1:
@@ -895,8 +904,8 @@ def measure_decode(args, torch, dist, sa, lib, dev, world, rank, local, *, heads
     if not args.no_parity:
         torch.cuda.synchronize(dev)
         res = out
-        if heads and peer is not None:  # the fused gather wrote the rank's heads into `gathered` only
-            res = gathered[..., shard.q_begin * D:(shard.q_begin + shard.q_count) * D]
+        if heads:  # the rank's own heads of the gathered output of the last step
+            res = last["res"][..., shard.q_begin * D:(shard.q_begin + shard.q_count) * D]
         cos_np, sin_np = rope_np(T, D, THETA)
         parity = parity_sample(torch, cache, q, k, res, cos_np, sin_np, kv_count, [0, B // 2, B - 1])
 
@@ -961,8 +970,7 @@ def measure_e2e(args, torch, sa, dev, stream, barrier, cache, cos, sin, q, k, v,
         dq.copy_(hq_, non_blocking=True)
         dk.copy_(hk_, non_blocking=True)
         dv.copy_(hv_, non_blocking=True)
-        gqa(dq, dk, dv)
-        hout.copy_(res_t, non_blocking=True)
+        hout.copy_(gqa(dq, dk, dv), non_blocking=True)
 
     for _ in range(3):
         serial_step()

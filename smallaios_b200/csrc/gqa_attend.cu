@@ -286,13 +286,18 @@ int launch_generic(const AttendArgs &a, int n_splits, int tps, cudaStream_t stre
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return check_cuda(e, "gqa_attend smem attribute");
     }
-    const int rows = a.batch * a.seq_len;
-    dim3 grid(n_splits, a.heads, rows);
+    const int64_t rows = (int64_t)a.batch * a.seq_len;
+    if (rows > 65535 || a.heads * a.group > 65535)  // grid y/z limits of the split and combine launches
+        return set_error(SA_ERR_UNSUPPORTED,
+                         "gqa_attend: batch*seq_len = %lld query rows exceed the 65535 rows one call of the "
+                         "general attention kernel takes; split the call into chunks of fewer rows",
+                         (long long)rows);
+    dim3 grid(n_splits, a.heads, (unsigned)rows);
     kern<<<grid, 32 * kWarps, smem, stream>>>(a, n_splits, tps);
     count_launch();
     int rc = check_cuda(cudaGetLastError(), "gqa_attend split launch");
     if (rc != SA_OK || n_splits == 1) return rc;
-    attend_combine_kernel<T, EPL><<<dim3(a.heads * a.group, rows), 32, 0, stream>>>(a, n_splits);
+    attend_combine_kernel<T, EPL><<<dim3(a.heads * a.group, (unsigned)rows), 32, 0, stream>>>(a, n_splits);
     count_launch();
     return check_cuda(cudaGetLastError(), "gqa_attend combine launch");
 }
