@@ -82,6 +82,7 @@ __global__ void __launch_bounds__(320) decode_prep8_kernel(AttendArgs a, AppendA
     const int q0w = do_append ? 2 : 0;
     const float *sg = a.signs + (int64_t)h * D;
     griddep_launch_dependents();
+    griddep_wait();  // launched as a dependent of the kernel before it: q and the cache are ready
     if (do_append && warp < 2) {
         encode_append_vector<T, EPL>(ap, b, 0, h, warp, lane, s_codes[warp]);
         return;
@@ -554,10 +555,20 @@ int launch8_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream
     AppendArgs apv{};
     if (ap) apv = *ap;
     const int prep_warps = (do_append ? 2 : 0) + 8;
-    decode_prep8_kernel<T, BITS, D><<<dim3(a.heads, a.batch), 32 * prep_warps, 0, stream>>>(a, apv, do_append,
-                                                                                             qfrag, qscal);
+    // prep, decode and merge are programmatic dependents of the kernel before them
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.heads, a.batch);
+    cfg.blockDim = dim3(32 * prep_warps);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    int rc = check_cuda(cudaLaunchKernelEx(&cfg, decode_prep8_kernel<T, BITS, D>, a, apv, do_append, qfrag, qscal),
+                        "gqa decode8 prep launch");
     count_launch();
-    int rc = check_cuda(cudaGetLastError(), "gqa decode8 prep launch");
     if (rc != SA_OK) return rc;
 
     auto kern = decode8_stream_kernel<T, BITS, D>;
@@ -571,10 +582,6 @@ int launch8_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream
         if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
     }
     const DecodeGrid8 dg = decode8_grid<BITS, D>(a);
-    cudaLaunchAttribute pdl[1];
-    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pdl[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)dg.ctas);
     cfg.blockDim = dim3(kNW8 * 32);
     cfg.dynamicSmemBytes = smem;

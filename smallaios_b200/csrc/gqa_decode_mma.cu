@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     // the decode kernel may start now: it waits for this grid before it
     // reads the q digits or the appended token
     griddep_launch_dependents();
+    griddep_wait();  // launched as a dependent of the kernel before it: q and the cache are ready
     if (do_append && warp < 2) {
         encode_append_vector<T, EPL>(ap, b, 0, h, warp, lane, s_codes[warp]);
         return;
@@ -583,10 +584,22 @@ int launch_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream)
     AppendArgs apv{};
     if (ap) apv = *ap;
     const int prep_warps = (do_append ? 2 : 0) + 4;  // the append warps, then one warp per fragment head
-    decode_prep_kernel<T, BITS, D><<<dim3(a.heads, a.batch), 32 * prep_warps, 0, stream>>>(a, apv, do_append,
-                                                                                            qfrag, qscal);
+    // All three launches are programmatic dependents of the kernel before them (prep of whatever
+    // kernel precedes the call), so each launch overlaps the tail of the one before; each kernel
+    // waits for its predecessor's grid before it reads what that grid wrote.
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.heads, a.batch);
+    cfg.blockDim = dim3(32 * prep_warps);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    int rc = check_cuda(cudaLaunchKernelEx(&cfg, decode_prep_kernel<T, BITS, D>, a, apv, do_append, qfrag, qscal),
+                        "gqa decode prep launch");
     count_launch();
-    int rc = check_cuda(cudaGetLastError(), "gqa decode prep launch");
     if (rc != SA_OK) return rc;
 
     using GG = WGeo<BITS, D>;
@@ -601,12 +614,6 @@ int launch_shape(const AttendArgs &a, const AppendArgs *ap, cudaStream_t stream)
         if (dev >= 0 && dev < 64) __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
     }
     const DecodeGrid dg = decode_grid<BITS, D>(a);
-    // decode and merge are launched as programmatic dependents of the kernel
-    // before them, so their launch overlaps its tail
-    cudaLaunchAttribute pdl[1];
-    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pdl[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)dg.ctas);
     cfg.blockDim = dim3(kNW * 32);
     cfg.dynamicSmemBytes = smem;

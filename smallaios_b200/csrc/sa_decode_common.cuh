@@ -6,6 +6,8 @@
 
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "sa_append.cuh"
 #include "sa_gather.cuh"
 
@@ -113,7 +115,8 @@ struct RecGeo {
 };
 
 template <typename T, int D, int HPR>
-__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane);
+__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane,
+                                                  const float (&sgw)[D / 32]);
 
 // Merge of each unit's partial records (one warp per query head), then
 // normalisation, inverse rotation and the store.  The records of unit u are
@@ -122,52 +125,89 @@ __device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, 
 // gather (sa_gather.cuh).
 template <typename T, int D, int HPR>
 __global__ void __launch_bounds__(32 * HPR) decode_merge_kernel(AttendArgs a, int ncu, int F, int W) {
+    constexpr int EPL = D / 32;
     const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+    // The next kernel of the stream may be scheduled now; a kernel of this library launched as a
+    // programmatic dependent waits for this grid before it reads anything.
+    griddep_launch_dependents();
+    // signs * 1/sqrt(n) of this unit's KV head: not written by the decode, so read before the wait
+    float sgw[EPL];
+    {
+        const float *sg = a.signs + (int64_t)(blockIdx.x % a.heads) * D + lane * EPL;
+#pragma unroll
+        for (int rr = 0; rr < EPL; rr++) sgw[rr] = a.wht_scale * sg[rr];
+    }
     griddep_wait();  // the decode grid's records
-    if (g < a.group) decode_merge_head<T, D, HPR>(a, ncu, F, W, g, lane);
+    if (g < a.group) decode_merge_head<T, D, HPR>(a, ncu, F, W, g, lane, sgw);
     if (a.gather.sig[0]) gather_complete(a.gather);  // every rank's heads are in this rank's buffer
 }
 
-// One query head's merge (warp g of the unit's CTA).
+// One query head's merge (warp g of the unit's CTA).  Up to kMergeBatch
+// records (the common case: a unit spans a handful of decode warps) are merged
+// with every load issued up front, so the merge costs one L2 round trip.
+constexpr int kMergeBatch = 8;
+
 template <typename T, int D, int HPR>
-__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane) {
+__device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, int F, int W, int g, int lane,
+                                                  const float (&sgw)[D / 32]) {
     using RG = RecGeo<D, HPR>;
     constexpr int EPL = D / 32;
+    using VT = typename std::conditional<EPL == 4, float4, float2>::type;
     const int u = blockIdx.x;
     const int w_lo = warp_of_chunk(u * ncu, F, W), w_hi = warp_of_chunk(u * ncu + ncu - 1, F, W);
     const float *base = a.workspace + ((int64_t)u + w_lo) * RG::REC;  // record w_lo + u, then one per warp
     const int nrec = w_hi - w_lo + 1;
-    // lane i handles the meta of records i, i + 32, ...
-    float M = -INFINITY;
-    for (int i = lane; i < nrec; i += 32) M = fmaxf(M, base[(int64_t)i * RG::REC + RG::R + g]);
-    M = warp_max(M);
     float x[EPL], L = 0.0f, Z = 0.0f;
 #pragma unroll
     for (int rr = 0; rr < EPL; rr++) x[rr] = 0.0f;
-    for (int i0 = 0; i0 < nrec; i0 += 32) {
-        float wt = 0.0f;
-        if (i0 + lane < nrec) {
-            const float *m = base + (int64_t)(i0 + lane) * RG::REC;
-            const float Rw = m[RG::R + g];
-            wt = Rw == -INFINITY ? 0.0f : exp2f(Rw - M);
-            L = fmaf(wt, m[RG::L + g], L);
-            Z = fmaf(wt, m[RG::Z + g], Z);
+    if (nrec <= kMergeBatch) {
+        float Rm = -INFINITY, Lm = 0.0f, Zm = 0.0f;
+        if (lane < nrec) {
+            const float *m = base + (int64_t)lane * RG::REC;
+            Rm = m[RG::R + g];
+            Lm = m[RG::L + g];
+            Zm = m[RG::Z + g];
         }
-        const int n = min(32, nrec - i0);
-#pragma unroll 4
-        for (int j = 0; j < n; j++) {
-            const float wj = __shfl_sync(0xffffffffu, wt, j);
-            const float *v = base + (int64_t)(i0 + j) * RG::REC + g * D + lane * EPL;
-            if constexpr (EPL == 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(v);
-                x[0] = fmaf(wj, t.x, x[0]);
-                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
-                x[2 % EPL] = fmaf(wj, t.z, x[2 % EPL]);
-                x[3 % EPL] = fmaf(wj, t.w, x[3 % EPL]);
-            } else {
-                const float2 t = *reinterpret_cast<const float2 *>(v);
-                x[0] = fmaf(wj, t.x, x[0]);
-                x[1 % EPL] = fmaf(wj, t.y, x[1 % EPL]);
+        VT vals[kMergeBatch];
+#pragma unroll
+        for (int j = 0; j < kMergeBatch; j++) {
+            if (j < nrec) vals[j] = *reinterpret_cast<const VT *>(base + (int64_t)j * RG::REC + g * D + lane * EPL);
+        }
+        const float M = warp_max(Rm);
+        const float wt = Rm == -INFINITY ? 0.0f : exp2f(Rm - M);
+        L = wt * Lm;
+        Z = wt * Zm;
+#pragma unroll
+        for (int j = 0; j < kMergeBatch; j++) {
+            if (j < nrec) {
+                const float wj = __shfl_sync(0xffffffffu, wt, j);
+                const float *t = reinterpret_cast<const float *>(&vals[j]);
+#pragma unroll
+                for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wj, t[rr], x[rr]);
+            }
+        }
+    } else {
+        // lane i handles the meta of records i, i + 32, ...
+        float M = -INFINITY;
+        for (int i = lane; i < nrec; i += 32) M = fmaxf(M, base[(int64_t)i * RG::REC + RG::R + g]);
+        M = warp_max(M);
+        for (int i0 = 0; i0 < nrec; i0 += 32) {
+            float wt = 0.0f;
+            if (i0 + lane < nrec) {
+                const float *m = base + (int64_t)(i0 + lane) * RG::REC;
+                const float Rw = m[RG::R + g];
+                wt = Rw == -INFINITY ? 0.0f : exp2f(Rw - M);
+                L = fmaf(wt, m[RG::L + g], L);
+                Z = fmaf(wt, m[RG::Z + g], Z);
+            }
+            const int n = min(32, nrec - i0);
+#pragma unroll 8
+            for (int j = 0; j < n; j++) {
+                const float wj = __shfl_sync(0xffffffffu, wt, j);
+                const VT tv = *reinterpret_cast<const VT *>(base + (int64_t)(i0 + j) * RG::REC + g * D + lane * EPL);
+                const float *t = reinterpret_cast<const float *>(&tv);
+#pragma unroll
+                for (int rr = 0; rr < EPL; rr++) x[rr] = fmaf(wj, t[rr], x[rr]);
             }
         }
     }
@@ -178,9 +218,8 @@ __device__ __forceinline__ void decode_merge_head(const AttendArgs &a, int ncu, 
     for (int rr = 0; rr < EPL; rr++) x[rr] = L > 0.0f ? (x[rr] + Z) * inv : 0.0f;
     warp_wht_butterfly<EPL>(x, lane, D);
     const int h = u % a.heads;
-    const float *sg = a.signs + (int64_t)h * D;
 #pragma unroll
-    for (int rr = 0; rr < EPL; rr++) x[rr] *= a.wht_scale * sg[lane * EPL + rr];
+    for (int rr = 0; rr < EPL; rr++) x[rr] *= sgw[rr];
     if (a.gather.n == 0) {
         T *dst = static_cast<T *>(a.out) + ((int64_t)u * a.group + g) * D;
 #pragma unroll
