@@ -779,9 +779,240 @@ int launch_packed(const void *a, const uint8_t *packed, const void *bias, void *
     return check_cuda(cudaGetLastError(), "MatMulNBits packed launch");
 }
 
+// ---- decode GEMV path, m <= 4 rows -------------------------------------------
+// The decode projections (one token per sequence, or a few) stream each weight
+// byte once, so they are HBM-bound if the per-code arithmetic stays below the
+// issue budget.  One CTA = 4 warps over 32 output columns; warp w reduces over
+// the w-th quarter of K and streams its 32 columns' codes and scales through
+// two shared-memory slots, 8 k-blocks (128 B of codes per column) per chunk:
+// one 2-D TMA copy of the 32 x 128 B code tile (128-byte swizzle) and one of
+// the 32 x 8 scales.  One ldmatrix.x4 gives a lane the fragment words of two
+// k-blocks for its rows g and g + 8 (the swizzle keeps the eight rows of each
+// 8 x 16 B matrix on distinct banks).  The dequant and the mma.m16n8k16 with
+// exact products and fp32 block sums are those of mnb_mma_kernel; the block
+// scale multiplies each block's sum in fp32.  The activation rows are turned
+// into B fragments once per CTA (permuted to the dequant's k order, odd pairs
+// pre-divided by 16 for fp16) and read with one 16-byte load per block.  The
+// weight copies are issued before the kernel waits for the previous grid (it
+// is a programmatic dependent launch): only the activations come from it.
+constexpr int kGvSplit = 4;                          // warps per CTA, each over a quarter of K
+constexpr int kGvCols = 32;                          // output columns per CTA (two 16-row MMA tiles)
+constexpr int kGvChunk = 8;                          // k-blocks per chunk
+constexpr int kGvSlots = 2;                          // chunks in flight per warp
+constexpr int kGvCodeTile = kGvCols * 128;           // 4096 B, 1024-aligned for the swizzle
+constexpr int kGvScaleTile = kGvCols * kGvChunk * 2; // 512 B
+// One activation row: with more rows the staged fragments push the CTA past four per SM and
+// the K-split kernel below is as fast (B200, C2 shape: m = 2 and 4 measured 14.1 and 14.6 us
+// here, with two warps of four slots 12.4 and 18.8 us).
+constexpr int kGvMaxM = 1;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kGvSplit)
+    mnb_gemv_tc_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_scales,
+                       const T *__restrict__ a, const T *__restrict__ bias, T *__restrict__ y, int m, int n, int k) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nblk = k / 32;
+    const int nbw = nblk / kGvSplit;  // k-blocks of this warp: a multiple of kGvChunk
+    const int nchunks = nbw / kGvChunk;
+    unsigned char *codes = smem + warp * kGvSlots * kGvCodeTile;
+    unsigned char *scl = smem + kGvSplit * kGvSlots * kGvCodeTile + warp * kGvSlots * kGvScaleTile;
+    uint4 *afrag = reinterpret_cast<uint4 *>(smem + kGvSplit * kGvSlots * (kGvCodeTile + kGvScaleTile));
+    uint64_t *bar_base = reinterpret_cast<uint64_t *>(afrag + (size_t)nblk * 4 * m);
+    uint64_t *bars = bar_base + warp * kGvSlots;
+    uint64_t *act_bar = bar_base + kGvSplit * kGvSlots;
+    float *red = reinterpret_cast<float *>(act_bar + 1);
+    const int n0 = blockIdx.x * kGvCols;
+    const int b0 = warp * nbw;
+    if (lane == 0) {
+        for (int i = 0; i < kGvSlots; i++) mbar_init(bars + i, 1);
+        if (warp == 0) mbar_init(act_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    auto issue = [&](int c) {  // lane 0: chunk c -> slot c % kGvSlots
+        const int s = c % kGvSlots;
+        const int blk = b0 + c * kGvChunk;
+        mbar_expect_tx(bars + s, kGvCodeTile + kGvScaleTile);
+        tma_load_2d(codes + s * kGvCodeTile, &tm_codes, blk * 16, n0, bars + s);
+        tma_load_2d(scl + s * kGvScaleTile, &tm_scales, blk, n0, bars + s);
+    };
+    // the weights do not depend on the kernel before this one: start streaming them now
+    if (lane == 0)
+        for (int c = 0; c < kGvSlots && c < nchunks; c++) issue(c);
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");  // the activations
+    // The m activation rows, one bulk copy each, then every 16-byte unit turned in place into the B
+    // fragment words of its k-block: [row][blk][t] = halves 8t..8t+7 as (h0,h4), (h1,h5)/16,
+    // (h2,h6), (h3,h7)/16 (the dequant's pair order; the 1/16 meets the in-place fp16 high nibbles).
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(act_bar, (uint32_t)(m * k * 2));
+        for (int r = 0; r < m; r++)
+            bulk_g2s(afrag + (size_t)r * nblk * 4, a + (int64_t)r * k, (uint32_t)(k * 2), act_bar);
+    }
+    bool ok = mbar_wait_bounded(act_bar, 0u);
+    if (ok) {
+        for (int i = threadIdx.x; i < nblk * 4 * m; i += blockDim.x) {
+            const uint4 x = afrag[i];
+            uint4 f;
+            f.x = __byte_perm(x.x, x.z, 0x5410);
+            f.y = mnb_act_scale_odd<T>(__byte_perm(x.x, x.z, 0x7632));
+            f.z = __byte_perm(x.y, x.w, 0x5410);
+            f.w = mnb_act_scale_odd<T>(__byte_perm(x.y, x.w, 0x7632));
+            afrag[i] = f;
+        }
+    }
+    __syncthreads();
+
+    // ldmatrix row addresses: lane L feeds row (L & 7) + 8 * ((L >> 3) & 1) of a 16-row tile, at
+    // 16-byte unit (block) + (L >> 4); the 128-byte swizzle puts unit u of row r at u ^ (r & 7)
+    const int lrow = (lane & 7) + 8 * ((lane >> 3) & 1), lunit = lane >> 4;
+    const bool has_row = g < m;
+    float tot[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) tot[nt][0] = tot[nt][1] = tot[nt][2] = tot[nt][3] = 0.0f;
+    int c = 0;
+    for (; c < nchunks; c++) {
+        const int s = c % kGvSlots;
+        if (ok && !mbar_wait_bounded(bars + s, (uint32_t)((c / kGvSlots) & 1))) ok = false;
+        if (__any_sync(0xffffffffu, !ok)) break;  // a copy never landed: give up (output left unwritten)
+        const uint32_t ct = smem_u32(codes + s * kGvCodeTile);
+        const unsigned char *sc = scl + s * kGvScaleTile;
+        // this lane's scales of the chunk's 8 blocks, rows 16 nt + g and 16 nt + g + 8
+        uint4 srow[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            srow[nt][0] = *reinterpret_cast<const uint4 *>(sc + (16 * nt + g) * kGvChunk * 2);
+            srow[nt][1] = *reinterpret_cast<const uint4 *>(sc + (16 * nt + g + 8) * kGvChunk * 2);
+        }
+        const int blk0 = b0 + c * kGvChunk;
+#pragma unroll
+        for (int bp = 0; bp < kGvChunk; bp += 2) {
+            uint4 bf[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                bf[h] = has_row ? afrag[((size_t)g * nblk + blk0 + bp + h) * 4 + t] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                const int row = 16 * nt + lrow;
+                uint32_t w[4];  // rows g, g+8 of block bp; rows g, g+8 of block bp+1
+                ldsm_x4(w, ct + row * 128 + (((bp + lunit) ^ (row & 7)) << 4));
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint32_t q0[4], q1[4];
+                    dq_word<T>(w[2 * h], q0);
+                    dq_word<T>(w[2 * h + 1], q1);
+                    const int bi = bp + h;
+                    const uint32_t sw0 = (&srow[nt][0].x)[bi >> 1], sw1 = (&srow[nt][1].x)[bi >> 1];
+                    const T s0 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw0) + (bi & 1));
+                    const T s1 = *reinterpret_cast<const T *>(reinterpret_cast<const uint16_t *>(&sw1) + (bi & 1));
+                    float acc[4];
+                    mma_16816<T>(acc, q0[0], q1[0], q0[1], q1[1], bf[h].x, bf[h].y, true);
+                    mma_16816<T>(acc, q0[2], q1[2], q0[3], q1[3], bf[h].z, bf[h].w, false);
+                    ffma2(tot[nt][0], tot[nt][1], DT<T>::to_f32(s0), acc[0], acc[1]);
+                    ffma2(tot[nt][2], tot[nt][3], DT<T>::to_f32(s1), acc[2], acc[3]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && c + kGvSlots < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            issue(c + kGvSlots);
+        }
+    }
+    if (!ok && lane == 0) {
+        // a copy never landed: let this warp's copies still in flight land (bounded)
+        for (int cc = c; cc < c + kGvSlots && cc < nchunks; cc++)
+            mbar_wait_bounded(bars + cc % kGvSlots, (uint32_t)((cc / kGvSlots) & 1));
+        if (warp == 0) mbar_wait_bounded(act_bar, 0u);
+    }
+    // sum the K quarters: warps 1.. leave their sums in shared memory, warp 0 adds and stores
+    if (warp > 0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) red[((warp - 1) * 32 + lane) * 8 + nt * 4 + j] = tot[nt][j];
+    }
+    const int bad = __syncthreads_or(!ok);
+    if (warp != 0 || bad) return;
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int row = 2 * t + (j & 1);
+            if (row < m) {
+                float v = tot[nt][j];
+#pragma unroll
+                for (int w = 1; w < kGvSplit; w++) v += red[((w - 1) * 32 + lane) * 8 + nt * 4 + j];
+                const int col = n0 + 16 * nt + g + ((j & 2) ? 8 : 0);
+                if (bias) v += DT<T>::to_f32(bias[col]);
+                st_from_f32(y + (int64_t)row * n + col, v);
+            }
+        }
+    }
+}
+
+size_t mnb_gemv_tc_smem(int64_t m, int64_t k) {
+    return 1024 + (size_t)kGvSplit * kGvSlots * (kGvCodeTile + kGvScaleTile) + (size_t)(k / 32) * 4 * m * 16 +
+           (kGvSplit * kGvSlots + 1) * 8 + (size_t)(kGvSplit - 1) * 32 * 8 * 4;
+}
+
+bool mnb_gemv_tc_eligible(int64_t m, int64_t n, int64_t k) {
+    return m >= 1 && m <= kGvMaxM && n % kGvCols == 0 && k % (32 * kGvSplit * kGvChunk) == 0 &&
+           mnb_gemv_tc_smem(m, k) <= 200 * 1024;
+}
+
+template <typename T>
+int launch_gemv_tc(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m, int64_t n,
+                   int64_t k, cudaStream_t stream) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return set_error(SA_ERR_CUDA, "MatMulNBits: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap tm_codes, tm_scales;
+    const cuuint32_t ones[2] = {1, 1};
+    const cuuint64_t cdim[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n}, cstride[1] = {(cuuint64_t)(k / 2)};
+    const cuuint32_t cbox[2] = {kGvChunk * 16, kGvCols};
+    CUresult r = encode(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(b), cdim, cstride, cbox,
+                        ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: code tensor map (%d)", (int)r);
+    const cuuint64_t sdim[2] = {(cuuint64_t)(k / 32), (cuuint64_t)n}, sstride[1] = {(cuuint64_t)(k / 32) * 2};
+    const cuuint32_t sbox[2] = {kGvChunk, kGvCols};
+    r = encode(&tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(scales), sdim, sstride, sbox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SA_ERR_CUDA, "MatMulNBits: scale tensor map (%d)", (int)r);
+    const size_t smem = mnb_gemv_tc_smem(m, k);
+    auto kern = mnb_gemv_tc_kernel<T>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "MatMulNBits gemv smem attribute");
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(n / kGvCols));
+    cfg.blockDim = dim3(32 * kGvSplit);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tm_codes, tm_scales, static_cast<const T *>(a), static_cast<const T *>(bias),
+                           static_cast<T *>(y), (int)m, (int)n, (int)k);
+    count_launch();
+    return check_cuda(e, "MatMulNBits gemv launch");
+}
+
 template <typename T>
 int launch_mma_rows(const void *a, const uint8_t *b, const void *scales, const void *bias, void *y, int64_t m,
                     int64_t n, int64_t k, cudaStream_t stream) {
+    if (mnb_gemv_tc_eligible(m, n, k)) return launch_gemv_tc<T>(a, b, scales, bias, y, m, n, k, stream);
     if (m <= 8) {
         // (chunks of two 128-byte sub-tiles per row, SUB = 2, measured slower on B200: 20.8 vs 16.8 us at m = 8)
         if (n % 32 == 0) return launch_mma<T, 1, 2>(a, b, scales, bias, y, m, n, k, stream);

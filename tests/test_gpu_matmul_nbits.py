@@ -70,11 +70,11 @@ def test_block_sizes_zero_points_bias(cuda_device, block):
     _run(cuda_device, 2, 200, 512, block=block, zp=True, bias=True, seed=block)
 
 
-@pytest.mark.parametrize("m", [1, 5, 8, 9, 16, 23, 33, 64])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 9, 16, 23, 33, 64])
 @pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
 def test_tensor_core_path(cuda_device, m, adtype):
-    """The mma.sync path (fp16/bf16, block 32, default zero point, K % 1024 == 0, m <= 64; N = 448 is not a
-    multiple of 128, so the tcgen05 path does not take it)."""
+    """The mma.sync paths (fp16/bf16, block 32, default zero point, K % 1024 == 0, m <= 64: the decode GEMV for
+    m = 1, the K-split kernel above it; N = 448 is not a multiple of 128, so the tcgen05 path does not take it)."""
     _run(cuda_device, m, 448, 2048, adtype=adtype, bias=True, seed=100 + m)
 
 
@@ -150,3 +150,12 @@ def test_c2_shape_m128_fp16(cuda_device):
 def test_tcgen05_row_blocks(cuda_device, m):
     """More than 128 rows (prefill): blocks of 128 activation rows, the last one ragged."""
     _run(cuda_device, m, 1024, 2048, adtype=torch.bfloat16, bias=True, seed=500 + m)
+
+
+@pytest.mark.parametrize("m", [1, 4])
+@pytest.mark.parametrize("adtype", [torch.float16, torch.bfloat16])
+def test_decode_gemv_c2_shape(cuda_device, m, adtype):
+    """m = 1 (the decode GEMV kernel) and m = 4 (the K-split kernel) at config 2's K=4096, N=14336, and at
+    K=14336 (a down projection)."""
+    _run(cuda_device, m, 14336, 4096, adtype=adtype, bias=True, seed=300 + m)
+    _run(cuda_device, m, 4096, 14336, adtype=adtype, seed=310 + m)
