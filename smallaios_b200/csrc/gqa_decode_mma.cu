@@ -98,12 +98,11 @@ __global__ void __launch_bounds__(192) decode_prep_kernel(AttendArgs a, AppendAr
     const T *src = static_cast<const T *>(a.query) + ((int64_t)b * qheads + h * G + g) * D;
     float x[EPL];
 #pragma unroll
-    for (int r = 0; r < EPL; r++) {
-        const int e = lane * EPL + r;
-        x[r] = ld_f32(src + e);
-        if (a.do_rotary) x[r] = rope_element(src, x[r], e, D, a.pos0, a.cos_cache, a.sin_cache, a.interleaved);
-        x[r] *= sg[e];
-    }
+    for (int r = 0; r < EPL; r++) x[r] = 0.0f;
+    load_elems<T, EPL>(src + lane * EPL, x);
+    if (a.do_rotary) rope_lane<EPL>(x, lane, D, a.pos0, a.cos_cache, a.sin_cache, a.interleaved);
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] *= sg[lane * EPL + r];
     warp_wht_butterfly<EPL>(x, lane, D);
     float sum = 0.0f, mabs = 0.0f;
     const float *vtr = a.lr_vtr ? a.lr_vtr + bh * D : nullptr;

@@ -8,21 +8,29 @@ namespace {
 
 constexpr int kAppendWarps = 4;
 
-template <typename T, int EPL>
+// IDX = uint32_t when every vector index fits 32 bits (the common case: 64-bit division costs
+// tens of instructions per warp), else int64_t.
+template <typename T, int EPL, typename IDX>
 __global__ void __launch_bounds__(32 * kAppendWarps) kv_append_kernel(AppendArgs a) {
     __shared__ uint8_t s_codes[kAppendWarps][256];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int64_t vec = (int64_t)blockIdx.x * kAppendWarps + warp;
-    const int64_t nvec = (int64_t)a.batch * a.seq_len * a.heads * 2;
+    const IDX vec = (IDX)blockIdx.x * kAppendWarps + warp;
+    const IDX nvec = (IDX)a.batch * a.seq_len * a.heads * 2;
     if (vec >= nvec) return;
     const int which = (int)(vec & 1);  // 0 = K, 1 = V
-    int64_t rest = vec >> 1;
-    const int h = (int)(rest % a.heads);
-    rest /= a.heads;
-    const int s = (int)(rest % a.seq_len);
-    const int b = (int)(rest / a.seq_len);
+    IDX rest = vec >> 1;
+    const int h = (int)(rest % (IDX)a.heads);
+    rest /= (IDX)a.heads;
+    const int s = (int)(rest % (IDX)a.seq_len);
+    const int b = (int)(rest / (IDX)a.seq_len);
     encode_append_vector<T, EPL>(a, b, s, h, which, lane, s_codes[warp]);
+}
+
+template <typename T, int EPL>
+void launch_epl(const AppendArgs &a, dim3 grid, dim3 block, bool small, cudaStream_t stream) {
+    if (small) kv_append_kernel<T, EPL, uint32_t><<<grid, block, 0, stream>>>(a);
+    else kv_append_kernel<T, EPL, int64_t><<<grid, block, 0, stream>>>(a);
 }
 
 template <typename T>
@@ -32,12 +40,13 @@ int launch_t(const AppendArgs &a, cudaStream_t stream) {
     const int64_t blocks = (nvec + kAppendWarps - 1) / kAppendWarps;
     if (blocks > 0x7fffffff) return set_error(SA_ERR_UNSUPPORTED, "kv_append: too many vectors");
     dim3 grid((unsigned)blocks), block(32 * kAppendWarps);
+    const bool small = blocks * kAppendWarps < ((int64_t)1 << 32);
     switch (a.head_dim) {
-        case 16: kv_append_kernel<T, 1><<<grid, block, 0, stream>>>(a); break;
-        case 32: kv_append_kernel<T, 1><<<grid, block, 0, stream>>>(a); break;
-        case 64: kv_append_kernel<T, 2><<<grid, block, 0, stream>>>(a); break;
-        case 128: kv_append_kernel<T, 4><<<grid, block, 0, stream>>>(a); break;
-        case 256: kv_append_kernel<T, 8><<<grid, block, 0, stream>>>(a); break;
+        case 16: launch_epl<T, 1>(a, grid, block, small, stream); break;
+        case 32: launch_epl<T, 1>(a, grid, block, small, stream); break;
+        case 64: launch_epl<T, 2>(a, grid, block, small, stream); break;
+        case 128: launch_epl<T, 4>(a, grid, block, small, stream); break;
+        case 256: launch_epl<T, 8>(a, grid, block, small, stream); break;
         default: return set_error(SA_ERR_UNSUPPORTED, "kv_append: head_dim %d not supported", a.head_dim);
     }
     count_launch();

@@ -6,6 +6,8 @@
 // the decode prep kernel.
 #pragma once
 
+#include <type_traits>
+
 #include "sa_common.cuh"
 #include "sa_internal.h"
 
@@ -41,6 +43,63 @@ __device__ __forceinline__ float rope_element(const T *src, float x, int e, int 
     return first ? __fsub_rn(__fmul_rn(c, x), __fmul_rn(sn, xo)) : __fadd_rn(__fmul_rn(sn, xo), __fmul_rn(c, x));
 }
 
+// The EPL consecutive elements at p as f32: one vector load when p is aligned to their size.
+template <typename T, int EPL>
+__device__ __forceinline__ void load_elems(const T *p, float (&x)[EPL]) {
+    constexpr int kBytes = EPL * (int)sizeof(T);
+    if constexpr (kBytes == 16 || kBytes == 8 || kBytes == 4) {
+        if ((reinterpret_cast<uintptr_t>(p) & (kBytes - 1)) == 0) {
+            using V = typename std::conditional<kBytes == 16, uint4,
+                                                typename std::conditional<kBytes == 8, uint2, uint32_t>::type>::type;
+            union {
+                V v;
+                T t[EPL];
+            } u;
+            u.v = *reinterpret_cast<const V *>(p);
+#pragma unroll
+            for (int r = 0; r < EPL; r++) x[r] = DT<T>::to_f32(u.t[r]);
+            return;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < EPL; r++) x[r] = ld_f32(p + r);
+}
+
+// RoPE of the EPL consecutive elements lane * EPL .. of a d-element vector held by a warp
+// (rotate_rope_block, ops/microsoft.rs:137-160: y0 = c*x0 - s*x1, y1 = s*x0 + c*x1, each
+// product rounded before the add).  The partner of element e is e ^ 1 (interleaved) or e +- d/2,
+// held by lane ^ (d / 2 / EPL) at the same slot, so it comes by a shuffle instead of a reload.
+// All 32 lanes must call it; lanes past d hold zeros and are left alone.
+template <int EPL>
+__device__ __forceinline__ void rope_lane(float (&x)[EPL], int lane, int d, int64_t pos, const float *cos_cache,
+                                          const float *sin_cache, int interleaved) {
+    float xp[EPL];
+    if (interleaved) {
+        if constexpr (EPL >= 2) {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) xp[r] = x[r ^ 1];
+        } else {
+            xp[0] = __shfl_xor_sync(0xffffffffu, x[0], 1);
+        }
+    } else {
+        const int m = d / 2 / EPL;
+#pragma unroll
+        for (int r = 0; r < EPL; r++) xp[r] = __shfl_xor_sync(0xffffffffu, x[r], m);
+    }
+    if (lane * EPL < d) {
+        const int half = d / 2;
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            const int e = lane * EPL + r;
+            const bool first = interleaved ? (e & 1) == 0 : e < half;
+            const int pair = interleaved ? e >> 1 : (first ? e : e - half);
+            const float c = cos_cache[pos * half + pair], sn = sin_cache[pos * half + pair];
+            x[r] = first ? __fsub_rn(__fmul_rn(c, x[r]), __fmul_rn(sn, xp[r]))
+                         : __fadd_rn(__fmul_rn(sn, xp[r]), __fmul_rn(c, x[r]));
+        }
+    }
+}
+
 // Encode and store vector (b, s, h, which) of an append (which: 0 = K, 1 = V).
 // All 32 lanes of the warp must call it; s_codes holds >= head_dim bytes.
 template <typename T, int EPL>
@@ -51,13 +110,14 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
     const bool active = lane * EPL < d;
     const T *src = static_cast<const T *>(which ? a.value : a.key) + (((int64_t)b * a.seq_len + s) * a.heads + h) * d;
     float x[EPL];
+    if (active) {
+        load_elems<T, EPL>(src + lane * EPL, x);
+    } else {
 #pragma unroll
-    for (int r = 0; r < EPL; r++) x[r] = active ? ld_f32(src + lane * EPL + r) : 0.0f;
-    if (which == 0 && a.do_rotary && active) {
-#pragma unroll
-        for (int r = 0; r < EPL; r++)
-            x[r] = rope_element(src, x[r], lane * EPL + r, d, pos, a.cos_cache, a.sin_cache, a.interleaved);
+        for (int r = 0; r < EPL; r++) x[r] = 0.0f;
     }
+    if (which == 0 && a.do_rotary)  // warp-uniform
+        rope_lane<EPL>(x, lane, d, pos, a.cos_cache, a.sin_cache, a.interleaved);
 
     float x0[EPL];  // the vector as written (after RoPE): the QJL residual is taken against it
 #pragma unroll
