@@ -218,9 +218,10 @@ int sa_kv_cache_memory_bytes(const sa_kv_cache *cache, uint64_t *reference_bytes
 int sa_kv_cache_device_status(sa_kv_cache *cache, int32_t *status, int32_t clear);
 
 /* Quantize-on-append: GpuKvCache::append (kv_cache.rs:233-277) fused with
- * CompressedKVCache::write_kv (kv_compression.rs:814-854, kv_qjl_residual and
- * kv_lowrank_k off) and with the K half of gqa_apply_rotary
- * (ops/microsoft.rs:1004-1050).
+ * CompressedKVCache::write_kv (kv_compression.rs:814-854) and with the K half of
+ * gqa_apply_rotary (ops/microsoft.rs:1004-1050).  With the cache's qjl_residual
+ * option it also stores each vector's QJL residual (:826-840), and with
+ * lowrank_k it updates the low-rank K state (:842-853), as write_kv does.
  *
  * key/value: (batch, seq_len, kv_head_count * head_dim) in `dtype`.  Token s
  * is written at position (cache position + s); RoPE on K uses that position
