@@ -159,3 +159,11 @@ def test_decode_gemv_c2_shape(cuda_device, m, adtype):
     K=14336 (a down projection)."""
     _run(cuda_device, m, 14336, 4096, adtype=adtype, bias=True, seed=300 + m)
     _run(cuda_device, m, 4096, 14336, adtype=adtype, seed=310 + m)
+
+
+@pytest.mark.parametrize("n,k", [(2400, 768), (7104, 256), (47360, 512), (16, 256), (28672, 4096)])
+def test_m1_shapes(cuda_device, n, k):
+    """m = 1 at widths and depths the decode GEMV does not take (K not a multiple of 1024, N not a
+    multiple of 32: the K-split kernel) and at the fused gate|up width (28672 x 4096, the GEMV)."""
+    _run(cuda_device, 1, n, k, adtype=torch.float16, bias=True, seed=n + k)
+    _run(cuda_device, 1, n, k, adtype=torch.bfloat16, seed=n + k + 1)
