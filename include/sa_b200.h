@@ -317,6 +317,11 @@ int sa_gqa_attend_no_alloc(const sa_kv_layer_view *layer, int64_t past_len, cons
  *   y            (m, n) in dtype
  * y[i][j] = sum_k a[i][k] * (code[j][k] - zp[j][k/bs]) * scale[j][k/bs] (+ bias[j]),
  * accumulated in f32.  bits must be 4; block_size a power of two >= 16.
+ * b and scales are weights (ONNX initializers): the 16-bit tensor-core kernels
+ * are programmatic dependent launches that start streaming them before the
+ * kernel ahead of them on the stream has finished, so no kernel enqueued just
+ * before the call may still be writing them (a copy or a synchronised stream
+ * is fine).  a, bias and y are only touched after that kernel completes.
  * ====================================================================== */
 int sa_matmul_nbits(const void *a, const uint8_t *b, const void *scales,
                     const uint8_t *zero_points, const void *bias, void *y,

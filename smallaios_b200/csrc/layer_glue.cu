@@ -21,6 +21,28 @@ __device__ __forceinline__ float glue_ld(const T *p, int64_t i) {
     return ld_f32(p + i);
 }
 
+// Both kernels run as programmatic dependent launches: the next kernel may be scheduled at
+// once (it waits for this grid before it reads what this grid writes), and this grid waits
+// for the previous one before it touches global memory.
+__device__ __forceinline__ void glue_pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+
+template <typename K, typename... Args>
+cudaError_t glue_launch(K kern, dim3 grid, cudaStream_t stream, Args... args) {
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kGlueThreads);
+    cfg.stream = stream;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // pre = x (+ skip) (+ bias); y = pre / sqrt(mean(pre^2) + eps) * w.
 // `pre` (optional) receives the rounded pre-sum: the residual of the next add.
 template <typename T>
@@ -30,6 +52,7 @@ __global__ void __launch_bounds__(kGlueThreads)
     __shared__ float s_red[kGlueThreads / 32];
     const int64_t base = (int64_t)blockIdx.x * cols;
     const int tid = threadIdx.x;
+    glue_pdl_enter();
     float ss = 0.0f;
     for (int i = tid; i < cols; i += kGlueThreads) {
         float v = glue_ld(x, base + i);
@@ -62,6 +85,7 @@ __global__ void __launch_bounds__(kGlueThreads)
     silu_mul_kernel(const T *__restrict__ gate, const T *__restrict__ up, int64_t ld_in, T *__restrict__ y,
                     int cols) {
     const int64_t r = blockIdx.y;
+    glue_pdl_enter();
     for (int j = blockIdx.x * kGlueThreads + threadIdx.x; j < cols; j += gridDim.x * kGlueThreads) {
         const float g = glue_ld(gate, r * ld_in + j), u = glue_ld(up, r * ld_in + j);
         st_from_f32(y + r * cols + j, g / (1.0f + expf(-g)) * u);
@@ -71,11 +95,12 @@ __global__ void __launch_bounds__(kGlueThreads)
 template <typename T>
 int launch_rms_t(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int64_t rows,
                  int64_t cols, float eps, cudaStream_t stream) {
-    rms_norm_kernel<T><<<(unsigned)rows, kGlueThreads, 0, stream>>>(
-        static_cast<const T *>(x), static_cast<const T *>(skip), static_cast<const T *>(bias),
-        static_cast<const T *>(w), static_cast<T *>(y), static_cast<T *>(pre), (int)cols, eps);
+    const cudaError_t e = glue_launch(rms_norm_kernel<T>, dim3((unsigned)rows), stream, static_cast<const T *>(x),
+                                      static_cast<const T *>(skip), static_cast<const T *>(bias),
+                                      static_cast<const T *>(w), static_cast<T *>(y), static_cast<T *>(pre), (int)cols,
+                                      eps);
     count_launch();
-    return check_cuda(cudaGetLastError(), "rms_norm launch");
+    return check_cuda(e, "rms_norm launch");
 }
 
 template <typename T>
@@ -83,10 +108,11 @@ int launch_silu_t(const void *gate, const void *up, int64_t ld_in, void *y, int6
                   cudaStream_t stream) {
     const int64_t blocks = (cols + kGlueThreads - 1) / kGlueThreads;
     const unsigned bx = (unsigned)(blocks < 64 ? blocks : 64);
-    silu_mul_kernel<T><<<dim3(bx, (unsigned)rows), kGlueThreads, 0, stream>>>(
-        static_cast<const T *>(gate), static_cast<const T *>(up), ld_in, static_cast<T *>(y), (int)cols);
+    const cudaError_t e = glue_launch(silu_mul_kernel<T>, dim3(bx, (unsigned)rows), stream,
+                                      static_cast<const T *>(gate), static_cast<const T *>(up), ld_in,
+                                      static_cast<T *>(y), (int)cols);
     count_launch();
-    return check_cuda(cudaGetLastError(), "silu_mul launch");
+    return check_cuda(e, "silu_mul launch");
 }
 
 }  // namespace

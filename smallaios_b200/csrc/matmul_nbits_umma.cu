@@ -218,6 +218,17 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     int issued = 0;  // producer: stages issued
     if (warp == 0) {
         if (lane == 0) {
+            auto load_act = [&](int c) {
+                unsigned char *st = smem + (c % GG::NS) * GG::STAGE;
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, (cb + c) * kUmKC + 64 * j,
+                                m0, full + c % GG::NS);
+            };
+            // The weights do not depend on the kernel before this one (a programmatic dependent
+            // launch may run this grid while it finishes): the first stages' codes and scales are
+            // requested before the wait for the activations.
+            const int pre = nchunks < GG::NS ? nchunks : GG::NS;
             for (int c = 0; c < nchunks; c++) {
                 const int s = c % GG::NS;
                 if (c >= GG::NS && !um_wait(empty + s, (uint32_t)(((c / GG::NS) - 1) & 1), abort_flag)) break;
@@ -226,10 +237,12 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 const int cg = cb + c;  // chunk of the tile's K
                 tma_load_2d(st, &tm_codes, cg * 128, n0, full + s);
                 tma_load_2d(st + kUmCodeTile, &tm_scales, cg * 8, n0, full + s);
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    tma_load_2d(st + kUmCodeTile + kUmScaleTile + j * GG::ACT_SUB, &tm_act, cg * kUmKC + 64 * j, m0,
-                                   full + s);
+                if (c + 1 == pre) {
+                    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+                    for (int c2 = 0; c2 < pre; c2++) load_act(c2);
+                } else if (c >= pre) {
+                    load_act(c);
+                }
                 issued = c + 1;
             }
         }
@@ -356,20 +369,27 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     const uint32_t tl = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
     bool ok = true;
     if (epi) {
+        asm volatile("griddepcontrol.wait;\n" ::: "memory");  // y (and bias) may belong to the previous kernel
         ok = um_wait(dfull, 0, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
     }
     // this CTA's f32 sums of output column n0 + row, 16 activation rows at a time
+    // (the accumulators' sum, in accumulator order; up to four TMEM loads in flight per wait)
     auto load_sums = [&](int c0, float (&acc)[16]) {
+        constexpr int G = GG::NACC < 4 ? GG::NACC : 4;
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = 0.0f;
-        for (int d = 0; d < GG::NACC; d++) {  // the accumulators' sum
-            uint32_t v[16];
-            tmem_ld16(tl + (uint32_t)(d * BN + c0), v);
+#pragma unroll
+        for (int d0 = 0; d0 < GG::NACC; d0 += G) {
+            uint32_t v[G][16];
+#pragma unroll
+            for (int d = 0; d < G; d++) tmem_ld16(tl + (uint32_t)((d0 + d) * BN + c0), v[d]);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(v[i]);
+            for (int d = 0; d < G; d++)
+#pragma unroll
+                for (int i = 0; i < 16; i++) acc[i] += __uint_as_float(v[d][i]);
         }
     };
     // split-K: ranks 1.. store their sums into rank 0's shared memory ([rank-1][column][row], the
@@ -469,8 +489,10 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
     cudaGetDevice(&dev);
     const int tiles = (int)(n / kUmBM);
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(kUmThreads);
     cfg.dynamicSmemBytes = GG::SMEM;
     cfg.stream = stream;
@@ -507,6 +529,7 @@ int launch_umma_bn(const void *a, const uint8_t *b, const void *scales, const vo
     at[0].val.clusterDim.x = (unsigned)split;
     at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(tiles * split), (unsigned)((m + BN - 1) / BN));
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tm_codes, tm_scales, tm_act, static_cast<const T *>(bias),
                                        static_cast<T *>(y), (int)m, (int)n, (int)k, qa);
     count_launch();
