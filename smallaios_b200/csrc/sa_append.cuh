@@ -100,6 +100,118 @@ __device__ __forceinline__ void rope_lane(float (&x)[EPL], int lane, int d, int6
     }
 }
 
+// PolarQuantizer::encode (kv_compression.rs:216-267) of NV vectors a warp holds, EPL elements
+// per lane each (x, rotated in place): apply_signs, butterfly and 1/sqrt_approx(n) (:81-123), the
+// first-occurrence min / max, scale = range / levels and codes round_f32((v - zp) / scale).  sg
+// holds this lane's signs (1 on inactive lanes), shared by the NV vectors.  The vectors are
+// independent: each step is issued for all of them before the next, so their shuffle and
+// reduction latencies overlap.  All 32 lanes must call it.
+template <int EPL, int NV = 1>
+__device__ __forceinline__ void polar_encode_warp(float (&x)[NV][EPL], const float (&sg)[EPL], bool active, int lane,
+                                                  int d, float wht_scale, uint32_t levels,
+                                                  uint32_t (&qc)[NV][EPL], float (&scale)[NV], float (&zp)[NV]) {
+#pragma unroll
+    for (int v = 0; v < NV; v++)
+#pragma unroll
+        for (int r = 0; r < EPL; r++) x[v][r] = __fmul_rn(x[v][r], sg[r]);
+    // the butterfly (warp_wht_butterfly) of the NV vectors, stage by stage
+#pragma unroll
+    for (int hs = 1; hs < EPL; hs <<= 1)
+#pragma unroll
+        for (int v = 0; v < NV; v++)
+#pragma unroll
+            for (int r = 0; r < EPL; r++)
+                if ((r & hs) == 0) {
+                    const float p0 = x[v][r], p1 = x[v][r + hs];
+                    x[v][r] = __fadd_rn(p0, p1);
+                    x[v][r + hs] = __fsub_rn(p0, p1);
+                }
+    for (int lm = 1; lm < d / EPL; lm <<= 1) {
+        float other[NV][EPL];
+#pragma unroll
+        for (int v = 0; v < NV; v++)
+#pragma unroll
+            for (int r = 0; r < EPL; r++) other[v][r] = __shfl_xor_sync(0xffffffffu, x[v][r], lm);
+#pragma unroll
+        for (int v = 0; v < NV; v++)
+#pragma unroll
+            for (int r = 0; r < EPL; r++)
+                x[v][r] = (lane & lm) ? __fsub_rn(other[v][r], x[v][r]) : __fadd_rn(x[v][r], other[v][r]);
+    }
+#pragma unroll
+    for (int v = 0; v < NV; v++)
+#pragma unroll
+        for (int r = 0; r < EPL; r++) x[v][r] = __fmul_rn(x[v][r], wht_scale);
+
+    // min / max with strict comparisons in index order: the first occurrence
+    // wins, as in the sequential loop of encode (this matters for +-0).
+    float mn[NV], mx[NV];
+    int imn[NV], imx[NV];
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        mn[v] = INFINITY;
+        mx[v] = -INFINITY;
+        imn[v] = imx[v] = 0x7fffffff;
+        if (active) {
+#pragma unroll
+            for (int r = 0; r < EPL; r++) {
+                const int e = lane * EPL + r;
+                if (x[v][r] < mn[v]) {
+                    mn[v] = x[v][r];
+                    imn[v] = e;
+                }
+                if (x[v][r] > mx[v]) {
+                    mx[v] = x[v][r];
+                    imx[v] = e;
+                }
+            }
+        }
+    }
+    // Across the warp: the extreme value by an integer reduction over an order-preserving key
+    // (-0 and +0 share the key of +0, since they compare equal), then the lowest element index
+    // among the lanes holding that value, and that element's own bits.
+    int kmn[NV], kmx[NV], wmn[NV], wmx[NV];
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        kmn[v] = __reduce_min_sync(0xffffffffu, order_key(mn[v] + 0.0f));
+        kmx[v] = __reduce_max_sync(0xffffffffu, order_key(mx[v] + 0.0f));
+    }
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        wmn[v] = __reduce_min_sync(0xffffffffu, order_key(mn[v] + 0.0f) == kmn[v] ? imn[v] : 0x7fffffff);
+        wmx[v] = __reduce_min_sync(0xffffffffu, order_key(mx[v] + 0.0f) == kmx[v] ? imx[v] : 0x7fffffff);
+    }
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const unsigned lmn = __ballot_sync(0xffffffffu, order_key(mn[v] + 0.0f) == kmn[v] && imn[v] == wmn[v]);
+        const unsigned lmx = __ballot_sync(0xffffffffu, order_key(mx[v] + 0.0f) == kmx[v] && imx[v] == wmx[v]);
+        mn[v] = __shfl_sync(0xffffffffu, mn[v], __ffs(lmn) - 1);
+        mx[v] = __shfl_sync(0xffffffffu, mx[v], __ffs(lmx) - 1);
+    }
+
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const float range = __fsub_rn(mx[v], mn[v]);
+        const float sc = range > 0.0f ? __fdiv_rn(range, (float)levels) : 1.0f;
+        scale[v] = sc;
+        zp[v] = mn[v];
+        // (x - zp) / scale with x - zp in [0, levels * scale]: by Markstein's correction from one
+        // reciprocal when scale is in [2^-90, 2^100] (warp-uniform), else by division; both give
+        // the correctly rounded quotient.
+        const bool fast = sc >= 0x1p-90f && sc <= 0x1p100f;
+        const float rcp = fast ? __frcp_rn(sc) : 1.0f;
+#pragma unroll
+        for (int r = 0; r < EPL; r++) {
+            uint32_t q = 0u;
+            if (active && sc > 0.0f) {
+                const float num = __fsub_rn(x[v][r], mn[v]);
+                q = __float2uint_rz(rust_round_f32(fast ? div_rn_markstein(num, sc, rcp) : __fdiv_rn(num, sc)));
+            }
+            qc[v][r] = q < levels ? q : levels;
+        }
+    }
+}
+
 // Encode and store vector (b, s, h, which) of an append (which: 0 = K, 1 = V).
 // All 32 lanes of the warp must call it; s_codes holds >= head_dim bytes.
 template <typename T, int EPL>
@@ -123,56 +235,27 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
 #pragma unroll
     for (int r = 0; r < EPL; r++) x0[r] = x[r];
 
-    // apply_signs + butterfly + 1/sqrt_approx(n) (kv_compression.rs:81-123).
-    const float *sg = a.signs + (int64_t)h * d;
+    const float *sgp = a.signs + (int64_t)h * d;
+    float sg[EPL];
 #pragma unroll
-    for (int r = 0; r < EPL; r++) x[r] = __fmul_rn(x[r], active ? sg[lane * EPL + r] : 1.0f);
-    warp_wht_butterfly<EPL>(x, lane, d);
+    for (int r = 0; r < EPL; r++) sg[r] = active ? sgp[lane * EPL + r] : 1.0f;
+    const uint32_t levels = (1u << a.bits) - 1u;
+    uint32_t qc[EPL];  // the codes of this lane's elements
+    float scale, zp;
+    {
+        float xv[1][EPL];
+        uint32_t qv[1][EPL];
+        float sv[1], zv[1];
 #pragma unroll
-    for (int r = 0; r < EPL; r++) x[r] = __fmul_rn(x[r], a.wht_scale);
-
-    // min / max with strict comparisons in index order: the first occurrence
-    // wins, as in the sequential loop of encode (this matters for +-0).
-    float mn = INFINITY, mx = -INFINITY;
-    int imn = 0x7fffffff, imx = 0x7fffffff;
-    if (active) {
+        for (int r = 0; r < EPL; r++) xv[0][r] = x[r];
+        polar_encode_warp<EPL, 1>(xv, sg, active, lane, d, a.wht_scale, levels, qv, sv, zv);
 #pragma unroll
         for (int r = 0; r < EPL; r++) {
-            const int e = lane * EPL + r;
-            if (x[r] < mn) {
-                mn = x[r];
-                imn = e;
-            }
-            if (x[r] > mx) {
-                mx = x[r];
-                imx = e;
-            }
+            x[r] = xv[0][r];
+            qc[r] = qv[0][r];
         }
-    }
-    // Across the warp: the extreme value by an integer reduction over an order-preserving key
-    // (-0 and +0 share the key of +0, since they compare equal), then the lowest element index
-    // among the lanes holding that value, and that element's own bits.
-    {
-        const int kmn = __reduce_min_sync(0xffffffffu, order_key(mn + 0.0f));
-        const int kmx = __reduce_max_sync(0xffffffffu, order_key(mx + 0.0f));
-        const int wmn = __reduce_min_sync(0xffffffffu, order_key(mn + 0.0f) == kmn ? imn : 0x7fffffff);
-        const int wmx = __reduce_min_sync(0xffffffffu, order_key(mx + 0.0f) == kmx ? imx : 0x7fffffff);
-        const unsigned lmn = __ballot_sync(0xffffffffu, order_key(mn + 0.0f) == kmn && imn == wmn);
-        const unsigned lmx = __ballot_sync(0xffffffffu, order_key(mx + 0.0f) == kmx && imx == wmx);
-        mn = __shfl_sync(0xffffffffu, mn, __ffs(lmn) - 1);
-        mx = __shfl_sync(0xffffffffu, mx, __ffs(lmx) - 1);
-    }
-
-    const uint32_t levels = (1u << a.bits) - 1u;
-    const float range = __fsub_rn(mx, mn);
-    const float scale = range > 0.0f ? __fdiv_rn(range, (float)levels) : 1.0f;
-    const float zp = mn;
-    uint32_t qc[EPL];  // the codes of this lane's elements
-#pragma unroll
-    for (int r = 0; r < EPL; r++) {
-        uint32_t q = 0u;
-        if (active && scale > 0.0f) q = __float2uint_rz(rust_round_f32(__fdiv_rn(__fsub_rn(x[r], zp), scale)));
-        qc[r] = q < levels ? q : levels;
+        scale = sv[0];
+        zp = zv[0];
     }
 
     // pack_bits (kv_compression.rs:294-312): LSB-first contiguous bit stream.
@@ -243,7 +326,7 @@ __device__ __forceinline__ void encode_append_vector(const AppendArgs &a, int b,
         uint32_t pos_bits[EPL];  // bit l: element l * EPL + r of the residual is >= 0
 #pragma unroll
         for (int r = 0; r < EPL; r++) {
-            const float sgn = active ? sg[lane * EPL + r] : 1.0f;
+            const float sgn = sg[r];
             y[r] = __fsub_rn(x0[r], __fmul_rn(__fmul_rn(y[r], a.wht_scale), sgn));
             pos_bits[r] = __ballot_sync(0xffffffffu, active && y[r] >= 0.0f);
         }

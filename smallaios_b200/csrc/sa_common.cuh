@@ -39,12 +39,26 @@ template <typename T> __device__ __forceinline__ void st_from_f32(T *p, float v)
 // ---- exact-rounding scalar helpers matching the reference's Rust ---------
 // `x as i32` (saturating, NaN -> 0): cvt.rzi.s32.f32 clamps and maps NaN to 0.
 __device__ __forceinline__ float rust_round_f32(float x) {
-    // kv_compression.rs:27-37 round_f32: half away from zero via trunc+frac.
-    float tr = __int2float_rn(__float2int_rz(x));
-    float frac = __fsub_rn(x, tr);
-    if (frac >= 0.5f) return __fadd_rn(tr, 1.0f);
-    if (frac <= -0.5f) return __fsub_rn(tr, 1.0f);
-    return tr;
+    // kv_compression.rs:27-37 round_f32: half away from zero via trunc+frac.  Branch-free: tr is
+    // never -0 (it comes from an integer), so tr + 0 is tr and tr - 1 is tr + (-1).
+    const float tr = __int2float_rn(__float2int_rz(x));
+    const float frac = __fsub_rn(x, tr);
+    return __fadd_rn(tr, frac >= 0.5f ? 1.0f : (frac <= -0.5f ? -1.0f : 0.0f));
+}
+
+// a / b correctly rounded (the value __fdiv_rn returns) from y = RN(1/b), for 2^-90 <= b <= 2^100
+// and 2^-100 <= a <= 256 b (or a = 0): every product and residual then stays in the normal range.
+// For 0 < a < 2^-100 the quotient is below 2^-10 and the result is within far less than 1/2 of it,
+// so a code rounded from it is the same.  Markstein's method (P. Markstein, IBM J. Res. Dev.
+// 34(1), 1990): q0 = RN(a*y) is within two ulps of a/b; each step forms the exact residual
+// r = a - b*q with an FMA and corrects q to RN(q + r*y).  The first step makes q faithful, and
+// from a faithful q and y = RN(1/b) the second returns RN(a/b) (Markstein's theorem).
+__device__ __forceinline__ float div_rn_markstein(float a, float b, float y) {
+    const float q0 = __fmul_rn(a, y);
+    const float r0 = __fmaf_rn(-q0, b, a);
+    const float q1 = __fmaf_rn(r0, y, q0);
+    const float r1 = __fmaf_rn(-q1, b, a);
+    return __fmaf_rn(r1, y, q1);
 }
 
 // ---- warp helpers ---------------------------------------------------------

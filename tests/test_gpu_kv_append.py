@@ -49,6 +49,10 @@ def _run_append_case(dev, *, b, s, h, d, bits, dtype, rotary, interleaved, pos0=
     g_vc = view.v_codes_tokens()[:, :, sl].cpu().numpy()
     g_km = view.k_meta[:, :, sl].cpu().numpy()
     g_vm = view.v_meta[:, :, sl].cpu().numpy()
+    # positions outside the append (the fresh cache's zeros) are left alone, in the word-interleaved
+    # V layout too
+    for codes in (view.k_codes.cpu().numpy(), view.v_codes_tokens().cpu().numpy()):
+        assert not codes[:, :, :pos0].any() and not codes[:, :, pos0 + s:].any()
     cache.close()
     return (g_kc, g_km, g_vc, g_vm), (kc, km, vc, vm)
 
@@ -132,3 +136,19 @@ def test_append_capacity_and_rope_errors(cuda_device):
     with pytest.raises(sa.ShapeMismatch):  # do_rotary without tables
         cache.append(0, k4, k4, do_rotary=True)
     cache.close()
+
+
+@pytest.mark.parametrize("bits,d", [(4, 64), (8, 256), (4, 128)])
+@pytest.mark.parametrize("mag", [2.0 ** -96, 2.0 ** -88, 2.0 ** 98, 2.0 ** 102])
+def test_append_scale_extremes(cuda_device, bits, d, mag):
+    """Vectors whose code scale sits on either side of the range where the encoder divides by a
+    reciprocal with Markstein's correction (2^-90 .. 2^100; outside it, by IEEE division): the codes
+    must be the reference's either way.  Positions 2..8 give partial and full position quads."""
+    r = np.random.default_rng(int(np.log2(mag)) + 200 + bits + d)
+    b, s, h = 2, 7, 2
+    k = (r.standard_normal((b, s, h, d)) * mag).astype(np.float32)
+    v = (r.standard_normal((b, s, h, d)) * mag).astype(np.float32)
+    v[0, 3] = np.float32(mag)  # a constant vector: range 0 after the first element
+    got, want = _run_append_case(cuda_device, b=b, s=s, h=h, d=d, bits=bits, dtype="f32", rotary=False,
+                                 interleaved=False, pos0=2, kx=k, vx=v)
+    _assert_bit_exact(got, want)
