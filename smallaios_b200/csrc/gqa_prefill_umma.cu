@@ -122,8 +122,9 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
     constexpr int EPL = D / 32;
     constexpr int CB = D * BITS / 8;
     extern __shared__ unsigned char pu_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(pu_raw) + 1023) &
-                                                            ~(uintptr_t)1023);
+    // aligned by pointer arithmetic on the shared array (not through an integer), so that the
+    // compiler keeps every access below in the shared address space (LDS/STS, not generic LD/ST)
+    unsigned char *smem = pu_raw + ((1024 - (smem_u32(pu_raw) & 1023)) & 1023);
     unsigned char *qh = smem, *ql = smem + GG::Q_PLANE;
     unsigned char *kt_s = smem + GG::K_OFF, *vt_s = smem + GG::V_OFF;
     float4 *meta = reinterpret_cast<float4 *>(smem + GG::META_OFF);
