@@ -63,7 +63,8 @@ struct PuGeo {
     static constexpr int V_TILE = D * 128;             // [D dims][64 tokens]
     static constexpr int K_OFF = 2 * Q_PLANE;
     static constexpr int V_OFF = K_OFF + K_TILE;
-    static constexpr int META_OFF = V_OFF + V_TILE;    // [2 tiles][64 tokens] float4
+    // per tile buffer: [32 token pairs] {k scale, k scale, k zp, k zp} then [32] {v scale x2, v zp x2}
+    static constexpr int META_OFF = V_OFF + V_TILE;
     static constexpr int QSUM_OFF = META_OFF + 2 * kPuTok * 16;
     static constexpr int BAR_OFF = QSUM_OFF + kPuRows * 4 + 16;  // + the tiles' V-scale maxima [2][2]
     static constexpr int SMEM = BAR_OFF + 64 + 1024;   // + slack to align the base to 1024 B
@@ -92,6 +93,35 @@ __device__ __forceinline__ float ex2_ftz(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Packed f32x2 arithmetic (fma / mul / add .rn.f32x2): each lane rounded exactly as the scalar
+// operation, two per instruction.
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+        "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+        "mul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    float2 d;
+    asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+        "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a [rows][128 B] 128-byte-swizzle tile.
@@ -286,7 +316,13 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
         // registers -> the metadata (buffer mb) and the fp16 K tile (128-byte swizzle) in shared memory
         auto stage_k = [&](int mb) {
             if (st < kPuTok) {
-                meta[mb * kPuTok + st] = make_float4(rkm.x, rkm.y, rvm.x, rvm.y);
+                // token st's metadata in the pair layout the softmax reads two tokens at a time
+                float *mt = reinterpret_cast<float *>(meta + mb * kPuTok);
+                const int j = st >> 1, sl = st & 1;
+                mt[4 * j + sl] = rkm.x;
+                mt[4 * j + 2 + sl] = rkm.y;
+                mt[4 * kPuTok / 2 + 4 * j + sl] = rvm.x;
+                mt[4 * kPuTok / 2 + 4 * j + 2 + sl] = rvm.y;
                 float vm = rvm.x;
 #pragma unroll
                 for (int m = 16; m >= 1; m >>= 1) vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, m));
@@ -441,7 +477,8 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
         for (int kt = 0; kt < ntiles; kt++) {
             const int t0 = kt * kPuTok;
             // S of this tile is complete (and with it every earlier MMA: O and U are free)
-            const float4 *mtile = meta + (kt & 1) * kPuTok;
+            // this tile's metadata, two tokens per float4: {k scale, k zp} pairs, then {v scale, v zp}
+            const float4 *kpt = meta + (kt & 1) * kPuTok, *vpt = kpt + kPuTok / 2;
             bool sok = tc_wait_sleep(bar_s, (uint32_t)(kt & 1), abort_flag, a.dev_status);
             sok = __all_sync(0xffffffffu, sok);
             if (!sok) {
@@ -461,11 +498,15 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                     tmem_ld16(tl + kPuS + c, *reinterpret_cast<uint32_t(*)[16]>(v));
                     tmem_ld16(tl + kPuS + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                     tmem_wait_ld();
+                    const float2 qq = make_float2(qs_r, qs_r);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const float2 mt = *reinterpret_cast<const float2 *>(&mtile[c + i]);
-                        const float s = fmaf(__uint_as_float(v[i]), mt.x, mt.y * qs_r);
-                        mx = fmaxf(mx, (MASK && t0 + c + i > pos_r) ? -INFINITY : s);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float4 kq = kpt[(c + i) >> 1];
+                        // s = acc * kscale + kzp * sum(q'), two tokens per instruction
+                        const float2 sp = f2_fma(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                                 make_float2(kq.x, kq.y), f2_mul(make_float2(kq.z, kq.w), qq));
+                        mx = fmaxf(mx, (MASK && t0 + c + i > pos_r) ? -INFINITY : sp.x);
+                        mx = fmaxf(mx, (MASK && t0 + c + i + 1 > pos_r) ? -INFINITY : sp.y);
                     }
                 }
                 const float lvmax =
@@ -497,6 +538,9 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                     }
                 }
                 // pass 2: p = 2^(s - m), the sums, U = p * vscale * 2^(m-R) as hi + lo fp16 into TMEM
+                // (sums of p and p * vzp kept per token parity, added at the end of the tile)
+                float2 l2 = make_float2(0.0f, 0.0f), z2 = make_float2(0.0f, 0.0f);
+                const float2 qq = make_float2(qs_r, qs_r), nm = make_float2(-mn, -mn), kk = make_float2(kr, kr);
 #pragma unroll 1
                 for (int c = 0; c < kPuTok; c += 16) {
                     uint32_t v[16];
@@ -505,22 +549,25 @@ __global__ void __launch_bounds__(32 * kPuWarps, 2) prefill_umma_kernel(AttendAr
                     uint32_t uh[8], ul[8];
 #pragma unroll
                     for (int i = 0; i < 16; i += 2) {
-                        const float4 m0 = mtile[c + i], m1 = mtile[c + i + 1];
-                        // s - m = acc * kscale + (kzp * sum(q') - m)
-                        float e0 = fmaf(__uint_as_float(v[i]), m0.x, fmaf(m0.y, qs_r, -mn));
-                        float e1 = fmaf(__uint_as_float(v[i + 1]), m1.x, fmaf(m1.y, qs_r, -mn));
+                        const float4 kq = kpt[(c + i) >> 1], vq = vpt[(c + i) >> 1];
+                        // s - m = acc * kscale + (kzp * sum(q') - m), two tokens per instruction
+                        float2 e = f2_fma(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                          make_float2(kq.x, kq.y), f2_fma(make_float2(kq.z, kq.w), qq, nm));
                         if (MASK) {
-                            if (t0 + c + i > pos_r) e0 = -INFINITY;
-                            if (t0 + c + i + 1 > pos_r) e1 = -INFINITY;
+                            if (t0 + c + i > pos_r) e.x = -INFINITY;
+                            if (t0 + c + i + 1 > pos_r) e.y = -INFINITY;
                         }
-                        const float p0 = ex2_ftz(e0), p1 = ex2_ftz(e1);
-                        l_r += p0 + p1;
-                        z_r = fmaf(p0, m0.w, fmaf(p1, m1.w, z_r));
-                        split_h2(p0 * (m0.z * kr), p1 * (m1.z * kr), uh[i / 2], ul[i / 2]);
+                        const float2 p = make_float2(ex2_ftz(e.x), ex2_ftz(e.y));
+                        l2 = f2_add(l2, p);
+                        z2 = f2_fma(p, make_float2(vq.z, vq.w), z2);
+                        const float2 u = f2_mul(p, f2_mul(make_float2(vq.x, vq.y), kk));  // p * (vscale * 2^(m-R))
+                        split_h2(u.x, u.y, uh[i / 2], ul[i / 2]);
                     }
                     tmem_st8(tl + kPuUh + c / 2, uh);
                     tmem_st8(tl + kPuUl + c / 2, ul);
                 }
+                l_r += l2.x + l2.y;
+                z_r += z2.x + z2.y;
             };
             if (full) softmax_tile(std::false_type{});
             else softmax_tile(std::true_type{});
