@@ -139,8 +139,11 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
 // hint of 10 us; the hardware wakes it when the phase completes), so warps that
 // wait long take no issue slots from the warps that compute.
 __device__ __forceinline__ bool tc_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
-    const uint64_t t0 = um_clock_ns();
-    for (;;) {
+    // The abort flag and the clock are read every 16th try only: a try often returns well before
+    // its hint (each return costs the waiting warp a few issue slots), and a try sleeps 10 us at
+    // most, so the bound is still checked every 160 us.
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
         uint32_t ok;
         asm volatile(
             "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
@@ -148,8 +151,11 @@ __device__ __forceinline__ bool tc_wait_sleep(uint64_t *bar, uint32_t parity, vo
             : "r"(smem_u32(bar)), "r"(parity), "r"(10000u)
             : "memory");
         if (ok) return true;
-        if (*abort_flag) return false;
-        if (um_clock_ns() - t0 > kTcWaitNs) break;
+        if ((it & 15) == 0) {
+            if (*abort_flag) return false;
+            if (it == 0) t0 = um_clock_ns();
+            else if (um_clock_ns() - t0 > kTcWaitNs) break;
+        }
     }
     *abort_flag = 1;
     if (status) atomicOr(status, 1);
