@@ -662,6 +662,105 @@ def run_decode_layer(args):
     return 0
 
 
+def run_prefill_stack(args):
+    """``--workload prefill_stack``: BASELINE config 4, the whole 32-layer prefill forward.
+
+    B = 8 prompts of 2048 tokens (token ids uniform in a 128256 vocabulary, an embedding
+    table of random bf16 rows), 32 Llama-3-8B layers (hidden 4096, 32 query / 8 KV heads of
+    128, intermediate 14336), each with its own random int4 MatMulNBits weights (block 32,
+    codes U{0..255} bytes, scales U[0.005, 0.02]) and its own int8 layer of the KV cache.
+    One step = the embedding gather, then prefill_layer_step for the 32 layers (RMSNorm, the
+    Q/K/V, o, gate|up and down MatMulNBits of 16384 rows on tcgen05, RoPE + quantize-on-append
+    of the prompts, the causal prefill attention, SwiGLU); no LM head.  Roofline: tensor, the
+    algorithmic FLOPs of the projections (2*M*N*K each) and of the causal attention
+    (4*B*Hq*S*S/2*D) against the measured bf16 peak.
+    """
+    import torch
+
+    import smallaios_b200 as sa
+    from smallaios_b200._lib import lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    b, s, hq, hkv, d, bits = 8, 2048, 32, 8, 128, 8
+    hidden, inter, layers, vocab = 4096, 14336, args.layers, 128256
+    m = b * s
+    cos_np, sin_np = rope_np(s + 8, d, THETA)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    cache = sa.GpuKvCache(layers, hkv, d, s + 8, batch=b, num_heads=hq, bits=bits, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def weight(n, k):
+        codes = torch.randint(0, 256, (n, k // 32, 16), dtype=torch.uint8, device=dev, generator=g)
+        scales = (torch.rand(n, k // 32, device=dev, generator=g) * 0.015 + 0.005).to(torch.bfloat16)
+        return codes, scales
+
+    ones = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+    ws = [sa.LayerWeights(*weight((hq + 2 * hkv) * d, hidden), *weight(hidden, hq * d), *weight(2 * inter, hidden),
+                          *weight(hidden, inter), ones, ones, 1e-5) for _ in range(layers)]
+    table = (torch.randn(vocab, hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    tokens = torch.randint(0, vocab, (m,), device=dev, generator=g)
+
+    def step():
+        x = torch.index_select(table, 0, tokens)
+        resid = None
+        for li in range(layers):
+            cache.set_position(0)
+            x, resid = sa.prefill_layer_step(x, resid, ws[li], cache, li, batch=b, seq_len=s, cos_cache=cos,
+                                             sin_cache=sin)
+        return x
+
+    warm = max(args.warmup, 1)
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    sampler.start()
+    l0 = lib.sa_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    launches = lib.sa_kernel_launches() - l0
+    t_ms = e0.elapsed_time(e1) / args.steps
+    finite = bool(torch.isfinite(out).all().item())
+    proj = 2.0 * m * hidden * ((hq + 2 * hkv) * d + 2 * inter) + 2.0 * m * hq * d * hidden + 2.0 * m * inter * hidden
+    attn = 4.0 * b * hq * s * s / 2 * d
+    flops = layers * (proj + attn)
+    peak_tf, peak_kind = 1590.0, "fallback 1590 TFLOP/s"
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            v = float(json.load(f).get("bf16_tflops_sustained", 0) or 0)
+        if v:
+            peak_tf, peak_kind = v, "measured bf16_tflops_sustained (a seconds-long step)"
+    achieved = flops / (t_ms * 1e-3) / 1e12
+    line = {
+        "metric": "prefill tokens/s, 32-layer Llama-3-8B stack (BASELINE config 4)",
+        "value": m / (t_ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": warm,
+        "ms_per_step": t_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4-w/int8-kv/bf16-act/f32-acc",
+        "data": "synthetic (random token ids, random embedding rows and int4 weights)",
+        "config": {"workload": "llama3-8b 32-layer prefill (BASELINE config 4)", "batch": b, "prompt": s,
+                   "layers": layers, "hidden": hidden, "intermediate": inter, "q_heads": hq, "kv_heads": hkv,
+                   "head_dim": d, "kv_bits": bits, "lm_head": False, "launch": "host launches",
+                   "l2": "activations of 16384 rows and 123 MB of weights per layer exceed L2"},
+        "gpu_launches": int(launches),
+        "output_finite": finite,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "algorithmic_flops": flops, "projection_flops": layers * proj,
+                     "attention_flops": layers * attn, "traffic": None, "peak_source": peak_kind},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    cache.close()
+    return 0
+
+
 def run_prefill_attention(args):
     """``--workload prefill``: the attention of the C4 prefill (not the headline).
 
@@ -751,9 +850,11 @@ def main():
                     help="gqa_decode shape: c3 = Llama-3-8B layer (the headline), c5 = Llama-3-70B layer")
     ap.add_argument("--batch", type=int, default=None,
                     help="gqa_decode: override the config's batch (a smaller case for profiler captures)")
-    ap.add_argument("--workload", default="gqa_decode", choices=["gqa_decode", "matmul_nbits", "decode_block", "decode_layer", "prefill"],
-                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); decode_layer = a whole decoder layer; prefill = the C4 prefill attention; one line, 1 GPU")
+    ap.add_argument("--workload", default="gqa_decode",
+                    choices=["gqa_decode", "matmul_nbits", "decode_block", "decode_layer", "prefill", "prefill_stack"],
+                    help="gqa_decode = the headline (config 3); matmul_nbits = config 2; decode_block = fused QKV projection + attention of one layer (with the unfused sequence timed beside it); decode_layer = a whole decoder layer; prefill = the C4 prefill attention; prefill_stack = the C4 32-layer prefill forward; one line, 1 GPU")
     ap.add_argument("--m", type=int, default=1, help="matmul_nbits rows (1 = decode GEMV, 64 = batched)")
+    ap.add_argument("--layers", type=int, default=32, help="prefill_stack: decoder layers (config 4: 32)")
     ap.add_argument("--packed", action="store_true", help="matmul_nbits: weights prepacked once (m <= 8)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every step from the host instead of replaying a CUDA graph of one step")
@@ -782,6 +883,8 @@ def main():
         return run_decode_layer(args)
     if args.workload == "prefill":
         return run_prefill_attention(args)
+    if args.workload == "prefill_stack":
+        return run_prefill_stack(args)
 
     return run_gqa_decode(args)
 

@@ -11,12 +11,12 @@ from .ops import (CapacityError, InternalError, InvalidAttribute, KvCacheDispatc
                   ShapeMismatch, UnsupportedOp, dispatch_gpu_node, finalize_kv_cache, gqa_attend,
                   group_query_attention, matmul_nbits, matmul_nbits_packed, qkv_project_append, rms_norm,
                   rotary_device_status, rotary_embedding, silu_mul, supports_op)
-from .layer import LayerWeights, decoder_layer_step
+from .layer import LayerWeights, decoder_layer_step, prefill_layer_step
 
 __all__ = [
     "DEFAULT_SEED", "GpuKvCache", "LayerView", "CapacityError", "InternalError", "InvalidAttribute",
     "KvCacheDispatchCtx", "OpError", "ShapeMismatch", "UnsupportedOp", "dispatch_gpu_node", "finalize_kv_cache",
     "gqa_attend", "group_query_attention", "matmul_nbits", "matmul_nbits_packed", "PackedNBitsWeight",
-    "qkv_project_append", "rms_norm", "silu_mul", "supports_op", "LayerWeights", "decoder_layer_step",
+    "qkv_project_append", "rms_norm", "silu_mul", "supports_op", "LayerWeights", "decoder_layer_step", "prefill_layer_step",
     "qjl_correction", "rotary_embedding", "rotary_device_status",
 ]

@@ -62,3 +62,41 @@ def decoder_layer_step(x: torch.Tensor, resid: torch.Tensor | None, w: LayerWeig
     m = silu_mul(gu)
     dn = matmul_nbits(m, w.wdown_codes, w.wdown_scales, K=f2 // 2, N=hidden)
     return dn, pre2
+
+
+def prefill_layer_step(x: torch.Tensor, resid: torch.Tensor | None, w: LayerWeights, cache, layer: int, *,
+                       batch: int, seq_len: int, cos_cache=None, sin_cache=None, do_rotary: bool = True,
+                       rotary_interleaved: bool = False):
+    """One layer over whole prompts: ``x`` (batch*seq_len, hidden) plus ``resid`` -> ``(d, pre2)``.
+
+    The same layer as decoder_layer_step with every projection a tcgen05 MatMulNBits of
+    batch*seq_len rows.  Q, K and V are three MatMulNBits calls on the row blocks of the packed
+    Wqkv (GroupQueryAttention takes separate contiguous Q/K/V), and GroupQueryAttention appends
+    the prompts' K/V at the cache position (RoPE, quantize-on-append) and runs the causal
+    prefill attention of every query over them.  The position is not advanced.
+    """
+    m, hidden = x.shape
+    if m != batch * seq_len:
+        raise ValueError("prefill_layer_step: x must have batch * seq_len rows")
+    from .ops import group_query_attention
+
+    cfg = cache.config
+    hkv = cfg.kv_head_count
+    hq = hkv * (cfg.num_heads // cfg.num_kv_heads)
+    d_head = cfg.head_dim
+    qd, kd = hq * d_head, hkv * d_head
+    h1, pre1 = rms_norm(x, w.input_norm, skip=resid, epsilon=w.epsilon)
+    proj = []
+    for r0, n in ((0, qd), (qd, kd), (qd + kd, kd)):
+        proj.append(matmul_nbits(h1, w.wqkv_codes[r0:r0 + n], w.wqkv_scales[r0:r0 + n], K=hidden, N=n))
+    q, k, v = (t.view(batch, seq_len, -1) for t in proj)
+    a = group_query_attention(q, k, v, cache, layer, num_heads=cfg.num_heads, kv_num_heads=cfg.num_kv_heads,
+                              do_rotary=do_rotary,
+                              rotary_interleaved=rotary_interleaved, cos_cache=cos_cache, sin_cache=sin_cache)
+    o = matmul_nbits(a.view(m, qd), w.wo_codes, w.wo_scales, K=qd, N=hidden)
+    h2, pre2 = rms_norm(o, w.post_norm, skip=pre1, epsilon=w.epsilon)
+    f2 = w.wgu_scales.shape[0]
+    gu = matmul_nbits(h2, w.wgu_codes, w.wgu_scales, K=hidden, N=f2)
+    mm = silu_mul(gu)
+    dn = matmul_nbits(mm, w.wdown_codes, w.wdown_scales, K=f2 // 2, N=hidden)
+    return dn, pre2
