@@ -8,9 +8,10 @@
 // returns, every rank's heads are in this rank's buffer, so the kernels that
 // follow on the stream may read it; no host barrier and no extra launch.
 //
-// Memory order: each thread's peer stores are followed by a system-scope
-// fence before its CTA is counted; the last CTA fences again and publishes
-// with st.release.sys; the waiter reads with ld.acquire.sys.  The epoch is a
+// Memory order: a CTA's peer stores are followed by a barrier and one
+// system-scope acquire-release fence before the CTA is counted; the last CTA
+// fences again after its count and publishes with st.release.sys; the waiter
+// reads with ld.acquire.sys.  The epoch is a
 // device-side counter (so a step replayed from a CUDA graph still advances
 // it) compared with wrap-around arithmetic.  The wait is bounded by
 // %globaltimer: after `timeout_ns` it sets bit 0 of the cache's device
@@ -39,15 +40,23 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     return v;
 }
 
-// Called by every thread of every CTA of the launch, after its stores.
+// Called by every thread of every CTA of the launch, after its stores.  Thread 0 of each CTA
+// releases the CTA's stores (the barrier orders every thread's stores before its fence, whose
+// cumulativity carries them) with an acquire-release fence at system scope before counting the
+// CTA; the last CTA's thread 0 fences again to acquire every counted CTA's stores, and its
+// publishing threads release the epoch.
 __device__ __forceinline__ void gather_complete(const GatherOut &g) {
     __shared__ int s_last;
     __shared__ uint32_t s_epoch;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned nblocks = gridDim.x * gridDim.y * gridDim.z;
-        s_last = atomicAdd(&g.state[0], 1u) == nblocks - 1;
+        asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // release: the CTA's stores before its count
+        const bool last = atomicAdd(&g.state[0], 1u) == nblocks - 1;
+        // acquire every counted CTA's stores: the epoch's st.release.sys below is cumulative over
+        // this GPU-scope chain, so it carries all of them to the peers
+        if (last) asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+        s_last = last;
     }
     __syncthreads();
     if (!s_last) return;
@@ -57,7 +66,6 @@ __device__ __forceinline__ void gather_complete(const GatherOut &g) {
         g.state[1] = s_epoch;
     }
     __syncthreads();
-    __threadfence_system();
     const uint32_t e = s_epoch;
     const int p = threadIdx.x;
     if (p < g.n) {
