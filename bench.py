@@ -711,7 +711,7 @@ def run_prefill_stack(args):
                                              sin_cache=sin)
         return x
 
-    warm = max(args.warmup, 1)
+    warm = max(args.warmup, 3)
     for _ in range(warm):
         step()
     torch.cuda.synchronize(dev)
