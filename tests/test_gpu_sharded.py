@@ -102,6 +102,25 @@ def _worker(rank, world, port, result_path):
                 sin_cache=tsin, do_rotary=True)
             torch.cuda.synchronize(dev)
             peer_ok = peer_ok and torch.equal(res[0], ref) and torch.equal(res[1], ref)
+        # The same graph replayed 16 times back to back with no host synchronisation in between (a
+        # rank may run ahead of its peer by up to the gather's own wait): every step's gathered
+        # output, copied out on the stream right after the step, must still equal its NCCL gather.
+        qns = [local((rng(700 + it).standard_normal((B, 1, HQ, D)) * 1.28).astype(np.float32), qs)
+               for it in range(16)]
+        kept = []
+        for qn in qns:
+            qd.copy_(qn)
+            graph.replay()
+            kept.append((res[0].clone(), res[1].clone()))
+        torch.cuda.synchronize(dev)
+        for qn, (r0, r1) in zip(qns, kept):
+            qd.copy_(qn)
+            cache.set_position(T - 1)
+            ref = sharding.sharded_group_query_attention(
+                qd, kd, vd, cache, LAYER, num_heads=HQ, kv_num_heads=HKV, shard=shard, cos_cache=tcos,
+                sin_cache=tsin, do_rotary=True)
+            torch.cuda.synchronize(dev)
+            peer_ok = peer_ok and torch.equal(r0, ref) and torch.equal(r1, ref)
         graph.reset()
         peer_ok = peer_ok and cache.device_status() == 0
         # this rank's codes against the oracle for its global heads
