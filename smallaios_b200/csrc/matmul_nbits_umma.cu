@@ -549,8 +549,8 @@ int launch_umma_t(const void *a, const uint8_t *b, const void *scales, const voi
 // fp16/bf16, block 32, default zero point, m >= 17 (blocks of 128 rows above
 // 128), N a multiple of 128, K a multiple of 256, codes / scales /
 // activations 16-byte aligned.
-// (Up to 16 rows the mma.sync kernels are faster: each tcgen05.mma here costs
-// about 65 cycles of issue whatever N is, and a tile needs K/8 of them.)
+// (Up to 16 rows the mma.sync kernels are faster: a tile here pays the whole
+// per-CTA dequant of its 128 weight rows and K/8 MMAs whatever the row count.)
 bool matmul_nbits_umma_eligible(const void *a, const uint8_t *b, const void *scales, const uint8_t *zp, int dtype,
                                 int64_t m, int64_t n, int64_t k, int block_size) {
     if (dtype != SA_DTYPE_FLOAT16 && dtype != SA_DTYPE_BFLOAT16) return false;
