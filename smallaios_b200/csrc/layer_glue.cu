@@ -92,6 +92,31 @@ __global__ void __launch_bounds__(kGlueThreads)
     }
 }
 
+// The same SwiGLU, 16 bytes of each operand per thread (16 / sizeof(T) elements): for rows whose
+// start and length keep every 16-byte unit aligned.  One thread per unit, grid.y = row.
+template <typename T>
+__global__ void __launch_bounds__(kGlueThreads)
+    silu_mul_vec_kernel(const T *__restrict__ gate, const T *__restrict__ up, int64_t ld_in, T *__restrict__ y,
+                        int cols) {
+    constexpr int V = 16 / (int)sizeof(T);
+    const int64_t r = blockIdx.y;
+    glue_pdl_enter();
+    const int j = (blockIdx.x * kGlueThreads + threadIdx.x) * V;
+    if (j >= cols) return;
+    union U {
+        uint4 v;
+        T t[V];
+    } g, u, o;
+    g.v = *reinterpret_cast<const uint4 *>(gate + r * ld_in + j);
+    u.v = *reinterpret_cast<const uint4 *>(up + r * ld_in + j);
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const float gf = DT<T>::to_f32(g.t[i]), uf = DT<T>::to_f32(u.t[i]);
+        o.t[i] = DT<T>::from_f32(gf / (1.0f + expf(-gf)) * uf);
+    }
+    *reinterpret_cast<uint4 *>(y + r * cols + j) = o.v;
+}
+
 template <typename T>
 int launch_rms_t(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int64_t rows,
                  int64_t cols, float eps, cudaStream_t stream) {
@@ -106,6 +131,18 @@ int launch_rms_t(const void *x, const void *skip, const void *bias, const void *
 template <typename T>
 int launch_silu_t(const void *gate, const void *up, int64_t ld_in, void *y, int64_t rows, int64_t cols,
                   cudaStream_t stream) {
+    constexpr int V = 16 / (int)sizeof(T);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+                         reinterpret_cast<uintptr_t>(y);
+    if ((al & 15) == 0 && cols % V == 0 && ld_in % V == 0 && rows <= 65535) {
+        const int64_t units = cols / V;
+        const cudaError_t e = glue_launch(silu_mul_vec_kernel<T>,
+                                          dim3((unsigned)((units + kGlueThreads - 1) / kGlueThreads), (unsigned)rows),
+                                          stream, static_cast<const T *>(gate), static_cast<const T *>(up), ld_in,
+                                          static_cast<T *>(y), (int)cols);
+        count_launch();
+        return check_cuda(e, "silu_mul launch");
+    }
     const int64_t blocks = (cols + kGlueThreads - 1) / kGlueThreads;
     const unsigned bx = (unsigned)(blocks < 64 ? blocks : 64);
     const cudaError_t e = glue_launch(silu_mul_kernel<T>, dim3(bx, (unsigned)rows), stream,

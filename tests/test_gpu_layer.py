@@ -57,12 +57,13 @@ def test_rms_norm(cuda_device, dt, skip, bias):
 
 
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
-def test_silu_mul_packed_and_separate(cuda_device, dt):
+@pytest.mark.parametrize("f", [3000, 3001])  # whole 16-byte units per row (vector kernel), or not
+def test_silu_mul_packed_and_separate(cuda_device, dt, f):
     import smallaios_b200 as sa
 
     dtype = DT[dt]
     r = rng(12)
-    rows, f = 5, 3000
+    rows = 5
     gu = _rt(r.standard_normal((rows, 2 * f)) * 3.0, dtype)
     t = torch.from_numpy(gu).to(dtype).to(cuda_device)
     want = oracle.silu_mul(gu[:, :f], gu[:, f:])
