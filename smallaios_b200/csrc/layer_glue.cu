@@ -92,6 +92,69 @@ __global__ void __launch_bounds__(kGlueThreads)
     }
 }
 
+// The same RMSNorm with the row held in registers between its two passes (one read of x and
+// skip instead of two) and 16-byte accesses: for rows of up to 256 * U 16-byte units whose
+// pointers and length keep every unit aligned.  Each thread sums the squares of its elements in
+// its own order (as the scalar kernel does, with another split of the row).
+template <typename T, int U>
+__global__ void __launch_bounds__(kGlueThreads)
+    rms_norm_vec_kernel(const T *__restrict__ x, const T *__restrict__ skip, const T *__restrict__ bias,
+                        const T *__restrict__ w, T *__restrict__ y, T *__restrict__ pre, int cols, float eps) {
+    constexpr int V = 16 / (int)sizeof(T);
+    union Vec {
+        uint4 v;
+        T t[V];
+    };
+    __shared__ float s_red[kGlueThreads / 32];
+    const int64_t base = (int64_t)blockIdx.x * cols;
+    const int tid = threadIdx.x;
+    glue_pdl_enter();
+    float v[U][V];
+    float ss = 0.0f;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const int j = (u * kGlueThreads + tid) * V;
+        if (j < cols) {
+            Vec a, b, c;
+            a.v = *reinterpret_cast<const uint4 *>(x + base + j);
+            if (skip) b.v = *reinterpret_cast<const uint4 *>(skip + base + j);
+            if (bias) c.v = *reinterpret_cast<const uint4 *>(bias + j);
+            Vec p;
+#pragma unroll
+            for (int i = 0; i < V; i++) {
+                float t = DT<T>::to_f32(a.t[i]);
+                if (skip) t += DT<T>::to_f32(b.t[i]);
+                if (bias) t += DT<T>::to_f32(c.t[i]);
+                v[u][i] = t;
+                p.t[i] = DT<T>::from_f32(t);
+                ss = fmaf(t, t, ss);
+            }
+            if (pre) *reinterpret_cast<uint4 *>(pre + base + j) = p.v;
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+        float t = tid < kGlueThreads / 32 ? s_red[tid] : 0.0f;
+        t = warp_sum(t);
+        if (tid == 0) s_red[0] = t;
+    }
+    __syncthreads();
+    const float rinv = 1.0f / sqrtf(s_red[0] / (float)cols + eps);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const int j = (u * kGlueThreads + tid) * V;
+        if (j < cols) {
+            Vec wv, o;
+            wv.v = *reinterpret_cast<const uint4 *>(w + j);
+#pragma unroll
+            for (int i = 0; i < V; i++) o.t[i] = DT<T>::from_f32(v[u][i] * rinv * DT<T>::to_f32(wv.t[i]));
+            *reinterpret_cast<uint4 *>(y + base + j) = o.v;
+        }
+    }
+}
+
 // The same SwiGLU, 16 bytes of each operand per thread (16 / sizeof(T) elements): for rows whose
 // start and length keep every 16-byte unit aligned.  One thread per unit, grid.y = row.
 template <typename T>
@@ -117,9 +180,32 @@ __global__ void __launch_bounds__(kGlueThreads)
     *reinterpret_cast<uint4 *>(y + r * cols + j) = o.v;
 }
 
+template <typename T, int U>
+cudaError_t launch_rms_vec(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre,
+                           int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+    return glue_launch(rms_norm_vec_kernel<T, U>, dim3((unsigned)rows), stream, static_cast<const T *>(x),
+                       static_cast<const T *>(skip), static_cast<const T *>(bias), static_cast<const T *>(w),
+                       static_cast<T *>(y), static_cast<T *>(pre), (int)cols, eps);
+}
+
 template <typename T>
 int launch_rms_t(const void *x, const void *skip, const void *bias, const void *w, void *y, void *pre, int64_t rows,
                  int64_t cols, float eps, cudaStream_t stream) {
+    constexpr int V = 16 / (int)sizeof(T);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(skip) |
+                         reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(w) |
+                         reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(pre);
+    const int64_t units = cols / V;
+    if ((al & 15) == 0 && cols % V == 0 && units <= 8 * kGlueThreads) {
+        const int64_t per = (units + kGlueThreads - 1) / kGlueThreads;  // units per thread: 1..8
+        cudaError_t e;
+        if (per <= 1) e = launch_rms_vec<T, 1>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        else if (per <= 2) e = launch_rms_vec<T, 2>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        else if (per <= 4) e = launch_rms_vec<T, 4>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        else e = launch_rms_vec<T, 8>(x, skip, bias, w, y, pre, rows, cols, eps, stream);
+        count_launch();
+        return check_cuda(e, "rms_norm launch");
+    }
     const cudaError_t e = glue_launch(rms_norm_kernel<T>, dim3((unsigned)rows), stream, static_cast<const T *>(x),
                                       static_cast<const T *>(skip), static_cast<const T *>(bias),
                                       static_cast<const T *>(w), static_cast<T *>(y), static_cast<T *>(pre), (int)cols,
