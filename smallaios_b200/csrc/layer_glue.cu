@@ -83,13 +83,13 @@ __global__ void __launch_bounds__(kGlueThreads)
 template <typename T>
 __global__ void __launch_bounds__(kGlueThreads)
     silu_mul_kernel(const T *__restrict__ gate, const T *__restrict__ up, int64_t ld_in, T *__restrict__ y,
-                    int cols) {
-    const int64_t r = blockIdx.y;
+                    int64_t rows, int cols) {
     glue_pdl_enter();
-    for (int j = blockIdx.x * kGlueThreads + threadIdx.x; j < cols; j += gridDim.x * kGlueThreads) {
-        const float g = glue_ld(gate, r * ld_in + j), u = glue_ld(up, r * ld_in + j);
-        st_from_f32(y + r * cols + j, g / (1.0f + expf(-g)) * u);
-    }
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)  // grid.y is capped at 65535 rows
+        for (int j = blockIdx.x * kGlueThreads + threadIdx.x; j < cols; j += gridDim.x * kGlueThreads) {
+            const float g = glue_ld(gate, r * ld_in + j), u = glue_ld(up, r * ld_in + j);
+            st_from_f32(y + r * cols + j, g / (1.0f + expf(-g)) * u);
+        }
 }
 
 // The same RMSNorm with the row held in registers between its two passes (one read of x and
@@ -160,24 +160,25 @@ __global__ void __launch_bounds__(kGlueThreads)
 template <typename T>
 __global__ void __launch_bounds__(kGlueThreads)
     silu_mul_vec_kernel(const T *__restrict__ gate, const T *__restrict__ up, int64_t ld_in, T *__restrict__ y,
-                        int cols) {
+                        int64_t rows, int cols) {
     constexpr int V = 16 / (int)sizeof(T);
-    const int64_t r = blockIdx.y;
     glue_pdl_enter();
     const int j = (blockIdx.x * kGlueThreads + threadIdx.x) * V;
     if (j >= cols) return;
-    union U {
-        uint4 v;
-        T t[V];
-    } g, u, o;
-    g.v = *reinterpret_cast<const uint4 *>(gate + r * ld_in + j);
-    u.v = *reinterpret_cast<const uint4 *>(up + r * ld_in + j);
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {  // grid.y is capped at 65535 rows
+        union U {
+            uint4 v;
+            T t[V];
+        } g, u, o;
+        g.v = *reinterpret_cast<const uint4 *>(gate + r * ld_in + j);
+        u.v = *reinterpret_cast<const uint4 *>(up + r * ld_in + j);
 #pragma unroll
-    for (int i = 0; i < V; i++) {
-        const float gf = DT<T>::to_f32(g.t[i]), uf = DT<T>::to_f32(u.t[i]);
-        o.t[i] = DT<T>::from_f32(gf / (1.0f + expf(-gf)) * uf);
+        for (int i = 0; i < V; i++) {
+            const float gf = DT<T>::to_f32(g.t[i]), uf = DT<T>::to_f32(u.t[i]);
+            o.t[i] = DT<T>::from_f32(gf / (1.0f + expf(-gf)) * uf);
+        }
+        *reinterpret_cast<uint4 *>(y + r * cols + j) = o.v;
     }
-    *reinterpret_cast<uint4 *>(y + r * cols + j) = o.v;
 }
 
 template <typename T, int U>
@@ -220,20 +221,20 @@ int launch_silu_t(const void *gate, const void *up, int64_t ld_in, void *y, int6
     constexpr int V = 16 / (int)sizeof(T);
     const uintptr_t al = reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
                          reinterpret_cast<uintptr_t>(y);
-    if ((al & 15) == 0 && cols % V == 0 && ld_in % V == 0 && rows <= 65535) {
+    const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
+    if ((al & 15) == 0 && cols % V == 0 && ld_in % V == 0) {
         const int64_t units = cols / V;
         const cudaError_t e = glue_launch(silu_mul_vec_kernel<T>,
-                                          dim3((unsigned)((units + kGlueThreads - 1) / kGlueThreads), (unsigned)rows),
-                                          stream, static_cast<const T *>(gate), static_cast<const T *>(up), ld_in,
-                                          static_cast<T *>(y), (int)cols);
+                                          dim3((unsigned)((units + kGlueThreads - 1) / kGlueThreads), gy), stream,
+                                          static_cast<const T *>(gate), static_cast<const T *>(up), ld_in,
+                                          static_cast<T *>(y), rows, (int)cols);
         count_launch();
         return check_cuda(e, "silu_mul launch");
     }
     const int64_t blocks = (cols + kGlueThreads - 1) / kGlueThreads;
     const unsigned bx = (unsigned)(blocks < 64 ? blocks : 64);
-    const cudaError_t e = glue_launch(silu_mul_kernel<T>, dim3(bx, (unsigned)rows), stream,
-                                      static_cast<const T *>(gate), static_cast<const T *>(up), ld_in,
-                                      static_cast<T *>(y), (int)cols);
+    const cudaError_t e = glue_launch(silu_mul_kernel<T>, dim3(bx, gy), stream, static_cast<const T *>(gate),
+                                      static_cast<const T *>(up), ld_in, static_cast<T *>(y), rows, (int)cols);
     count_launch();
     return check_cuda(e, "silu_mul launch");
 }

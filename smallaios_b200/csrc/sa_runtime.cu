@@ -790,7 +790,7 @@ int sa_rms_norm(const void *x, const void *skip, const void *bias, const void *w
 int sa_silu_mul(const void *gate, const void *up, int64_t ld_in, void *y, int32_t dtype, int64_t rows,
                 int64_t cols, sa_stream_t stream) {
     if (!dtype_ok(dtype)) return set_error(SA_ERR_UNSUPPORTED, "silu_mul: dtype %d not supported", dtype);
-    if (rows < 0 || cols <= 0 || ld_in < cols || rows > 65535 || cols > (1 << 30))
+    if (rows < 0 || cols <= 0 || ld_in < cols || cols > (1 << 30))
         return set_error(SA_ERR_SHAPE_MISMATCH, "silu_mul: bad shape (rows %lld, cols %lld, ld_in %lld)",
                          (long long)rows, (long long)cols, (long long)ld_in);
     if (rows == 0) return SA_OK;

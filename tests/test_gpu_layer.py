@@ -159,3 +159,18 @@ def test_dispatch_norm_nodes(cuda_device):
     assert np.allclose(pre.cpu().numpy(), want_pre, rtol=1e-6, atol=1e-6)
     with pytest.raises(sa.InvalidAttribute):
         sa.dispatch_gpu_node("RMSNormalization", [t(x), t(w)], {"axis": 1})
+
+
+@pytest.mark.parametrize("f", [8, 7])  # the vector kernel and the scalar one
+def test_silu_mul_rows_beyond_one_grid_dimension(cuda_device, f):
+    """More rows than a launch's grid.y takes (65535): the kernels loop over the rest."""
+    import smallaios_b200 as sa
+
+    r = rng(13)
+    rows = 70001
+    gu = _rt(r.standard_normal((rows, 2 * f)) * 3.0, torch.bfloat16)
+    got = sa.silu_mul(torch.from_numpy(gu).to(torch.bfloat16).to(cuda_device))
+    torch.cuda.synchronize()
+    want = oracle.silu_mul(gu[:, :f], gu[:, f:])
+    g = got.float().cpu().numpy()
+    assert np.all(np.abs(g - want) <= _bound(want, torch.bfloat16)), f"max err {np.abs(g - want).max():.3e}"
