@@ -86,6 +86,25 @@ def test_matmul_nbits_validation_without_gpu():
     assert lib.sa_matmul_nbits(None, None, None, None, None, None, 1, 1, 8, 64, 4, 32, None) == 9
 
 
+def test_silu_mul_validation_without_gpu():
+    """Shape checks of sa_silu_mul run before any launch: any row count is accepted (the kernels loop
+    over rows beyond one launch's grid.y), a row shorter than its stride's half is not."""
+    from smallaios_b200._lib import lib
+
+    assert lib.sa_silu_mul(None, None, 8, None, 1, 0, 8, None) == 0          # no rows: nothing to do
+    assert lib.sa_silu_mul(None, None, 4, None, 1, 70001, 8, None) == 2       # ld_in < cols
+    assert lib.sa_silu_mul(None, None, 16, None, 1, 70001, 8, None) == 9      # shape fine, NULL pointers
+
+
+def test_prefill_layer_rows_must_match_batch_and_prompt():
+    import torch
+
+    import smallaios_b200 as sa
+
+    with pytest.raises(ValueError):
+        sa.prefill_layer_step(torch.zeros(5, 8), None, None, None, 0, batch=2, seq_len=3)
+
+
 def test_rotary_embedding_validation_without_gpu():
     from smallaios_b200 import ops
     from smallaios_b200._lib import lib
